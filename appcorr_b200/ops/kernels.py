@@ -1,0 +1,137 @@
+"""Functional wrappers around the sm_100a kernels (one call = one or two kernel launches).
+
+All tensors are CUDA tensors in the layouts the kernels expect (bf16 row-major activations, BTHD
+attention tensors, int32 row maps). Shapes are validated in the C++ bindings.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from .native import err_word, lib
+
+EPI_BF16, EPI_F32, EPI_GELU, EPI_SWIGLU, EPI_RESID, EPI_QKV = range(6)
+AUX_NONE, AUX_SET, AUX_ADD, AUX_OUT_MINUS = range(4)
+
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
+
+
+def _pick_bn(n: int, m: int) -> int:
+    if n >= 1024 and n % 256 == 0:
+        return 256
+    if n % 128 == 0 and n >= 128:
+        return 128
+    return 64
+
+
+def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_BF16,
+         bias: Optional[torch.Tensor] = None, out_rows: Optional[torch.Tensor] = None,
+         gamma: Optional[torch.Tensor] = None, resid: Optional[torch.Tensor] = None,
+         resid_rows: Optional[torch.Tensor] = None, aux: Optional[torch.Tensor] = None,
+         aux_rows: Optional[torch.Tensor] = None, aux_mode: int = AUX_NONE,
+         resid2: Optional[torch.Tensor] = None, bn: Optional[int] = None,
+         max_ctas: int = 0) -> torch.Tensor:
+    """out = epilogue(a @ w^T). `a` [M, K] bf16, `w` [N, K] bf16 (nn.Linear layout)."""
+    if bn is None:
+        bn = 256 if epi == EPI_SWIGLU else _pick_bn(w.shape[0], a.shape[0])
+    lib().gemm(a, w, epi, bn, err_word(a.device), out=out, out_rows=out_rows, bias=bias, gamma=gamma,
+               resid=resid, resid_rows=resid_rows, aux=aux, aux_rows=aux_rows, aux_mode=aux_mode,
+               resid2=resid2, max_ctas=max_ctas)
+    return out
+
+
+def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_out: torch.Tensor,
+             k_out: torch.Tensor, v_out: torch.Tensor, *, head_dim: int, seq_len: int = 0,
+             tok_idx: Optional[torch.Tensor] = None, kv_rows: Optional[torch.Tensor] = None,
+             rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, n_prefix: int = 0,
+             bn: Optional[int] = None) -> None:
+    """qkv projection with RoPE on q/k (tokens >= n_prefix) split into three BTHD buffers.
+
+    q row m is written at q_out[m]; k/v rows at kv_rows[m] (or m). `rope` = (sin, cos) fp32
+    tables [n_patch_tokens, head_dim].
+    """
+    dim = w.shape[0] // 3
+    if bn is None:
+        bn = 256 if dim % 256 == 0 else 128
+    sin, cos = rope if rope is not None else (None, None)
+    lib().gemm(a, w, EPI_QKV, bn, err_word(a.device), bias=bias, q_out=q_out, k_out=k_out, v_out=v_out,
+               kv_rows=kv_rows, tok_idx=tok_idx, seq_len=seq_len, rope_sin=sin, rope_cos=cos,
+               n_prefix=n_prefix, head_dim=head_dim)
+
+
+def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, out: torch.Tensor,
+              rows: Optional[torch.Tensor] = None, copy_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[i] = LN(x[rows[i]]) (rows=None: every row). copy_out[i] receives the raw gathered row."""
+    lib().layernorm(x, rows, w, b, float(eps), out, copy_out)
+    return out
+
+
+def add_(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    lib().add_(x, y)
+    return x
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, *, B: int, Tq: int,
+              Tk: int, H: int, Dh: int, scale: Optional[float] = None,
+              lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Non-causal attention on BTHD tensors: q/o [B*Tq, H*Dh], k/v [B*Tk, H*Dh]."""
+    if scale is None:
+        scale = Dh ** -0.5
+    lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
+    return o
+
+
+def patch_im2col(img: torch.Tensor, patch: int, out: torch.Tensor,
+                 mean: Sequence[float] = IMAGENET_MEAN, std: Sequence[float] = IMAGENET_STD) -> torch.Tensor:
+    lib().patch_im2col(img, patch, list(mean), list(std), out)
+    return out
+
+
+def set_prefix(x: torch.Tensor, prefix: torch.Tensor, B: int, N: int) -> None:
+    lib().set_prefix(x, prefix, B, N)
+
+
+def gather_rows(src: torch.Tensor, rows: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    lib().gather_rows(src, rows, out)
+    return out
+
+
+def scatter_rows(src: torch.Tensor, rows: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
+    lib().scatter_rows(src, rows, dst)
+    return dst
+
+
+def cls_attn_pscore(q: torch.Tensor, k: torch.Tensor, *, B: int, N: int, H: int, Dh: int,
+                    scratch: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None) -> torch.Tensor:
+    if scale is None:
+        scale = Dh ** -0.5
+    lib().cls_attn_pscore(q, k, B, N, H, Dh, float(scale), scratch, out)
+    return out
+
+
+FUSION = {"add": 0, "multiply": 1, "geo_mean": 2}
+
+
+def correction_plan(server: torch.Tensor, pre: torch.Tensor, cand: torch.Tensor, k: int, upd: torch.Tensor,
+                    rows: torch.Tensor, *, mobile: Optional[torch.Tensor] = None, ws: float = 1.0,
+                    wm: float = 0.0, fusion: str = "add", valid: Optional[torch.Tensor] = None,
+                    stats: Optional[torch.Tensor] = None) -> None:
+    lib().correction_plan(server, pre, cand, mobile, float(ws), float(wm), FUSION.get(fusion, 0), valid, int(k),
+                          upd, rows, stats)
+
+
+def pyrup_add(src: torch.Tensor, res: Optional[torch.Tensor], out: torch.Tensor) -> torch.Tensor:
+    lib().pyrup_add(src, res, out)
+    return out
+
+
+def upsample_argmax(logits: torch.Tensor, C: int, H: int, W: int, out: torch.Tensor) -> torch.Tensor:
+    lib().upsample_argmax(logits, C, H, W, out)
+    return out
+
+
+def mean_rows(x: torch.Tensor, B: int, N: int, start: int, out: torch.Tensor) -> torch.Tensor:
+    lib().mean_rows(x, B, N, start, out)
+    return out

@@ -1,0 +1,128 @@
+// Python bindings of the appcorr_b200 native extension (`appcorr_b200._C`).
+//
+// Every op here launches hand-written sm_100a kernels on the current CUDA stream. Tensor
+// arguments are validated on the host (device, dtype, contiguity, alignment) before launch so a
+// bad call raises a Python exception instead of faulting the GPU.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "ops.h"
+
+namespace py = pybind11;
+using at::Tensor;
+using c10::optional;
+
+namespace appcorr {
+
+template <typename T = void>
+static T* opt_ptr(const optional<Tensor>& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+static void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+static void check_rows_i32(const optional<Tensor>& t, const char* name) {
+  if (t.has_value() && t->defined()) {
+    check_cuda(*t, name);
+    TORCH_CHECK(t->scalar_type() == at::kInt && t->is_contiguous(), name, " must be contiguous int32");
+  }
+}
+
+void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Tensor& err,
+             optional<Tensor> out, optional<Tensor> out_rows, optional<Tensor> bias, optional<Tensor> gamma,
+             optional<Tensor> resid, optional<Tensor> resid_rows, optional<Tensor> aux,
+             optional<Tensor> aux_rows, int64_t aux_mode, optional<Tensor> resid2, optional<Tensor> q_out,
+             optional<Tensor> k_out, optional<Tensor> v_out, optional<Tensor> kv_rows,
+             optional<Tensor> tok_idx, int64_t seq_len, optional<Tensor> rope_sin, optional<Tensor> rope_cos,
+             int64_t n_prefix, int64_t head_dim, int64_t max_ctas) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm expects bf16 operands");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm: A [M,K], B [N,K]");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm operands must have unit inner stride");
+  TORCH_CHECK(err.scalar_type() == at::kInt && err.is_cuda(), "err must be a CUDA int32 tensor");
+  c10::cuda::CUDAGuard guard(A.device());
+  const int M = static_cast<int>(A.size(0));
+  const int K = static_cast<int>(A.size(1));
+  int N = static_cast<int>(B.size(0));
+  TORCH_CHECK(K % 8 == 0, "gemm: K must be a multiple of 8");
+  for (auto* t : {&out_rows, &resid_rows, &aux_rows, &kv_rows, &tok_idx}) check_rows_i32(*t, "row map");
+  GemmEpilogue ep{};
+  ep.out = opt_ptr(out);
+  ep.ldo = out.has_value() ? out->stride(0) : 0;
+  ep.out_rows = opt_ptr<const int>(out_rows);
+  ep.bias = opt_ptr<const __nv_bfloat16>(bias);
+  ep.gamma = opt_ptr<const __nv_bfloat16>(gamma);
+  ep.resid = opt_ptr<const __nv_bfloat16>(resid);
+  ep.ldr = resid.has_value() ? resid->stride(0) : 0;
+  ep.resid_rows = opt_ptr<const int>(resid_rows);
+  ep.aux = opt_ptr<__nv_bfloat16>(aux);
+  ep.ldaux = aux.has_value() ? aux->stride(0) : 0;
+  ep.aux_rows = opt_ptr<const int>(aux_rows);
+  ep.aux_mode = static_cast<int>(aux_mode);
+  ep.resid2 = opt_ptr<const __nv_bfloat16>(resid2);
+  ep.ldr2 = resid2.has_value() ? resid2->stride(0) : 0;
+  ep.q_out = opt_ptr<__nv_bfloat16>(q_out);
+  ep.k_out = opt_ptr<__nv_bfloat16>(k_out);
+  ep.v_out = opt_ptr<__nv_bfloat16>(v_out);
+  ep.ld_qkv = q_out.has_value() ? q_out->stride(0) : 0;
+  ep.kv_rows = opt_ptr<const int>(kv_rows);
+  ep.tok_idx = opt_ptr<const int>(tok_idx);
+  ep.seq_len = static_cast<int>(seq_len);
+  ep.rope_sin = opt_ptr<const float>(rope_sin);
+  ep.rope_cos = opt_ptr<const float>(rope_cos);
+  ep.n_prefix = static_cast<int>(n_prefix);
+  ep.head_dim = static_cast<int>(head_dim);
+  if (epi == EPI_QKV) {
+    TORCH_CHECK(q_out && k_out && v_out, "qkv epilogue needs q_out, k_out, v_out");
+    TORCH_CHECK(N % 3 == 0, "qkv weight rows must be 3*dim");
+    ep.dim = N / 3;
+    TORCH_CHECK(ep.dim % bn == 0, "qkv: dim must be a multiple of BN");
+    TORCH_CHECK(head_dim == 64 || head_dim == 128, "qkv: head_dim must be 64 or 128");
+    TORCH_CHECK(bn % head_dim == 0, "qkv: BN must be a multiple of head_dim");
+    TORCH_CHECK(tok_idx.has_value() || seq_len > 0, "qkv: need tok_idx or seq_len");
+  } else {
+    TORCH_CHECK(out.has_value(), "gemm: out is required");
+    check_cuda(*out, "out");
+    TORCH_CHECK(out->stride(1) == 1, "out must have unit inner stride");
+    if (epi == EPI_SWIGLU) {
+      TORCH_CHECK(N % 256 == 0, "swiglu: packed w1||w2 rows must be a multiple of 256");
+    } else {
+      TORCH_CHECK(N % 32 == 0, "gemm: N must be a multiple of 32 (pad the weight)");
+    }
+    if (epi == EPI_RESID) TORCH_CHECK(resid.has_value() && gamma.has_value(), "resid epilogue needs resid, gamma");
+    if (aux_mode == AUX_OUT_MINUS) TORCH_CHECK(resid2.has_value(), "AUX_OUT_MINUS needs resid2");
+  }
+  if (M == 0) return;
+  gemm_dispatch(static_cast<int>(epi), static_cast<int>(bn), A, B, M, N, K, ep, err.data_ptr<int>(),
+                static_cast<int>(max_ctas));
+}
+
+}  // namespace appcorr
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  using namespace appcorr;
+  m.doc() = "appcorr_b200 native sm_100a kernels";
+  m.def("gemm", &gemm_op, py::arg("A"), py::arg("B"), py::arg("epi"), py::arg("bn"), py::arg("err"),
+        py::arg("out") = py::none(), py::arg("out_rows") = py::none(), py::arg("bias") = py::none(),
+        py::arg("gamma") = py::none(), py::arg("resid") = py::none(), py::arg("resid_rows") = py::none(),
+        py::arg("aux") = py::none(), py::arg("aux_rows") = py::none(), py::arg("aux_mode") = 0,
+        py::arg("resid2") = py::none(), py::arg("q_out") = py::none(), py::arg("k_out") = py::none(),
+        py::arg("v_out") = py::none(), py::arg("kv_rows") = py::none(), py::arg("tok_idx") = py::none(),
+        py::arg("seq_len") = 0, py::arg("rope_sin") = py::none(), py::arg("rope_cos") = py::none(),
+        py::arg("n_prefix") = 0, py::arg("head_dim") = 128, py::arg("max_ctas") = 0);
+  m.attr("EPI_BF16") = static_cast<int>(EPI_BF16);
+  m.attr("EPI_F32") = static_cast<int>(EPI_F32);
+  m.attr("EPI_GELU") = static_cast<int>(EPI_GELU);
+  m.attr("EPI_SWIGLU") = static_cast<int>(EPI_SWIGLU);
+  m.attr("EPI_RESID") = static_cast<int>(EPI_RESID);
+  m.attr("EPI_QKV") = static_cast<int>(EPI_QKV);
+  m.attr("AUX_NONE") = static_cast<int>(AUX_NONE);
+  m.attr("AUX_SET") = static_cast<int>(AUX_SET);
+  m.attr("AUX_ADD") = static_cast<int>(AUX_ADD);
+  m.attr("AUX_OUT_MINUS") = static_cast<int>(AUX_OUT_MINUS);
+  register_elementwise_ops(m);
+  register_attention_ops(m);
+}

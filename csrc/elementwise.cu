@@ -1,0 +1,710 @@
+// Memory-bound sm_100a kernels of appcorr_b200: normalisation, row movement, token preparation,
+// attention-derived patch scores, the sync-free correction plan builder, pyramid decode and heads.
+//
+// Each replaces one reference op (file:line within the reference project):
+//   layernorm_rows      norm1/norm2/final norm, optionally fused with the active-row gather
+//                       (block.py:1111 gather + norm1; triton token_update.py:352-473)
+//   add_rows            x + blocks_out_sum for every token (block.py:1146-1149)
+//   patch_im2col        uint8 HWC pixels -> normalised bf16 16x16 patches feeding the patch-embed
+//                       GEMM (layers/patch_embed.py:61-76 Conv2d k=s=16)
+//   set_prefix_rows     CLS + storage tokens in front of the patch tokens
+//                       (models/vision_transformer.py:308-340)
+//   cls_attn_pscore     softmax(q_cls k^T / sqrt(d)) averaged over heads (attention.py:266-268)
+//   correction_plan     server pscore (+ mobile hint) -> top-k over candidates -> ascending packed
+//                       plan with gather/scatter row maps (block.py:360-443, 1017-1078)
+//   pyrup_add           cv2.pyrUp of the coarser level + int16 residual, clipped to uint8
+//                       (policies/transmission/laplacian.py:122-162, closed loop :234-262)
+//   upsample_argmax     bilinear upsample of head logits + argmax (dinov3_segmentor_linhead.py:
+//                       749-851 interpolate/softmax/argmax)
+//   mean_rows           mean over patch tokens for the classifier head (dinov3_classifier.py:665)
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cfloat>
+
+#include "sm100_common.cuh"
+#include "ops.h"
+
+namespace appcorr {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < NT / 32) ? red[l] : 0.f;
+  return warp_sum(t);
+}
+
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < NT / 32) ? red[l] : -FLT_MAX;
+  return warp_max(t);
+}
+
+// ------------------------------------------------------------------------------ LayerNorm
+// One CTA (128 threads) per row; the row stays in registers (D <= 8192, D % 8 == 0).
+constexpr int kLnThreads = 128;
+constexpr int kLnMaxVec = 8;
+
+__global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
+    const bf16* __restrict__ x, long ldx, const int* __restrict__ rows, const bf16* __restrict__ w,
+    const bf16* __restrict__ b, float eps, bf16* __restrict__ out, long ldo, bf16* __restrict__ copy_out,
+    long ldc, int D, int nrows) {
+  __shared__ float red[kLnThreads / 32];
+  const int r = blockIdx.x;
+  if (r >= nrows) return;
+  const long src = rows ? rows[r] : r;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + src * ldx);
+  const int nvec = D >> 3;
+  float v[kLnMaxVec][8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int c = threadIdx.x + i * kLnThreads;
+    if (c < nvec) {
+      uint4 u = xr[c];
+      if (copy_out) reinterpret_cast<uint4*>(copy_out + (long)r * ldc)[c] = u;
+      float2 p0 = unpack_bf16x2(u.x), p1 = unpack_bf16x2(u.y), p2 = unpack_bf16x2(u.z), p3 = unpack_bf16x2(u.w);
+      v[i][0] = p0.x; v[i][1] = p0.y; v[i][2] = p1.x; v[i][3] = p1.y;
+      v[i][4] = p2.x; v[i][5] = p2.y; v[i][6] = p3.x; v[i][7] = p3.y;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[i][j];
+    }
+  }
+  const float mean = block_sum<kLnThreads>(s, red) / D;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int c = threadIdx.x + i * kLnThreads;
+    if (c < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[i][j] - mean;
+        q += d * d;
+      }
+    }
+  }
+  const float rstd = rsqrtf(block_sum<kLnThreads>(q, red) / D + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + (long)r * ldo);
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  const uint4* bv = reinterpret_cast<const uint4*>(b);
+#pragma unroll
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int c = threadIdx.x + i * kLnThreads;
+    if (c < nvec) {
+      uint4 wu = __ldg(wv + c), bu = __ldg(bv + c);
+      const uint32_t* wp = &wu.x;
+      const uint32_t* bp = &bu.x;
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 ww = unpack_bf16x2(wp[j]), bb = unpack_bf16x2(bp[j]);
+        const float y0 = (v[i][2 * j] - mean) * rstd * ww.x + bb.x;
+        const float y1 = (v[i][2 * j + 1] - mean) * rstd * ww.y + bb.y;
+        o[j] = pack_bf16x2(y0, y1);
+      }
+      orow[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at::Tensor& w, const at::Tensor& b,
+                  double eps, at::Tensor& out, c10::optional<at::Tensor> copy_out) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "layernorm: bf16 CUDA x");
+  const int D = static_cast<int>(x.size(-1));
+  TORCH_CHECK(D % 8 == 0 && D <= kLnThreads * kLnMaxVec * 8, "layernorm: D % 8 == 0 and D <= 8192");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && w.numel() == D, "layernorm: bf16 affine");
+  const long ldx = x.stride(-2);
+  const int nrows = static_cast<int>(out.size(0));
+  const int* rp = nullptr;
+  if (rows.has_value()) {
+    TORCH_CHECK(rows->scalar_type() == at::kInt && rows->numel() == nrows, "layernorm: rows int32 [nrows]");
+    rp = rows->data_ptr<int>();
+  } else {
+    TORCH_CHECK(x.numel() / D == nrows, "layernorm: row count mismatch");
+  }
+  bf16* cp = nullptr;
+  long ldc = 0;
+  if (copy_out.has_value()) {
+    cp = reinterpret_cast<bf16*>(copy_out->data_ptr());
+    ldc = copy_out->stride(0);
+  }
+  if (nrows == 0) return;
+  c10::cuda::CUDAGuard g(x.device());
+  layernorm_kernel<<<nrows, kLnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
+      reinterpret_cast<const bf16*>(b.data_ptr()), static_cast<float>(eps), reinterpret_cast<bf16*>(out.data_ptr()),
+      out.stride(0), cp, ldc, D, nrows);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ x += y
+__global__ void add_bf16_kernel(bf16* __restrict__ x, const bf16* __restrict__ y, long n8) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    uint4 a = reinterpret_cast<uint4*>(x)[i];
+    uint4 c = reinterpret_cast<const uint4*>(y)[i];
+    uint32_t* ap = &a.x;
+    const uint32_t* cp = &c.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 p = unpack_bf16x2(ap[j]), q = unpack_bf16x2(cp[j]);
+      ap[j] = pack_bf16x2(p.x + q.x, p.y + q.y);
+    }
+    reinterpret_cast<uint4*>(x)[i] = a;
+  }
+}
+
+void add_inplace_op(at::Tensor& x, const at::Tensor& y) {
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous() && x.numel() == y.numel() && x.numel() % 8 == 0, "add_: contiguous, numel % 8");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16, "add_: bf16");
+  const long n8 = x.numel() / 8;
+  if (n8 == 0) return;
+  c10::cuda::CUDAGuard g(x.device());
+  const int grid = static_cast<int>(std::min<long>((n8 + 255) / 256, num_sms() * 8L));
+  add_bf16_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(y.data_ptr()), n8);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ patch im2col
+// img: uint8 [B, H, W, 3] (HWC as decoded). out: bf16 [B * (H/p) * (W/p), 3*p*p], column index
+// c*p*p + ky*p + kx (the Conv2d weight flattening order). Pixels are normalised as
+// (v / 255 - mean[c]) / std[c].
+__global__ void patch_im2col_kernel(const uint8_t* __restrict__ img, int H, int W, int p, float3 mean,
+                                    float3 inv_std, bf16* __restrict__ out, long total) {
+  const int gw = W / p, gh = H / p;
+  const int K = 3 * p * p;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long row = i / K;
+    const int col = static_cast<int>(i - row * K);
+    const int c = col / (p * p);
+    const int rem = col - c * p * p;
+    const int ky = rem / p, kx = rem - (rem / p) * p;
+    const long b = row / (gh * gw);
+    const int t = static_cast<int>(row - b * gh * gw);
+    const int py = t / gw, px = t - (t / gw) * gw;
+    const int y = py * p + ky, x = px * p + kx;
+    const float v = img[((b * H + y) * W + x) * 3 + c] * (1.0f / 255.0f);
+    const float m = c == 0 ? mean.x : (c == 1 ? mean.y : mean.z);
+    const float s = c == 0 ? inv_std.x : (c == 1 ? inv_std.y : inv_std.z);
+    out[i] = __float2bfloat16_rn((v - m) * s);
+  }
+}
+
+void patch_im2col_op(const at::Tensor& img, int64_t patch, std::vector<double> mean, std::vector<double> std_,
+                     at::Tensor& out) {
+  TORCH_CHECK(img.is_cuda() && img.scalar_type() == at::kByte && img.dim() == 4 && img.size(3) == 3 && img.is_contiguous(),
+              "patch_im2col: uint8 [B,H,W,3] contiguous");
+  const int H = static_cast<int>(img.size(1)), W = static_cast<int>(img.size(2)), p = static_cast<int>(patch);
+  TORCH_CHECK(H % p == 0 && W % p == 0, "patch_im2col: H, W multiples of patch");
+  const long total = img.size(0) * (long)(H / p) * (W / p) * 3 * p * p;
+  TORCH_CHECK(out.numel() == total && out.is_contiguous() && out.scalar_type() == at::kBFloat16, "patch_im2col: out shape");
+  c10::cuda::CUDAGuard g(img.device());
+  const int grid = static_cast<int>(std::min<long>((total + 255) / 256, num_sms() * 16L));
+  patch_im2col_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      img.data_ptr<uint8_t>(), H, W, p, make_float3(mean[0], mean[1], mean[2]),
+      make_float3(1.0 / std_[0], 1.0 / std_[1], 1.0 / std_[2]), reinterpret_cast<bf16*>(out.data_ptr()), total);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ prefix rows
+// x: [B, N, D]; rows 0..npre-1 of each image <- prefix [npre, D].
+__global__ void set_prefix_kernel(bf16* __restrict__ x, long ldx, int N, const bf16* __restrict__ prefix, int npre,
+                                  int D, int B) {
+  const int n8 = D >> 3;
+  const long total = (long)B * npre * n8;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long row = i / n8;
+    const int c = static_cast<int>(i - row * n8);
+    const int b = static_cast<int>(row / npre);
+    const int t = static_cast<int>(row - (long)b * npre);
+    reinterpret_cast<uint4*>(x + ((long)b * N + t) * ldx)[c] = reinterpret_cast<const uint4*>(prefix + (long)t * D)[c];
+  }
+}
+
+void set_prefix_op(at::Tensor& x, const at::Tensor& prefix, int64_t B, int64_t N) {
+  const int D = static_cast<int>(x.size(-1));
+  const int npre = static_cast<int>(prefix.size(0));
+  TORCH_CHECK(prefix.is_contiguous() && prefix.size(1) == D && D % 8 == 0, "set_prefix: prefix [npre, D]");
+  if (B * npre == 0) return;
+  c10::cuda::CUDAGuard g(x.device());
+  set_prefix_kernel<<<std::max<long>(1, (B * npre * (D / 8) + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<bf16*>(x.data_ptr()), x.stride(-2), static_cast<int>(N),
+      reinterpret_cast<const bf16*>(prefix.data_ptr()), npre, D, static_cast<int>(B));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ row gather
+__global__ void gather_rows_kernel(const bf16* __restrict__ src, long lds, const int* __restrict__ rows,
+                                   bf16* __restrict__ dst, long ldd, int n8, int nrows) {
+  const long total = (long)nrows * n8;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int r = static_cast<int>(i / n8);
+    const int c = static_cast<int>(i - (long)r * n8);
+    reinterpret_cast<uint4*>(dst + (long)r * ldd)[c] = reinterpret_cast<const uint4*>(src + (long)rows[r] * lds)[c];
+  }
+}
+
+__global__ void scatter_rows_kernel(const bf16* __restrict__ src, long lds, const int* __restrict__ rows,
+                                    bf16* __restrict__ dst, long ldd, int n8, int nrows) {
+  const long total = (long)nrows * n8;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int r = static_cast<int>(i / n8);
+    const int c = static_cast<int>(i - (long)r * n8);
+    reinterpret_cast<uint4*>(dst + (long)rows[r] * ldd)[c] = reinterpret_cast<const uint4*>(src + (long)r * lds)[c];
+  }
+}
+
+void gather_rows_op(const at::Tensor& src, const at::Tensor& rows, at::Tensor& dst) {
+  const int D = static_cast<int>(src.size(-1));
+  TORCH_CHECK(D % 8 == 0 && src.scalar_type() == at::kBFloat16 && dst.scalar_type() == at::kBFloat16, "gather_rows: bf16, D%8");
+  TORCH_CHECK(rows.scalar_type() == at::kInt, "gather_rows: int32 rows");
+  const int nrows = static_cast<int>(rows.numel());
+  if (nrows == 0) return;
+  c10::cuda::CUDAGuard g(src.device());
+  const long total = (long)nrows * (D / 8);
+  gather_rows_kernel<<<static_cast<int>(std::min<long>((total + 255) / 256, num_sms() * 16L)), 256, 0,
+                       at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const bf16*>(src.data_ptr()), src.stride(-2),
+                                                           rows.data_ptr<int>(), reinterpret_cast<bf16*>(dst.data_ptr()),
+                                                           dst.stride(-2), D / 8, nrows);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void scatter_rows_op(const at::Tensor& src, const at::Tensor& rows, at::Tensor& dst) {
+  const int D = static_cast<int>(src.size(-1));
+  TORCH_CHECK(D % 8 == 0 && src.scalar_type() == at::kBFloat16 && dst.scalar_type() == at::kBFloat16, "scatter_rows: bf16, D%8");
+  TORCH_CHECK(rows.scalar_type() == at::kInt, "scatter_rows: int32 rows");
+  const int nrows = static_cast<int>(rows.numel());
+  if (nrows == 0) return;
+  c10::cuda::CUDAGuard g(src.device());
+  const long total = (long)nrows * (D / 8);
+  scatter_rows_kernel<<<static_cast<int>(std::min<long>((total + 255) / 256, num_sms() * 16L)), 256, 0,
+                        at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const bf16*>(src.data_ptr()), src.stride(-2),
+                                                            rows.data_ptr<int>(), reinterpret_cast<bf16*>(dst.data_ptr()),
+                                                            dst.stride(-2), D / 8, nrows);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ CLS attention pscore
+// grid (B, H). q: [B*N, H*Dh] rows (only row b*N of each image is read), k: [B*N, H*Dh].
+// probs: fp32 [B, H, N] = softmax over keys of the CLS query. A second pass averages over heads.
+constexpr int kPsThreads = 256;
+
+__global__ void __launch_bounds__(kPsThreads) cls_attn_probs_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                                    long ld, int N, int H, int Dh, float scale,
+                                                                    float* __restrict__ probs) {
+  extern __shared__ float s_buf[];  // [N] logits, then [Dh] query
+  __shared__ float red[kPsThreads / 32];
+  const int b = blockIdx.x, h = blockIdx.y;
+  float* qs = s_buf + N;
+  const bf16* qrow = q + (long)b * N * ld + (long)h * Dh;
+  for (int d = threadIdx.x; d < Dh; d += kPsThreads) qs[d] = __bfloat162float(qrow[d]);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // One warp per key; lanes split the head dim.
+  for (int j = warp; j < N; j += kPsThreads / 32) {
+    const bf16* krow = k + ((long)b * N + j) * ld + (long)h * Dh;
+    float acc = 0.f;
+    for (int d = lane * 2; d < Dh; d += 64) {
+      float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(krow + d));
+      acc += kk.x * qs[d] + kk.y * qs[d + 1];
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) s_buf[j] = acc * scale;
+  }
+  __syncthreads();
+  float mx = -FLT_MAX;
+  for (int j = threadIdx.x; j < N; j += kPsThreads) mx = fmaxf(mx, s_buf[j]);
+  mx = block_max<kPsThreads>(mx, red);
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < N; j += kPsThreads) {
+    const float e = __expf(s_buf[j] - mx);
+    s_buf[j] = e;
+    sum += e;
+  }
+  sum = block_sum<kPsThreads>(sum, red);
+  const float inv = 1.0f / sum;
+  float* out = probs + ((long)b * H + h) * N;
+  for (int j = threadIdx.x; j < N; j += kPsThreads) out[j] = s_buf[j] * inv;
+}
+
+// out[b, j] = mean_h probs[b, h, j]
+__global__ void head_mean_kernel(const float* __restrict__ probs, int B, int H, int N, float* __restrict__ out) {
+  const long total = (long)B * N;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long b = i / N;
+    const int j = static_cast<int>(i - b * N);
+    float s = 0.f;
+    for (int h = 0; h < H; ++h) s += probs[(b * H + h) * N + j];
+    out[i] = s / H;
+  }
+}
+
+void cls_attn_pscore_op(const at::Tensor& q, const at::Tensor& k, int64_t B, int64_t N, int64_t H, int64_t Dh,
+                        double scale, at::Tensor& scratch, at::Tensor& out) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16, "cls_attn_pscore: bf16");
+  TORCH_CHECK(q.stride(0) == k.stride(0), "cls_attn_pscore: q and k share a row stride");
+  TORCH_CHECK(scratch.scalar_type() == at::kFloat && scratch.numel() >= B * H * N, "cls_attn_pscore: scratch fp32 [B,H,N]");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.numel() == B * N && out.is_contiguous(), "cls_attn_pscore: out fp32 [B,N]");
+  TORCH_CHECK(Dh % 64 == 0, "cls_attn_pscore: Dh multiple of 64");
+  c10::cuda::CUDAGuard g(q.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const size_t smem = (N + Dh) * sizeof(float);
+  TORCH_CHECK(smem <= 200 * 1024, "cls_attn_pscore: sequence too long");
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(cls_attn_probs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cls_attn_probs_kernel<<<dim3(B, H), kPsThreads, smem, st>>>(
+      reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()), q.stride(0),
+      static_cast<int>(N), static_cast<int>(H), static_cast<int>(Dh), static_cast<float>(scale), scratch.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  head_mean_kernel<<<static_cast<int>(std::max<long>(1, (B * N + 255) / 256)), 256, 0, st>>>(
+      scratch.data_ptr<float>(), static_cast<int>(B), static_cast<int>(H), static_cast<int>(N), out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ correction plan
+// One CTA per image. Candidates are the patch tokens cand[b, 0..P). The combined score is
+//   s = ws * server[b, cand] (+|*|geo) wm * mobile[b, i]
+// and the plan keeps the k highest-scoring candidates (radix select on the fp32 order key; ties
+// resolved towards lower candidate position), emitted in ascending candidate order after the
+// npre prefix tokens, exactly the layout of the fixed-k builder (block.py:398-443).
+// Outputs (T = npre + k):
+//   upd  [B, T]      token indices (update_indice)
+//   rows [B*T]       b*N + token: gather rows of x, scatter rows of the KV cache / stream
+//   stats [B, 2]     kept / full score mass (block.py:763-791)
+constexpr int kPlanThreads = 512;
+
+__device__ __forceinline__ uint32_t f32_order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kPlanThreads) correction_plan_kernel(
+    const float* __restrict__ server, int N, const int* __restrict__ pre, int npre, const int* __restrict__ cand, int P,
+    const float* __restrict__ mobile, float ws, float wm, int fusion, const uint8_t* __restrict__ valid, int k,
+    int* __restrict__ upd, int* __restrict__ rows, float* __restrict__ stats) {
+  extern __shared__ uint32_t sm[];
+  uint32_t* keys = sm;                                  // [P]
+  float* sc = reinterpret_cast<float*>(sm + P);         // [P]
+  int* flag = reinterpret_cast<int*>(sm + 2 * P);       // [P]
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix, s_remaining;
+  __shared__ float red[kPlanThreads / 32];
+  __shared__ int warp_tot[kPlanThreads / 32];
+  const int b = blockIdx.x;
+  const int T = npre + k;
+  float full = 0.f;
+  for (int i = threadIdx.x; i < P; i += kPlanThreads) {
+    const int tok = cand[(long)b * P + i];
+    float s = ws * server[(long)b * N + tok];
+    if (mobile != nullptr && wm != 0.f) {
+      const float mt = wm * mobile[(long)b * P + i];
+      if (fusion == 1) s = s * mt;
+      else if (fusion == 2) s = sqrtf(fmaxf(s * mt, 0.f));
+      else s = s + mt;
+    }
+    if (valid != nullptr && !valid[(long)b * P + i]) s = -INFINITY;
+    sc[i] = s;
+    keys[i] = f32_order_key(s);
+    if (isfinite(s)) full += s;
+  }
+  full = block_sum<kPlanThreads>(full, red);
+  // Radix select the k-th largest key, 8 bits per pass, most significant first.
+  if (threadIdx.x == 0) { s_prefix = 0; s_remaining = k; }
+  __syncthreads();
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const uint32_t hi_mask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
+    for (int i = threadIdx.x; i < 256; i += kPlanThreads) hist[i] = 0;
+    __syncthreads();
+    const uint32_t pref = s_prefix;
+    for (int i = threadIdx.x; i < P; i += kPlanThreads) {
+      const uint32_t kk = keys[i];
+      if ((kk & hi_mask) == (pref & hi_mask)) atomicAdd(&hist[(kk >> shift) & 0xFF], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t rem = s_remaining;
+      int digit = 255;
+      for (; digit > 0; --digit) {
+        if (hist[digit] >= rem) break;
+        rem -= hist[digit];
+      }
+      s_prefix = pref | (static_cast<uint32_t>(digit) << shift);
+      s_remaining = rem;
+    }
+    __syncthreads();
+  }
+  const uint32_t kth = s_prefix;
+  const uint32_t ties_needed = s_remaining;  // how many keys equal to kth are kept
+  // Flag: 1 if kept. Keys > kth are kept; keys == kth kept in ascending position until filled.
+  for (int i = threadIdx.x; i < P; i += kPlanThreads) flag[i] = keys[i] > kth ? 1 : (keys[i] == kth ? 2 : 0);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t left = ties_needed;
+    for (int i = 0; i < P; ++i) {
+      if (flag[i] == 2) {
+        flag[i] = left > 0 ? 1 : 0;
+        if (left > 0) --left;
+      }
+    }
+  }
+  __syncthreads();
+  // Block-wide exclusive scan over flags in chunks of kPlanThreads, emitting kept candidates in order.
+  float kept = 0.f;
+  int base = 0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int c0 = 0; c0 < P; c0 += kPlanThreads) {
+    const int i = c0 + threadIdx.x;
+    const int f = (i < P && k > 0) ? flag[i] : 0;
+    int incl = f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int woff = 0, tot = 0;
+    for (int w = 0; w < kPlanThreads / 32; ++w) {
+      if (w < warp) woff += warp_tot[w];
+      tot += warp_tot[w];
+    }
+    if (f) {
+      const int pos = base + woff + incl - 1;
+      const int tok = cand[(long)b * P + i];
+      upd[(long)b * T + npre + pos] = tok;
+      rows[(long)b * T + npre + pos] = b * N + tok;
+      if (isfinite(sc[i])) kept += sc[i];
+    }
+    base += tot;
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < npre; i += kPlanThreads) {
+    const int tok = pre[(long)b * npre + i];
+    upd[(long)b * T + i] = tok;
+    rows[(long)b * T + i] = b * N + tok;
+  }
+  kept = block_sum<kPlanThreads>(kept, red);
+  if (threadIdx.x == 0 && stats != nullptr) {
+    stats[2 * b] = kept;
+    stats[2 * b + 1] = full;
+  }
+}
+
+void correction_plan_op(const at::Tensor& server, const at::Tensor& pre, const at::Tensor& cand,
+                        c10::optional<at::Tensor> mobile, double ws, double wm, int64_t fusion,
+                        c10::optional<at::Tensor> valid, int64_t k, at::Tensor& upd, at::Tensor& rows,
+                        c10::optional<at::Tensor> stats) {
+  TORCH_CHECK(server.scalar_type() == at::kFloat && server.dim() == 2 && server.is_contiguous(), "plan: server fp32 [B,N]");
+  const int B = static_cast<int>(server.size(0)), N = static_cast<int>(server.size(1));
+  TORCH_CHECK(cand.scalar_type() == at::kInt && cand.dim() == 2 && cand.size(0) == B && cand.is_contiguous(), "plan: cand int32 [B,P]");
+  TORCH_CHECK(pre.scalar_type() == at::kInt && pre.dim() == 2 && pre.size(0) == B && pre.is_contiguous(), "plan: pre int32 [B,npre]");
+  const int P = static_cast<int>(cand.size(1)), npre = static_cast<int>(pre.size(1));
+  TORCH_CHECK(k >= 0 && k <= P, "plan: 0 <= k <= P");
+  TORCH_CHECK(upd.scalar_type() == at::kInt && upd.numel() == (long)B * (npre + k), "plan: upd int32 [B, npre+k]");
+  TORCH_CHECK(rows.scalar_type() == at::kInt && rows.numel() == (long)B * (npre + k), "plan: rows int32 [B*(npre+k)]");
+  const float* mp = nullptr;
+  if (mobile.has_value()) {
+    TORCH_CHECK(mobile->scalar_type() == at::kFloat && mobile->numel() == (long)B * P, "plan: mobile fp32 [B,P]");
+    mp = mobile->data_ptr<float>();
+  }
+  const uint8_t* vp = nullptr;
+  if (valid.has_value()) {
+    TORCH_CHECK(valid->scalar_type() == at::kBool && valid->numel() == (long)B * P, "plan: valid bool [B,P]");
+    vp = reinterpret_cast<const uint8_t*>(valid->data_ptr());
+  }
+  float* sp = nullptr;
+  if (stats.has_value()) {
+    TORCH_CHECK(stats->scalar_type() == at::kFloat && stats->numel() >= 2L * B, "plan: stats fp32 [B,2]");
+    sp = stats->data_ptr<float>();
+  }
+  const size_t smem = 3 * sizeof(uint32_t) * P;
+  TORCH_CHECK(smem <= 190 * 1024, "plan: too many candidates");
+  c10::cuda::CUDAGuard g(server.device());
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(correction_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  correction_plan_kernel<<<B, kPlanThreads, smem, at::cuda::getCurrentCUDAStream()>>>(
+      server.data_ptr<float>(), N, pre.data_ptr<int>(), npre, cand.data_ptr<int>(), P, mp, static_cast<float>(ws),
+      static_cast<float>(wm), static_cast<int>(fusion), vp, static_cast<int>(k), upd.data_ptr<int>(), rows.data_ptr<int>(), sp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ pyramid decode
+// Integer pyrUp matching OpenCV (5-tap [1 4 6 4 1] kernel on the zero-upsampled image, x4 gain):
+// per axis, even output 2i = s[i-1] + 6 s[i] + s[i+1], odd 2i+1 = 4 s[i] + 4 s[i+1], with the
+// left border mirrored (s[-1] = s[1]) and the last source sample giving s[n-2] + 7 s[n-1] and
+// 8 s[n-1]; result = (sum + 32) >> 6. Optionally adds an int16 residual and clips to [0, 255].
+__device__ __forceinline__ void pyr_taps(int o, int n, int (&idx)[3], int (&wt)[3]) {
+  const int i = o >> 1;
+  if ((o & 1) == 0) {
+    if (i == n - 1) {
+      idx[0] = n > 1 ? n - 2 : 0; wt[0] = 1; idx[1] = n - 1; wt[1] = 7; idx[2] = n - 1; wt[2] = 0;
+    } else {
+      idx[0] = i == 0 ? (n > 1 ? 1 : 0) : i - 1; wt[0] = 1;
+      idx[1] = i; wt[1] = 6;
+      idx[2] = i + 1; wt[2] = 1;
+    }
+  } else {
+    if (i == n - 1) {
+      idx[0] = i; wt[0] = 8; idx[1] = i; wt[1] = 0; idx[2] = i; wt[2] = 0;
+    } else {
+      idx[0] = i; wt[0] = 4; idx[1] = i + 1; wt[1] = 4; idx[2] = i + 1; wt[2] = 0;
+    }
+  }
+}
+
+__global__ void pyrup_add_kernel(const uint8_t* __restrict__ src, int h, int w, const int16_t* __restrict__ res,
+                                 uint8_t* __restrict__ dst, int B, int C) {
+  const int H = 2 * h, W = 2 * w;
+  const long total = (long)B * H * W;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long b = i / ((long)H * W);
+    const int rem = static_cast<int>(i - b * H * W);
+    const int y = rem / W, x = rem - (rem / W) * W;
+    int yi[3], yw[3], xi[3], xw[3];
+    pyr_taps(y, h, yi, yw);
+    pyr_taps(x, w, xi, xw);
+    const uint8_t* sb = src + b * h * w * C;
+    for (int c = 0; c < C; ++c) {
+      int acc = 0;
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        int rs = 0;
+#pragma unroll
+        for (int e = 0; e < 3; ++e) rs += xw[e] * sb[((long)yi[a] * w + xi[e]) * C + c];
+        acc += yw[a] * rs;
+      }
+      int v = (acc + 32) >> 6;
+      if (res != nullptr) v += res[i * C + c];
+      dst[i * C + c] = static_cast<uint8_t>(min(255, max(0, v)));
+    }
+  }
+}
+
+void pyrup_add_op(const at::Tensor& src, c10::optional<at::Tensor> res, at::Tensor& dst) {
+  TORCH_CHECK(src.scalar_type() == at::kByte && src.dim() == 4 && src.is_contiguous(), "pyrup: uint8 [B,h,w,C]");
+  const int B = static_cast<int>(src.size(0)), h = static_cast<int>(src.size(1)), w = static_cast<int>(src.size(2)),
+            C = static_cast<int>(src.size(3));
+  TORCH_CHECK(dst.scalar_type() == at::kByte && dst.is_contiguous() && dst.size(1) == 2 * h && dst.size(2) == 2 * w &&
+                  dst.size(3) == C, "pyrup: dst uint8 [B,2h,2w,C]");
+  const int16_t* rp = nullptr;
+  if (res.has_value()) {
+    TORCH_CHECK(res->scalar_type() == at::kShort && res->is_contiguous() && res->numel() == dst.numel(), "pyrup: residual int16 like dst");
+    rp = reinterpret_cast<const int16_t*>(res->data_ptr());
+  }
+  const long total = (long)B * 4 * h * w;
+  if (total == 0) return;
+  c10::cuda::CUDAGuard g(src.device());
+  pyrup_add_kernel<<<static_cast<int>(std::min<long>((total + 255) / 256, num_sms() * 16L)), 256, 0,
+                     at::cuda::getCurrentCUDAStream()>>>(src.data_ptr<uint8_t>(), h, w, rp, dst.data_ptr<uint8_t>(), B, C);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ segmentation head tail
+// logits: fp32 [B, h, w, ldl] (first C channels valid). Bilinear upsample (align_corners=False,
+// PyTorch's source-index rule) to [H, W] and argmax over channels -> uint8 labels.
+__global__ void upsample_argmax_kernel(const float* __restrict__ logits, int h, int w, int ldl, int C, int H, int W,
+                                       uint8_t* __restrict__ out, long total) {
+  const float sy = static_cast<float>(h) / H, sx = static_cast<float>(w) / W;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long b = i / ((long)H * W);
+    const int rem = static_cast<int>(i - b * H * W);
+    const int y = rem / W, x = rem - (rem / W) * W;
+    float fy = fmaxf((y + 0.5f) * sy - 0.5f, 0.f);
+    float fx = fmaxf((x + 0.5f) * sx - 0.5f, 0.f);
+    int y0 = min(static_cast<int>(fy), h - 1), x0 = min(static_cast<int>(fx), w - 1);
+    const int y1 = min(y0 + 1, h - 1), x1 = min(x0 + 1, w - 1);
+    const float ly = fy - y0, lx = fx - x0;
+    const float w00 = (1.f - ly) * (1.f - lx), w01 = (1.f - ly) * lx, w10 = ly * (1.f - lx), w11 = ly * lx;
+    const float* p00 = logits + ((b * h + y0) * (long)w + x0) * ldl;
+    const float* p01 = logits + ((b * h + y0) * (long)w + x1) * ldl;
+    const float* p10 = logits + ((b * h + y1) * (long)w + x0) * ldl;
+    const float* p11 = logits + ((b * h + y1) * (long)w + x1) * ldl;
+    float best = -FLT_MAX;
+    int arg = 0;
+    for (int c = 0; c < C; ++c) {
+      const float v = w00 * __ldg(p00 + c) + w01 * __ldg(p01 + c) + w10 * __ldg(p10 + c) + w11 * __ldg(p11 + c);
+      if (v > best) { best = v; arg = c; }
+    }
+    out[i] = static_cast<uint8_t>(arg);
+  }
+}
+
+void upsample_argmax_op(const at::Tensor& logits, int64_t C, int64_t H, int64_t W, at::Tensor& out) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 4 && logits.stride(3) == 1 && logits.is_contiguous(),
+              "upsample_argmax: fp32 [B,h,w,ldl] contiguous");
+  TORCH_CHECK(out.scalar_type() == at::kByte && out.is_contiguous(), "upsample_argmax: uint8 out");
+  const int B = static_cast<int>(logits.size(0)), h = static_cast<int>(logits.size(1)), w = static_cast<int>(logits.size(2));
+  const long total = (long)B * H * W;
+  TORCH_CHECK(out.numel() == total && C <= 256 && C <= logits.size(3), "upsample_argmax: shapes");
+  c10::cuda::CUDAGuard g(logits.device());
+  upsample_argmax_kernel<<<static_cast<int>(std::min<long>((total + 255) / 256, num_sms() * 16L)), 256, 0,
+                           at::cuda::getCurrentCUDAStream()>>>(logits.data_ptr<float>(), h, w, static_cast<int>(logits.size(3)),
+                                                               static_cast<int>(C), static_cast<int>(H), static_cast<int>(W),
+                                                               out.data_ptr<uint8_t>(), total);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ mean over rows
+// x: [B, N, D] bf16 rows [start, N) averaged -> out bf16 [B, D] (written at out + b*ldo).
+__global__ void mean_rows_kernel(const bf16* __restrict__ x, long ldx, int N, int start, int D, bf16* __restrict__ out,
+                                 long ldo) {
+  const int b = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= D) return;
+  float s = 0.f;
+  for (int t = start; t < N; ++t) s += __bfloat162float(x[((long)b * N + t) * ldx + c]);
+  out[(long)b * ldo + c] = __float2bfloat16_rn(s / (N - start));
+}
+
+void mean_rows_op(const at::Tensor& x, int64_t B, int64_t N, int64_t start, at::Tensor& out) {
+  const int D = static_cast<int>(x.size(-1));
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16, "mean_rows: bf16");
+  c10::cuda::CUDAGuard g(x.device());
+  mean_rows_kernel<<<dim3((D + 255) / 256, B), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(-2), static_cast<int>(N), static_cast<int>(start), D,
+      reinterpret_cast<bf16*>(out.data_ptr()), out.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void register_elementwise_ops(pybind11::module_& m) {
+  namespace py = pybind11;
+  m.def("layernorm", &layernorm_op, py::arg("x"), py::arg("rows"), py::arg("w"), py::arg("b"), py::arg("eps"),
+        py::arg("out"), py::arg("copy_out") = py::none());
+  m.def("add_", &add_inplace_op);
+  m.def("patch_im2col", &patch_im2col_op);
+  m.def("set_prefix", &set_prefix_op);
+  m.def("gather_rows", &gather_rows_op);
+  m.def("scatter_rows", &scatter_rows_op);
+  m.def("cls_attn_pscore", &cls_attn_pscore_op);
+  m.def("correction_plan", &correction_plan_op, py::arg("server"), py::arg("pre"), py::arg("cand"), py::arg("mobile"),
+        py::arg("ws"), py::arg("wm"), py::arg("fusion"), py::arg("valid"), py::arg("k"), py::arg("upd"), py::arg("rows"),
+        py::arg("stats") = py::none());
+  m.def("pyrup_add", &pyrup_add_op);
+  m.def("upsample_argmax", &upsample_argmax_op);
+  m.def("mean_rows", &mean_rows_op);
+}
+
+}  // namespace appcorr

@@ -1,0 +1,497 @@
+// Persistent tcgen05 GEMM for sm_100a with fused epilogues.
+//
+// C[M, N] = A[M, K] * B[N, K]^T with bf16 operands and fp32 accumulation in TMEM. A is the
+// activation matrix (row-major, K contiguous) and B an nn.Linear weight (row-major [out, in]),
+// so both operands are K-major.
+//
+// Structure (one CTA per SM, 6 warps):
+//   warp 0      TMA producer: streams 128xBK A tiles and BNxBK B tiles into a STAGES-deep ring
+//               of 128-byte-swizzled shared-memory buffers, signalling `full[s]` by tx-count.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two
+//               TMEM accumulators, commits `empty[s]` per stage and `tfull[acc]` per tile.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per
+//               thread), fused elementwise work, direct global stores; then `tempty[acc]`.
+// Two accumulators let the epilogue of tile t overlap the main loop of tile t+1.
+//
+// The fused epilogues replace the separate elementwise launches of the reference block
+// (appcorr/models/dinov3/layers/block.py:312-349 approx, :943-1191 correct):
+//   EPI_BF16 / EPI_F32  bias add (+ optional output row map, e.g. patch-embed into token rows)
+//   EPI_GELU            fc1 + exact GELU (Mlp, layers/ffn_layers.py:24-49)
+//   EPI_SWIGLU          w1||w2 interleaved in 128-row blocks -> silu(x1) * x2 (ffn_layers.py:60-104,
+//                       the Triton SwiGLU epilogue token_update.py:620-669)
+//   EPI_RESID           out = resid + gamma * (acc + bias) with an optional increment side output
+//                       (LayerScale + residual, token_update.py:11-60; blocks_out_sum bookkeeping
+//                       block.py:333,342,1177-1179; active-row scatter token_update.py:257-347)
+//   EPI_QKV             qkv + bias, RoPE on q/k of patch tokens, split into q / k-cache / v-cache
+//                       with a scatter row map (attention.py:215-240,393-454; rope.py:121-184)
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+
+#include "sm100_common.cuh"
+#include "ops.h"
+
+namespace appcorr {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct TmemCols {
+  static constexpr uint32_t value = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
+                                    : (2 * BN <= 256) ? 256 : 512;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  // Grouped raster: walk 16 M-tiles for every N-tile so a weight tile is reused from L2.
+  constexpr int G = 16;
+  const int per_group = G * num_n;
+  const int group = tile / per_group;
+  const int first_m = group * G;
+  const int gsz = min(G, num_m - first_m);
+  const int r = tile - group * per_group;
+  mb = first_m + r % gsz;
+  nb = r / gsz;
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, float (&v)[32]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u = __ldg(q + i);
+    float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+    v[8 * i + 0] = a.x; v[8 * i + 1] = a.y; v[8 * i + 2] = b.x; v[8 * i + 3] = b.y;
+    v[8 * i + 4] = c.x; v[8 * i + 5] = c.y; v[8 * i + 6] = d.x; v[8 * i + 7] = d.y;
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32_plain(const __nv_bfloat16* p, float (&v)[32]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u = q[i];
+    float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+    v[8 * i + 0] = a.x; v[8 * i + 1] = a.y; v[8 * i + 2] = b.x; v[8 * i + 3] = b.y;
+    v[8 * i + 4] = c.x; v[8 * i + 5] = c.y; v[8 * i + 6] = d.x; v[8 * i + 7] = d.y;
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&v)[32]) {
+  uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+    u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+    u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+    u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+    q[i] = u;
+  }
+}
+
+__device__ __forceinline__ void store_f32x32(float* p, const float (&v)[32]) {
+  float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+__device__ __forceinline__ void acc_to_float(const uint32_t (&r)[32], float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ void add_bias(float (&v)[32], const __nv_bfloat16* bias, int n) {
+  if (bias == nullptr) return;
+  float b[32];
+  load_bf16x32(bias + n, b);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] += b[j];
+}
+
+// Epilogue for one 128 x BN accumulator; each thread owns one row (`m`, possibly >= M).
+template <int BN, int EPI>
+__device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, const GemmShape& shp,
+                                             const GemmEpilogue& ep) {
+  const bool row_ok = m < shp.M;
+  if constexpr (EPI == EPI_SWIGLU) {
+    // Tile columns [0,BN/2) hold w1 rows, [BN/2,BN) the matching w2 rows.
+    constexpr int H = BN / 2;
+    const int nout0 = n0 / 2;
+    const int orow = row_ok ? (ep.out_rows ? ep.out_rows[m] : m) : -1;
+#pragma unroll 1
+    for (int c = 0; c < H / 32; ++c) {
+      uint32_t r1[32], r2[32];
+      tmem_ld32(taddr + c * 32, r1);
+      tmem_ld32(taddr + H + c * 32, r2);
+      tmem_wait_ld();
+      if (orow < 0) continue;
+      float a[32], g[32];
+      acc_to_float(r1, a);
+      acc_to_float(r2, g);
+      add_bias(a, ep.bias, n0 + c * 32);
+      add_bias(g, ep.bias, n0 + H + c * 32);
+      float h[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x1 = bf16_round(a[j]);
+        const float x2 = bf16_round(g[j]);
+        h[j] = bf16_round(silu(x1)) * x2;
+      }
+      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + nout0 + c * 32, h);
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    const int which = n0 / ep.dim;          // 0 = q, 1 = k, 2 = v (tiles never straddle)
+    const int c0 = n0 - which * ep.dim;     // column inside q / k / v
+    int tok = 0, kvrow = 0;
+    if (row_ok) {
+      tok = ep.tok_idx ? ep.tok_idx[m] : (m % ep.seq_len);
+      kvrow = ep.kv_rows ? ep.kv_rows[m] : m;
+    }
+    __nv_bfloat16* dst = nullptr;
+    if (row_ok) {
+      if (which == 0) dst = ep.q_out + (long)m * ep.ld_qkv;
+      else if (which == 1) dst = ep.k_out + (long)kvrow * ep.ld_qkv;
+      else dst = ep.v_out + (long)kvrow * ep.ld_qkv;
+      if (kvrow < 0 && which != 0) dst = nullptr;
+    }
+    if (which == 2) {
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_wait_ld();
+        if (dst == nullptr) continue;
+        float v[32];
+        acc_to_float(r, v);
+        add_bias(v, ep.bias, n0 + c * 32);
+        store_bf16x32(dst + c0 + c * 32, v);
+      }
+    } else {
+      const int Dh = ep.head_dim;
+      const int half = Dh >> 1;
+      const bool rope = row_ok && ep.rope_sin != nullptr && tok >= ep.n_prefix;
+      const int rrow = tok - ep.n_prefix;
+#pragma unroll 1
+      for (int hb = 0; hb < BN; hb += Dh) {
+#pragma unroll 1
+        for (int c = 0; c < half; c += 32) {
+          uint32_t rl[32], rh[32];
+          tmem_ld32(taddr + hb + c, rl);
+          tmem_ld32(taddr + hb + half + c, rh);
+          tmem_wait_ld();
+          if (dst == nullptr) continue;
+          float lo[32], hi[32];
+          acc_to_float(rl, lo);
+          acc_to_float(rh, hi);
+          add_bias(lo, ep.bias, n0 + hb + c);
+          add_bias(hi, ep.bias, n0 + hb + half + c);
+          if (rope) {
+            const float* sn = ep.rope_sin + (long)rrow * Dh;
+            const float* cs = ep.rope_cos + (long)rrow * Dh;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float xl = bf16_round(lo[j]);
+              const float xh = bf16_round(hi[j]);
+              const float sl = __ldg(sn + c + j), cl = __ldg(cs + c + j);
+              const float sh = __ldg(sn + half + c + j), ch = __ldg(cs + half + c + j);
+              lo[j] = xl * cl - xh * sl;
+              hi[j] = xh * ch + xl * sh;
+            }
+          }
+          store_bf16x32(dst + c0 + hb + c, lo);
+          store_bf16x32(dst + c0 + hb + half + c, hi);
+        }
+      }
+    }
+  } else {
+    int orow = -1, rrow = -1, arow = -1;
+    if (row_ok) {
+      orow = ep.out_rows ? ep.out_rows[m] : m;
+      if constexpr (EPI == EPI_RESID) {
+        rrow = ep.resid_rows ? ep.resid_rows[m] : m;
+        arow = ep.aux_rows ? ep.aux_rows[m] : orow;
+      }
+    }
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const int n = n0 + c * 32;
+      if (orow < 0 || n >= shp.N) continue;
+      float v[32];
+      acc_to_float(r, v);
+      add_bias(v, ep.bias, n);
+      if constexpr (EPI == EPI_F32) {
+        store_f32x32(reinterpret_cast<float*>(ep.out) + (long)orow * ep.ldo + n, v);
+      } else if constexpr (EPI == EPI_BF16) {
+        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + n, v);
+      } else if constexpr (EPI == EPI_GELU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(bf16_round(v[j]));
+        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + n, v);
+      } else if constexpr (EPI == EPI_RESID) {
+        float gm[32], rs[32];
+        load_bf16x32(ep.gamma + n, gm);
+        load_bf16x32_plain(ep.resid + (long)rrow * ep.ldr + n, rs);
+        float d[32], o[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          d[j] = bf16_round(bf16_round(v[j]) * gm[j]);
+          o[j] = rs[j] + d[j];
+        }
+        if (ep.aux_mode != AUX_NONE && arow >= 0) {
+          __nv_bfloat16* ap = ep.aux + (long)arow * ep.ldaux + n;
+          float a[32];
+          if (ep.aux_mode == AUX_SET) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = d[j];
+          } else if (ep.aux_mode == AUX_ADD) {
+            load_bf16x32_plain(ap, a);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = a[j] + d[j];
+          } else {
+            float r2[32];
+            load_bf16x32_plain(ep.resid2 + (long)m * ep.ldr2 + n, r2);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = bf16_round(rs[j] - r2[j]) + d[j];
+          }
+          store_bf16x32(ap, a);
+        }
+        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + n, o);
+      }
+    }
+  }
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmShape shp, GemmEpilogue ep) {
+  constexpr uint32_t A_BYTES = kBM * kBK * 2;
+  constexpr uint32_t B_BYTES = BN * kBK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = TmemCols<BN>::value;
+  constexpr uint32_t IDESC = idesc_bf16_f32(kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_addr(&tfull[a]), 1);
+      mbar_init(smem_addr(&tempty[a]), 128);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (shp.M + kBM - 1) / kBM;
+  const int num_n = (shp.N + BN - 1) / BN;
+  const int KB = (shp.K + kBK - 1) / kBK;
+  const int total = num_m * num_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) goto producer_done;
+          const uint32_t fb = smem_addr(&full[s]);
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
+          tma_load_2d(sa, &tmA, fb, kb * kBK, mb * kBM);
+          tma_load_2d(sa + A_BYTES, &tmB, fb, kb * kBK, nb * BN);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+      }
+      // Drain: wait until the consumer has released every stage we filled.
+      for (int i = 0; i < STAGES; ++i) {
+        if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) break;
+        if (++s == STAGES) { s = 0; ph ^= 1; }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int t_local = 0;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++t_local) {
+        const int acc = t_local & 1;
+        const uint32_t acc_ph = (t_local >> 1) & 1;
+        if (!mbar_wait(smem_addr(&tempty[acc]), acc_ph ^ 1, shp.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_f16(d_tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
+                     (kb | k) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(smem_addr(&empty[s]));
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(smem_addr(&tfull[acc]));
+      }
+      (void)issued;
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int t_local = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++t_local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int acc = t_local & 1;
+      const uint32_t acc_ph = (t_local >> 1) & 1;
+      // All lanes wait (tcgen05.ld below is warp-collective).
+      if (!mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      run_epilogue<BN, EPI>(taddr, mb * kBM + row_in_tile, nb * BN, shp, ep);
+      tc_fence_before();
+      mbar_arrive(smem_addr(&tempty[acc]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------ host side
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult qres;
+    void* p = nullptr;
+    auto st = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qres);
+    TORCH_CHECK(st == cudaSuccess && qres == cudaDriverEntryPointSuccess && p != nullptr,
+                "appcorr_b200: cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// Row-major bf16 matrix [rows, cols] with row stride `ld` elements, box = box_rows x 64 columns,
+// 128-byte swizzle. Exposed for the attention kernels as well.
+CUtensorMap make_tmap_bf16_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                              int box_cols) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(r));
+  return m;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, int STAGES, int EPI>
+void launch_gemm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const GemmEpilogue& ep,
+                 int* err, int max_ctas, cudaStream_t stream) {
+  constexpr uint32_t STAGE_BYTES = (kBM + BN) * kBK * 2;
+  constexpr size_t SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  auto kern = gemm_bf16_tn_kernel<BN, STAGES, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM));
+    configured = true;
+  }
+  CUtensorMap ta = make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), kBM, kBK);
+  CUtensorMap tb = make_tmap_bf16_2d(B.data_ptr(), B.size(0), K, B.stride(0), BN, kBK);
+  GemmShape shp{M, N, K, err};
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
+  if (grid <= 0) return;
+  kern<<<grid, kThreads, SMEM, stream>>>(ta, tb, shp, ep);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Dispatch on (epilogue, BN). STAGES chosen to fill ~192 KB of shared memory.
+void gemm_dispatch(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
+                   const GemmEpilogue& ep, int* err, int max_ctas) {
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+#define APPCORR_GEMM_CASE(E)                                                              \
+  case E:                                                                                 \
+    if (bn == 256) launch_gemm<256, 4, E>(A, B, M, N, K, ep, err, max_ctas, st);          \
+    else if (bn == 128) launch_gemm<128, 6, E>(A, B, M, N, K, ep, err, max_ctas, st);     \
+    else if (bn == 64) launch_gemm<64, 8, E>(A, B, M, N, K, ep, err, max_ctas, st);       \
+    else TORCH_CHECK(false, "unsupported BN ", bn);                                       \
+    break;
+  switch (epi) {
+    APPCORR_GEMM_CASE(EPI_BF16)
+    APPCORR_GEMM_CASE(EPI_F32)
+    APPCORR_GEMM_CASE(EPI_GELU)
+    APPCORR_GEMM_CASE(EPI_RESID)
+    case EPI_SWIGLU:
+      TORCH_CHECK(bn == 256, "swiglu epilogue uses BN=256");
+      launch_gemm<256, 4, EPI_SWIGLU>(A, B, M, N, K, ep, err, max_ctas, st);
+      break;
+    case EPI_QKV:
+      if (bn == 256) launch_gemm<256, 4, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
+      else if (bn == 128) launch_gemm<128, 6, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
+      else TORCH_CHECK(false, "qkv epilogue uses BN=128 or 256");
+      break;
+    default:
+      TORCH_CHECK(false, "unknown epilogue ", epi);
+  }
+#undef APPCORR_GEMM_CASE
+}
+
+}  // namespace appcorr
