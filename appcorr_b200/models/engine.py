@@ -1,0 +1,366 @@
+"""sm_100a execution engine for the DINOv3 ViT approximate / correct passes.
+
+The engine owns kernel-layout copies of the backbone weights and a per-session workspace, and
+drives the hand-written kernels of `appcorr_b200._C` directly; no PyTorch compute op runs on
+its hot path. One layer of the approximate pass (reference block.py:312-349) is
+
+    LN1 -> qkv GEMM [+bias, RoPE, split into q / K-cache / V-cache] -> CLS pscore
+        -> attention -> proj GEMM [x + ls1*(.), increment := ls1*(.)]
+        -> LN2 -> fc1/w12 GEMM [GELU | SwiGLU] -> fc2/w3 GEMM [x + ls2*(.), increment += ls2*(.)]
+
+and one layer of the correction pass (block.py:943-1191) is
+
+    plan (score + top-k, on device) -> gather + LN1 of the kept rows -> x += increment (all rows)
+        -> qkv GEMM on kept rows [RoPE, K/V rows scattered into the cache]
+        -> attention (packed queries vs. the whole cache) -> proj GEMM [x_act + ls1*(.)]
+        -> LN2 -> fc1/w12 GEMM -> fc2/w3 GEMM [scatter x_attn + ls2*(.) into x;
+                                               increment := (x_attn - x_act) + ls2*(.)]
+
+Everything is statically shaped for a given (batch, resolution, keep ratio), so a pass can be
+captured into a CUDA graph (see `capture`).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from ..common.protocol import LAYERMEAN_SERVER_PSCORES
+from ..ops import kernels as K
+from .dinov3.layers import linear_bias
+from .dinov3.vit import DinoVisionTransformer, ViTConfig
+from .weights import pack_swiglu
+
+BF16 = torch.bfloat16
+
+
+@dataclass
+class LayerW:
+    norm1_w: torch.Tensor
+    norm1_b: torch.Tensor
+    qkv_w: torch.Tensor
+    qkv_b: Optional[torch.Tensor]
+    proj_w: torch.Tensor
+    proj_b: Optional[torch.Tensor]
+    ls1: torch.Tensor
+    norm2_w: torch.Tensor
+    norm2_b: torch.Tensor
+    fc1_w: torch.Tensor           # fc1 [hidden, D] or packed w1||w2 [2*hidden, D]
+    fc1_b: Optional[torch.Tensor]
+    fc2_w: torch.Tensor           # fc2 / w3 [D, hidden]
+    fc2_b: Optional[torch.Tensor]
+    ls2: torch.Tensor
+
+
+@dataclass
+class EngineWeights:
+    cfg: ViTConfig
+    patch_w: torch.Tensor         # [D, 3*p*p]
+    patch_b: torch.Tensor         # [D]
+    prefix: torch.Tensor          # [1 + n_storage, D]
+    periods: torch.Tensor         # RoPE periods (fp32)
+    layers: List[LayerW]
+    norm_w: torch.Tensor
+    norm_b: torch.Tensor
+    cls_norm_w: Optional[torch.Tensor] = None
+    cls_norm_b: Optional[torch.Tensor] = None
+
+
+def _bf(t: Optional[torch.Tensor], device) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    return t.detach().to(device=device, dtype=BF16).contiguous()
+
+
+def weights_from_module(model: DinoVisionTransformer, device) -> EngineWeights:
+    """Kernel-layout copy of a (CPU or GPU) DINOv3 module's parameters."""
+    cfg = model.cfg
+    layers = []
+    for blk in model.blocks:
+        mlp = blk.mlp
+        if cfg.is_swiglu:
+            w, b = pack_swiglu(mlp.w1.weight.detach(), mlp.w2.weight.detach(),
+                               None if mlp.w1.bias is None else mlp.w1.bias.detach(),
+                               None if mlp.w2.bias is None else mlp.w2.bias.detach())
+            fc1_w, fc1_b, fc2 = w, b, mlp.w3
+        else:
+            fc1_w, fc1_b, fc2 = mlp.fc1.weight.detach(), mlp.fc1.bias, mlp.fc2
+        layers.append(LayerW(
+            norm1_w=_bf(blk.norm1.weight, device), norm1_b=_bf(blk.norm1.bias, device),
+            qkv_w=_bf(blk.attn.qkv.weight, device), qkv_b=_bf(linear_bias(blk.attn.qkv), device),
+            proj_w=_bf(blk.attn.proj.weight, device), proj_b=_bf(blk.attn.proj.bias, device),
+            ls1=_bf(blk.ls1.gamma, device), norm2_w=_bf(blk.norm2.weight, device),
+            norm2_b=_bf(blk.norm2.bias, device), fc1_w=_bf(fc1_w, device), fc1_b=_bf(fc1_b, device),
+            fc2_w=_bf(fc2.weight, device), fc2_b=_bf(fc2.bias, device), ls2=_bf(blk.ls2.gamma, device)))
+    pw = model.patch_embed.proj.weight.detach()
+    return EngineWeights(
+        cfg=cfg,
+        patch_w=_bf(pw.reshape(pw.shape[0], -1), device),
+        patch_b=_bf(model.patch_embed.proj.bias, device),
+        prefix=_bf(model.prefix_tokens(), device),
+        periods=model.rope_embed.periods.detach().to(device=device, dtype=torch.float32),
+        layers=layers,
+        norm_w=_bf(model.norm.weight, device), norm_b=_bf(model.norm.bias, device),
+        cls_norm_w=_bf(model.cls_norm.weight, device) if model.cls_norm is not None else None,
+        cls_norm_b=_bf(model.cls_norm.bias, device) if model.cls_norm is not None else None,
+    )
+
+
+def random_weights(cfg: ViTConfig, device, seed: int = 0, std: float = 0.02) -> EngineWeights:
+    """Random-init weights generated directly on the device in kernel layout (synthetic runs).
+
+    Same distribution family as the reference init (trunc-normal std 0.02 Linears, zero biases,
+    LayerScale 1e-5, unit LayerNorm); built layer by layer so a 7B model never exists twice.
+    """
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    D, Hd = cfg.embed_dim, cfg.ffn_hidden
+
+    def lin(o, i):
+        return (torch.randn(o, i, device=device, generator=g) * std).clamp_(-2 * std, 2 * std).to(BF16)
+
+    def zeros(n):
+        return torch.zeros(n, device=device, dtype=BF16)
+
+    def ones(n):
+        return torch.ones(n, device=device, dtype=BF16)
+
+    ls = cfg.layerscale_init or 1.0
+    layers = []
+    for _ in range(cfg.depth):
+        fc1 = 2 * Hd if cfg.is_swiglu else Hd
+        layers.append(LayerW(
+            norm1_w=ones(D), norm1_b=zeros(D), qkv_w=lin(3 * D, D), qkv_b=zeros(3 * D) if cfg.qkv_bias else None,
+            proj_w=lin(D, D), proj_b=zeros(D) if cfg.proj_bias else None, ls1=torch.full((D,), ls, device=device, dtype=BF16),
+            norm2_w=ones(D), norm2_b=zeros(D), fc1_w=lin(fc1, D), fc1_b=zeros(fc1) if cfg.ffn_bias else None,
+            fc2_w=lin(D, Hd), fc2_b=zeros(D) if cfg.ffn_bias else None, ls2=torch.full((D,), ls, device=device, dtype=BF16)))
+    p = cfg.patch_size
+    bound = 1.0 / math.sqrt(3 * p * p)
+    n = cfg.head_dim // 4
+    periods = cfg.pos_embed_rope_base ** (2 * torch.arange(n, device=device, dtype=torch.float32) / (cfg.head_dim // 2))
+    return EngineWeights(
+        cfg=cfg,
+        patch_w=((torch.rand(D, 3 * p * p, device=device, generator=g) * 2 - 1) * bound).to(BF16),
+        patch_b=((torch.rand(D, device=device, generator=g) * 2 - 1) * bound).to(BF16),
+        prefix=(torch.randn(cfg.n_prefix, D, device=device, generator=g) * 0.02).to(BF16),
+        periods=periods, layers=layers, norm_w=ones(D), norm_b=zeros(D),
+        cls_norm_w=ones(D) if cfg.untie_cls_and_patch_norms else None,
+        cls_norm_b=zeros(D) if cfg.untie_cls_and_patch_norms else None)
+
+
+def rope_tables(cfg: ViTConfig, periods: torch.Tensor, H: int, W: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """fp32 (sin, cos) [H*W, head_dim], same construction as RopePositionEmbedding.forward."""
+    dev = periods.device
+    if cfg.pos_embed_rope_normalize_coords == "max":
+        dh = dw = max(H, W)
+    elif cfg.pos_embed_rope_normalize_coords == "min":
+        dh = dw = min(H, W)
+    else:
+        dh, dw = H, W
+    ch = torch.arange(0.5, H, device=dev, dtype=torch.float32) / dh
+    cw = torch.arange(0.5, W, device=dev, dtype=torch.float32) / dw
+    coords = torch.stack(torch.meshgrid(ch, cw, indexing="ij"), dim=-1).flatten(0, 1) * 2.0 - 1.0
+    ang = (2 * math.pi * coords[:, :, None] / periods.float()[None, None, :]).flatten(1, 2).tile(2)
+    return torch.sin(ang).contiguous(), torch.cos(ang).contiguous()
+
+
+@dataclass
+class Session:
+    """Per-request device state: activations, per-layer caches and correction scratch."""
+
+    B: int
+    img_hw: Tuple[int, int]
+    grid_hw: Tuple[int, int]
+    N: int
+    P: int
+    x_in: torch.Tensor            # fresh tokens from the current canvas [B*N, D]
+    x: torch.Tensor               # running features [B*N, D]
+    x_tmp: torch.Tensor           # approx ping-pong partner
+    xn: torch.Tensor              # LayerNorm output [B*N, D]
+    q: torch.Tensor               # [B*N, D]
+    o: torch.Tensor               # attention output [B*N, D]
+    h: torch.Tensor               # MLP hidden [B*N, hidden]
+    kc: torch.Tensor              # [L, B*N, D] K after RoPE
+    vc: torch.Tensor              # [L, B*N, D]
+    bos: torch.Tensor             # [L, B*N, D] per-layer increment
+    pscore: torch.Tensor          # [L, B, N] fp32 server score
+    ps_scratch: torch.Tensor      # [B, H, N] fp32
+    cols: torch.Tensor            # im2col [B*P, 3*p*p]
+    patch_rows: torch.Tensor      # int32 token rows of the patch tokens [B*P]
+    rope: Tuple[torch.Tensor, torch.Tensor]
+    # correction scratch (sized for keeping every candidate)
+    upd: torch.Tensor
+    rows: torch.Tensor
+    x_act: torch.Tensor
+    x_att: torch.Tensor
+    plan_stats: torch.Tensor      # [B, 2] fp32
+    stat_acc: torch.Tensor        # [5] fp32 accumulated plan statistics
+    approx_done: int = 0
+    extra: Dict[str, torch.Tensor] = field(default_factory=dict)
+
+
+class ViTEngine:
+    def __init__(self, weights: EngineWeights, device=None):
+        self.w = weights
+        self.cfg = weights.cfg
+        self.device = torch.device(device) if device is not None else weights.patch_w.device
+        if self.cfg.head_dim not in (64, 128):
+            raise ValueError("the sm_100a engine supports head_dim 64 or 128")
+
+    @classmethod
+    def from_module(cls, model: DinoVisionTransformer, device) -> "ViTEngine":
+        return cls(weights_from_module(model, device), device)
+
+    @classmethod
+    def random(cls, cfg: ViTConfig, device, seed: int = 0) -> "ViTEngine":
+        return cls(random_weights(cfg, device, seed), device)
+
+    # -------------------------------------------------------------- sessions
+    def new_session(self, B: int, H: int, W: int) -> Session:
+        c, dev = self.cfg, self.device
+        p = c.patch_size
+        gh, gw = H // p, W // p
+        P = gh * gw
+        N = P + c.n_prefix
+        D, L, Hd = c.embed_dim, c.depth, c.ffn_hidden
+        M = B * N
+
+        def e(*shape, dtype=BF16):
+            return torch.empty(*shape, device=dev, dtype=dtype)
+
+        patch_rows = (torch.arange(B, device=dev)[:, None] * N + c.n_prefix + torch.arange(P, device=dev)[None, :])
+        T = c.n_prefix + P
+        sess = Session(
+            B=B, img_hw=(H, W), grid_hw=(gh, gw), N=N, P=P,
+            x_in=e(M, D), x=e(M, D), x_tmp=e(M, D), xn=e(M, D), q=e(M, D), o=e(M, D), h=e(M, Hd),
+            kc=e(L, M, D), vc=e(L, M, D), bos=e(L, M, D), pscore=torch.zeros(L, B, N, device=dev),
+            ps_scratch=e(B, c.num_heads, N, dtype=torch.float32), cols=e(B * P, 3 * p * p),
+            patch_rows=patch_rows.reshape(-1).to(torch.int32).contiguous(),
+            rope=rope_tables(c, self.w.periods, gh, gw),
+            upd=torch.zeros(B, T, device=dev, dtype=torch.int32), rows=torch.zeros(B * T, device=dev, dtype=torch.int32),
+            x_act=e(B * T, D), x_att=e(B * T, D), plan_stats=torch.zeros(B, 2, device=dev),
+            stat_acc=torch.zeros(5, device=dev))
+        return sess
+
+    # -------------------------------------------------------------- tokens
+    def prepare_tokens(self, sess: Session, img: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """uint8 [B, H, W, 3] image -> tokens [B*N, D] (CLS + storage + patch embeddings)."""
+        c = self.cfg
+        out = sess.x_in if out is None else out
+        K.patch_im2col(img, c.patch_size, sess.cols)
+        K.gemm(sess.cols, self.w.patch_w, out, bias=self.w.patch_b, out_rows=sess.patch_rows)
+        K.set_prefix(out, self.w.prefix, sess.B, sess.N)
+        return out
+
+    # -------------------------------------------------------------- approximate pass
+    def _mlp(self, lw: LayerW, xin: torch.Tensor, hbuf: torch.Tensor) -> torch.Tensor:
+        if self.cfg.is_swiglu:
+            K.gemm(xin, lw.fc1_w, hbuf, epi=K.EPI_SWIGLU, bias=lw.fc1_b)
+        else:
+            K.gemm(xin, lw.fc1_w, hbuf, epi=K.EPI_GELU, bias=lw.fc1_b)
+        return hbuf
+
+    def approx_layer(self, sess: Session, l: int, x: torch.Tensor, x_out: torch.Tensor, server_pscore: str) -> None:
+        c, lw = self.cfg, self.w.layers[l]
+        B, N, H, Dh = sess.B, sess.N, c.num_heads, c.head_dim
+        K.layernorm(x, lw.norm1_w, lw.norm1_b, c.norm_eps, sess.xn)
+        K.qkv_gemm(sess.xn, lw.qkv_w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
+                   rope=sess.rope, n_prefix=c.n_prefix)
+        if server_pscore not in ("none", "disabled"):
+            K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=sess.pscore[l])
+        K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh)
+        # x_out = x + ls1 * proj(o); bos[l] = ls1 * proj(o)
+        K.gemm(sess.o, lw.proj_w, x_out, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x,
+               aux=sess.bos[l], aux_mode=K.AUX_SET)
+        K.layernorm(x_out, lw.norm2_w, lw.norm2_b, c.norm_eps, sess.xn)
+        self._mlp(lw, sess.xn, sess.h)
+        # x_out += ls2 * mlp (in place: each output element reads only its own residual); bos[l] += same
+        K.gemm(sess.h, lw.fc2_w, x_out, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_out,
+               aux=sess.bos[l], aux_mode=K.AUX_ADD)
+
+    def approx(self, sess: Session, start: int, end: int, server_pscore: str = "cls_attn_prob") -> torch.Tensor:
+        """Approximate pass over layers [start, end) on the running features."""
+        if start == 0:
+            sess.x.copy_(sess.x_in)
+        for l in range(start, end):
+            self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
+        sess.approx_done = max(sess.approx_done, end)
+        return sess.x
+
+    # -------------------------------------------------------------- correction pass
+    def plan(self, sess: Session, l: int, pre: torch.Tensor, cand: torch.Tensor, k: int, opts: Dict,
+             mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None,
+             server: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        B = sess.B
+        T = pre.shape[1] + k
+        upd = sess.upd.view(-1)[: B * T].view(B, T)
+        rows = sess.rows[: B * T]
+        if server is None:
+            server = sess.pscore[l]
+        K.correction_plan(server, pre, cand, k, upd, rows, mobile=mobile, ws=float(opts.get("server_pscore_weight", 1.0)),
+                          wm=float(opts.get("mobile_pscore_weight", 0.0)), fusion=opts.get("pscore_fusion", "add"),
+                          valid=valid, stats=sess.plan_stats)
+        return upd, rows
+
+    def correct_layer(self, sess: Session, l: int, x: torch.Tensor, upd: torch.Tensor, rows: torch.Tensor) -> None:
+        c, lw = self.cfg, self.w.layers[l]
+        B, N, H, Dh = sess.B, sess.N, c.num_heads, c.head_dim
+        T = upd.shape[1]
+        MT = B * T
+        x_act, x_att = sess.x_act[:MT], sess.x_att[:MT]
+        xn = sess.xn[:MT]
+        q, o, h = sess.q[:MT], sess.o[:MT], sess.h[:MT]
+        K.layernorm(x, lw.norm1_w, lw.norm1_b, c.norm_eps, xn, rows=rows, copy_out=x_act)
+        K.add_(x, sess.bos[l])
+        K.qkv_gemm(xn, lw.qkv_w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
+                   kv_rows=rows, rope=sess.rope, n_prefix=c.n_prefix)
+        K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh)
+        K.gemm(o, lw.proj_w, x_att, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x_act)
+        K.layernorm(x_att, lw.norm2_w, lw.norm2_b, c.norm_eps, xn)
+        self._mlp(lw, xn, h)
+        # x[rows] = x_att + ls2 * mlp; bos[l][rows] = (x_att - x_act) + ls2 * mlp
+        K.gemm(h, lw.fc2_w, x, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_att, out_rows=rows,
+               aux=sess.bos[l], aux_mode=K.AUX_OUT_MINUS, resid2=x_act)
+
+    def correct(self, sess: Session, start: int, end: int, pre: torch.Tensor, cand: torch.Tensor, opts: Dict,
+                mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Correction pass over layers [start, end) starting from the fresh tokens `sess.x_in`.
+
+        pre: int32 [B, n_prefix] prefix token indices; cand: int32 [B, P_g] candidate patch tokens
+        (the residual group that just arrived). Keeps k = int(P_g * token_keep_ratio) per image.
+        """
+        P_g = cand.shape[1]
+        ratio = float(opts.get("token_keep_ratio", 0.2))
+        k = min(int(P_g * ratio), P_g)
+        if opts.get("token_keep_thres") is not None:
+            raise NotImplementedError("threshold selection on the sm_100a engine uses token_keep_cap (sync-free)")
+        kind = str(opts.get("server_pscore", "cls_attn_prob"))
+        if start == 0:
+            sess.x.copy_(sess.x_in)
+        x = sess.x
+        shared = None
+        if kind in LAYERMEAN_SERVER_PSCORES:
+            shared = sess.extra.get("layermean")
+            if shared is None:
+                shared = sess.pscore[: max(sess.approx_done, 1)].mean(0)
+                sess.extra["layermean"] = shared
+        upd = rows = None
+        for l in range(start, end):
+            if upd is None or shared is None:
+                upd, rows = self.plan(sess, l, pre, cand, k, opts, mobile=mobile, valid=valid, server=shared)
+            self.correct_layer(sess, l, x, upd, rows)
+        return x
+
+    # -------------------------------------------------------------- outputs
+    def patch_features(self, sess: Session, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Final LayerNorm of the patch tokens -> [B*P, D]."""
+        c = self.cfg
+        if out is None:
+            out = sess.extra.get("patch_feat")
+            if out is None:
+                out = torch.empty(sess.B * sess.P, c.embed_dim, device=self.device, dtype=BF16)
+                sess.extra["patch_feat"] = out
+        K.layernorm(sess.x, self.w.norm_w, self.w.norm_b, c.norm_eps, out, rows=sess.patch_rows)
+        return out

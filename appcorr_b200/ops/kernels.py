@@ -14,6 +14,14 @@ from .native import err_word, lib
 EPI_BF16, EPI_F32, EPI_GELU, EPI_SWIGLU, EPI_RESID, EPI_QKV = range(6)
 AUX_NONE, AUX_SET, AUX_ADD, AUX_OUT_MINUS = range(4)
 
+# Number of native kernel launches issued through this module (read by the benchmark).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
 IMAGENET_MEAN = (0.485, 0.456, 0.406)
 IMAGENET_STD = (0.229, 0.224, 0.225)
 
@@ -36,6 +44,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
     """out = epilogue(a @ w^T). `a` [M, K] bf16, `w` [N, K] bf16 (nn.Linear layout)."""
     if bn is None:
         bn = 256 if epi == EPI_SWIGLU else _pick_bn(w.shape[0], a.shape[0])
+    _count()
     lib().gemm(a, w, epi, bn, err_word(a.device), out=out, out_rows=out_rows, bias=bias, gamma=gamma,
                resid=resid, resid_rows=resid_rows, aux=aux, aux_rows=aux_rows, aux_mode=aux_mode,
                resid2=resid2, max_ctas=max_ctas)
@@ -56,6 +65,7 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
     if bn is None:
         bn = 256 if dim % 256 == 0 else 128
     sin, cos = rope if rope is not None else (None, None)
+    _count()
     lib().gemm(a, w, EPI_QKV, bn, err_word(a.device), bias=bias, q_out=q_out, k_out=k_out, v_out=v_out,
                kv_rows=kv_rows, tok_idx=tok_idx, seq_len=seq_len, rope_sin=sin, rope_cos=cos,
                n_prefix=n_prefix, head_dim=head_dim)
@@ -64,11 +74,13 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
 def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, out: torch.Tensor,
               rows: Optional[torch.Tensor] = None, copy_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out[i] = LN(x[rows[i]]) (rows=None: every row). copy_out[i] receives the raw gathered row."""
+    _count()
     lib().layernorm(x, rows, w, b, float(eps), out, copy_out)
     return out
 
 
 def add_(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    _count()
     lib().add_(x, y)
     return x
 
@@ -79,26 +91,31 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor
     """Non-causal attention on BTHD tensors: q/o [B*Tq, H*Dh], k/v [B*Tk, H*Dh]."""
     if scale is None:
         scale = Dh ** -0.5
+    _count()
     lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
     return o
 
 
 def patch_im2col(img: torch.Tensor, patch: int, out: torch.Tensor,
                  mean: Sequence[float] = IMAGENET_MEAN, std: Sequence[float] = IMAGENET_STD) -> torch.Tensor:
+    _count()
     lib().patch_im2col(img, patch, list(mean), list(std), out)
     return out
 
 
 def set_prefix(x: torch.Tensor, prefix: torch.Tensor, B: int, N: int) -> None:
+    _count()
     lib().set_prefix(x, prefix, B, N)
 
 
 def gather_rows(src: torch.Tensor, rows: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    _count()
     lib().gather_rows(src, rows, out)
     return out
 
 
 def scatter_rows(src: torch.Tensor, rows: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
+    _count()
     lib().scatter_rows(src, rows, dst)
     return dst
 
@@ -107,6 +124,7 @@ def cls_attn_pscore(q: torch.Tensor, k: torch.Tensor, *, B: int, N: int, H: int,
                     scratch: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None) -> torch.Tensor:
     if scale is None:
         scale = Dh ** -0.5
+    _count(2)
     lib().cls_attn_pscore(q, k, B, N, H, Dh, float(scale), scratch, out)
     return out
 
@@ -118,20 +136,24 @@ def correction_plan(server: torch.Tensor, pre: torch.Tensor, cand: torch.Tensor,
                     rows: torch.Tensor, *, mobile: Optional[torch.Tensor] = None, ws: float = 1.0,
                     wm: float = 0.0, fusion: str = "add", valid: Optional[torch.Tensor] = None,
                     stats: Optional[torch.Tensor] = None) -> None:
+    _count()
     lib().correction_plan(server, pre, cand, mobile, float(ws), float(wm), FUSION.get(fusion, 0), valid, int(k),
                           upd, rows, stats)
 
 
 def pyrup_add(src: torch.Tensor, res: Optional[torch.Tensor], out: torch.Tensor) -> torch.Tensor:
+    _count()
     lib().pyrup_add(src, res, out)
     return out
 
 
 def upsample_argmax(logits: torch.Tensor, C: int, H: int, W: int, out: torch.Tensor) -> torch.Tensor:
+    _count()
     lib().upsample_argmax(logits, C, H, W, out)
     return out
 
 
 def mean_rows(x: torch.Tensor, B: int, N: int, start: int, out: torch.Tensor) -> torch.Tensor:
+    _count()
     lib().mean_rows(x, B, N, start, out)
     return out

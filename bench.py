@@ -1,0 +1,440 @@
+#!/usr/bin/env python
+"""Headline benchmark: corrected-result latency and images/s of DINOv3 ViT-7B/16 serving.
+
+One step = one request of `--batch` synthetic 512x512 images encoded as a 2-level Laplacian
+pyramid (256x256 uint8 base + 512x512 int16 residual):
+    reconstruct base-only canvas -> tokens -> approximate pass over all 40 layers
+    -> reconstruct full canvas -> tokens -> correction pass over all 40 layers keeping the top 30%
+       of patch tokens (CLS-attention server score) with cached K/V rewrite
+    -> final norm -> linear segmentation head (150 classes) -> pixel labels.
+
+Two measurements per run:
+  value  device time of K steps (CUDA events, inputs already on the device), max over ranks.
+  e2e    the same request through the public executor API (`get_model_executor(...)` +
+         preprocess / prepare_tokens / approx_forward / correct_forward / head_inference /
+         get_final_results) including the host->device copy of the pyramid from pinned memory and
+         the device->host read of the labels every step.
+
+`--impl reference` runs the unmodified reference implementation installed under baseline/_ref
+through its own executor API on the same workload.
+
+Launch: python bench.py [--gpus 1] or, for N > 1,
+  python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+BASELINE_METRIC = "corrected-result p50/p99 latency & images/s, ViT-7B TP at 1/2/4/8 B200"
+# BASELINE.md publishes no images/s figure for this config, so vs_baseline is null.
+BASELINE_VALUE = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--res", type=int, default=512)
+    ap.add_argument("--keep", type=float, default=0.3)
+    ap.add_argument("--arch", default="vit7b16")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- data
+def synthetic_pyramid(batch: int, res: int, seed: int):
+    """Clipped N(128, 60^2) RGB images -> (images, base uint8, residual int16) on the host."""
+    sys.path.insert(0, ROOT)
+    from appcorr_b200.policies.transmission.pyramid import pyr_down, pyr_up
+
+    rng = np.random.default_rng(seed)
+    imgs = np.clip(rng.normal(128, 60, size=(batch, res, res, 3)), 0, 255).astype(np.uint8)
+    base = np.stack([pyr_down(im) for im in imgs])
+    res_ = np.stack([im.astype(np.int16) - pyr_up(b).astype(np.int16) for im, b in zip(imgs, base)])
+    return imgs, base, res_
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpu_indices):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if gpu_indices is not None and idx not in gpu_indices:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                pass
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        busy = [s for s in sm if mx is None or s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup(n_gpus: int):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- our implementation
+def make_config(args):
+    sys.path.insert(0, ROOT)
+    from appcorr_b200.common.protocol import ExperimentConfig
+
+    return ExperimentConfig(
+        exp_id="bench", model_name="dinov3_segmentor_linhead", batch_size=args.batch,
+        image_shape=(args.res, args.res, 3), input_profile_name="dinov3_ade20k_linhead_official",
+        input_profile_kwargs={"backbone_arch": args.arch, "server_inference_mode": "whole"},
+        scheduler_policy_name="GroupTrigger", transmission_policy_name="ProgressiveLaplacian",
+        transmission_kwargs={"pyramid_levels": [1, 0], "num_groups": 1, "grouping_strategy": "grid"},
+        appcorr_kwargs={"token_keep_ratio": args.keep, "server_pscore": "cls_attn_prob"})
+
+
+def run_mine(args, rank, world):
+    import torch
+
+    sys.path.insert(0, ROOT)
+    from appcorr_b200.common.protocol import Task
+    from appcorr_b200.ops import kernels as K
+    from appcorr_b200.ops.native import check_errors
+    from appcorr_b200.server.model import PyramidBatch, get_model_executor
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = make_config(args)
+    ex = get_model_executor(cfg.model_name, dev)
+    ex.load_model(cfg.model_name, cfg)
+    L = ex.cfg.depth
+    imgs, base, resid = synthetic_pyramid(args.batch, args.res, seed=rank)
+    base_h = torch.from_numpy(base).pin_memory()
+    res_h = torch.from_numpy(resid).pin_memory()
+    task = Task(task_id=0, request_id=0, payload=[], instructions=[])
+
+    # ---- device-resident variant for the kernel-time measurement
+    base_d = base_h.to(dev)
+    res_d = res_h.to(dev)
+
+    def device_step(ctx):
+        ex.preprocess(PyramidBatch(base_d, None), task, ctx, cfg)
+        ex.prepare_tokens(task, ctx, cfg)
+        ex.approx_forward({"layers": (0, L)}, ctx, cfg)
+        ex.preprocess(PyramidBatch(base_d, res_d), task, ctx, cfg)
+        ex.prepare_tokens(task, ctx, cfg)
+        ex.correct_forward({"layers": (0, L), "group_id": 1}, ctx, cfg)
+        ex.head_inference(task, ctx, cfg)
+
+    ctx = {}
+    for _ in range(args.warmup):
+        device_step(ctx)
+    torch.cuda.synchronize()
+    check_errors(dev)
+    n0 = K.LAUNCHES[0]
+    device_step(ctx)
+    launches_per_step = K.LAUNCHES[0] - n0
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler() if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    t0.record()
+    step_ev[0].record()
+    for i in range(args.steps):
+        device_step(ctx)
+        step_ev[i + 1].record()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop(None) if clocks else None
+    check_errors(dev)
+    ms = t0.elapsed_time(t1) / args.steps
+    per_step = sorted(step_ev[i].elapsed_time(step_ev[i + 1]) for i in range(args.steps))
+    ms_max = max_over_ranks(ms, world)
+
+    # ---- end-to-end through the public API: pinned host inputs in, labels out, every step
+    e2e = None
+    if not args.no_e2e:
+        n_e2e = args.e2e_steps or max(3, args.steps)
+        h2d = base_h.numel() * base_h.element_size() + res_h.numel() * res_h.element_size()
+        d2h = args.batch * args.res * args.res  # uint8 labels
+        ctx2 = {}
+
+        def e2e_step():
+            ex.preprocess(PyramidBatch(base_h, None), task, ctx2, cfg)
+            ex.prepare_tokens(task, ctx2, cfg)
+            ex.approx_forward({"layers": (0, L)}, ctx2, cfg)
+            ex.preprocess(PyramidBatch(base_h, res_h), task, ctx2, cfg)
+            ex.prepare_tokens(task, ctx2, cfg)
+            ex.correct_forward({"layers": (0, L), "group_id": 1}, ctx2, cfg)
+            ex.head_inference(task, ctx2, cfg)
+            return ex.get_final_results(task, ctx2, cfg)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        lat = []
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n_e2e):
+            s = time.perf_counter()
+            out = e2e_step()
+            lat.append((time.perf_counter() - s) * 1e3)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / n_e2e, world)
+        assert len(out) == args.batch and out[0]["mask"].shape == (args.res, args.res)
+        lat.sort()
+        e2e = {"value": round(args.batch * world * 1e3 / e2e_ms, 3), "unit": "images/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "p50_ms": round(lat[len(lat) // 2], 3), "p99_ms": round(lat[min(len(lat) - 1, int(0.99 * len(lat)))], 3),
+               "ms_per_step": round(e2e_ms, 3)}
+    return ms_max, per_step, launches_per_step, clk, e2e
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    """Reference executor (baseline/_ref, unmodified) on the same synthetic workload.
+
+    Two accommodations, neither touching the compute path: the `nvtx` Python package it imports
+    is not installed here, so a no-op stand-in is registered; and there are no checkpoints, so
+    its weight loader is pointed at the randomly initialised modules it just built.
+    """
+    import types
+
+    import torch
+
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "offload")):
+        return None, "baseline/_ref/offload missing (reference not installed)"
+    sys.path.insert(0, ref_root)
+    if "nvtx" not in sys.modules:
+        nv = types.ModuleType("nvtx")
+
+        def annotate(*a, **k):
+            if a and callable(a[0]) and not k:
+                return a[0]
+            return lambda f: f
+
+        nv.annotate = annotate
+        sys.modules["nvtx"] = nv
+    from offload.common.protocol import ExperimentConfig, Task  # reference's own classes
+    import offload.server.model.dinov3_segmentor_linhead as lh
+
+    holder = {}
+    orig_vit = None
+
+    def fake_loader(path):
+        if "head" in str(path):
+            D = holder["backbone"].embed_dim
+            g = torch.Generator().manual_seed(0)
+            sd = {"batchnorm_layer.weight": 1 + 0.1 * torch.randn(D, generator=g),
+                  "batchnorm_layer.bias": 0.1 * torch.randn(D, generator=g),
+                  "batchnorm_layer.running_mean": 0.1 * torch.randn(D, generator=g),
+                  "batchnorm_layer.running_var": 1 + 0.1 * torch.rand(D, generator=g),
+                  "batchnorm_layer.num_batches_tracked": torch.tensor(0),
+                  "conv.weight": 0.02 * torch.randn(150, D, 1, 1, generator=g), "conv.bias": torch.zeros(150)}
+            return {"segmentation_model.1." + k: v for k, v in sd.items()}
+        return holder["backbone"].state_dict()
+
+    lh.load_weight_mmap = fake_loader
+    lh.DINOv3SegmentorLinheadExecutor._ensure_dinov3_import_path()
+    import dinov3.hub.backbones as hb
+
+    orig_vit = hb.dinov3_vit7b16
+
+    def capture_vit(*a, **k):
+        m = orig_vit(*a, **k)
+        holder["backbone"] = m
+        return m
+
+    hb.dinov3_vit7b16 = capture_vit
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = ExperimentConfig(
+        exp_id="bench_ref", model_name="dinov3_segmentor_linhead", batch_size=args.batch,
+        image_shape=(args.res, args.res, 3), input_profile_name="dinov3_ade20k_linhead_official",
+        input_profile_kwargs={"server_inference_mode": "whole"},
+        scheduler_policy_name="GroupTrigger", transmission_policy_name="ProgressiveLaplacian",
+        transmission_kwargs={"pyramid_levels": [1, 0], "num_groups": 1, "grouping_strategy": "grid"},
+        appcorr_kwargs={"token_keep_ratio": args.keep, "server_pscore": "cls_attn_prob"})
+    ex = lh.DINOv3SegmentorLinheadExecutor(dev)
+    ex.load_model("dinov3_segmentor_linhead", cfg)
+    L = len(ex.vit_backbone.blocks)
+    imgs, base, resid = synthetic_pyramid(args.batch, args.res, seed=rank)
+    from appcorr_b200.policies.transmission.pyramid import pyr_up
+
+    approx_imgs = [pyr_up(b) for b in base]
+    task = Task(task_id=0, request_id=0, payload=[], instructions=[])
+
+    def step():
+        ctx = {}
+        ex.preprocess(approx_imgs, task, ctx, cfg)
+        ex.prepare_tokens(task, ctx, cfg)
+        ex.approx_forward({"layers": (0, L)}, ctx, cfg)
+        ex.preprocess(list(imgs), task, ctx, cfg)
+        ex.prepare_tokens(task, ctx, cfg)
+        ex.correct_forward({"layers": (0, L), "group_id": 1}, ctx, cfg)
+        ex.head_inference(task, ctx, cfg)
+        return ex.get_final_results(task, ctx, cfg)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    lat = []
+    t0.record()
+    for _ in range(args.steps):
+        s = time.perf_counter()
+        out = step()
+        lat.append((time.perf_counter() - s) * 1e3)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+    assert len(out) == args.batch
+    lat.sort()
+    return {"ms": ms, "p50": lat[len(lat) // 2], "p99": lat[min(len(lat) - 1, int(0.99 * len(lat)))]}, None
+
+
+def main():
+    args = parse_args()
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gpus != world_env and world_env == 1 and args.gpus > 1:
+        print(json.dumps({"error": "for --gpus > 1 launch with torch.distributed.run"}))
+        sys.exit(2)
+    rank, world, local = dist_setup(args.gpus)
+    parallelism = f"dp{world}" if world > 1 else "single"
+    cfg_out = {"model": "DINOv3 ViT-7B/16 + linear seg head (150 cls)" if args.arch == "vit7b16" else args.arch,
+               "global_batch": args.batch * world, "per_gpu_batch": args.batch, "seq_len": (args.res // 16) ** 2 + 5,
+               "image": f"{args.res}x{args.res}", "keep_ratio": args.keep, "pyramid_levels": [1, 0],
+               "parallelism": parallelism,
+               "l2": "working set > L2 each step (13.4 GB bf16 weights + 8 GB K/V/increment caches)"}
+    if args.impl == "reference":
+        try:
+            res, why = run_reference(args, rank, world)
+        except Exception as exc:  # report, do not crash the driver
+            res, why = None, f"{type(exc).__name__}: {exc}"[:300]
+        if rank == 0:
+            if res is None:
+                print(json.dumps({"impl": "reference", "unavailable": why}))
+            else:
+                v = args.batch * world * 1e3 / res["ms"]
+                print(json.dumps({"impl": "reference", "metric": BASELINE_METRIC, "value": round(v, 3),
+                                  "unit": "images/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                                  "ms_per_step": round(res["ms"], 3), "p50_ms": round(res["p50"], 3),
+                                  "p99_ms": round(res["p99"], 3), "higher_is_better": True,
+                                  "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                                  "data": "synthetic images, random-init weights", "config": cfg_out}))
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+    ms, per_step, launches, clk, e2e = run_mine(args, rank, world)
+    if rank == 0:
+        value = args.batch * world * 1e3 / ms
+        line = {"metric": BASELINE_METRIC, "value": round(value, 3), "unit": "images/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+                "p50_ms": round(per_step[len(per_step) // 2], 3),
+                "p99_ms": round(per_step[min(len(per_step) - 1, int(0.99 * len(per_step)))], 3),
+                "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
+                "dtype": "bf16", "data": "synthetic images (clipped N(128,60^2)), random-init weights",
+                "config": cfg_out, "gpu_launches": int(launches * args.steps), "clocks": clk, "e2e": e2e}
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,108 @@
+"""CPU fp32 oracle: the approximate / correct partial-token semantics of the DINOv3 block."""
+import pytest
+import torch
+
+from appcorr_b200.models.dinov3 import build_vit, create_group_index
+from appcorr_b200.models.dinov3.vit import ViTConfig, DinoVisionTransformer
+
+
+def _model(name="vits16", seed=0, **over):
+    m = build_vit(name, depth=3, **over).init_weights(seed).eval()
+    with torch.no_grad():
+        for blk in m.blocks:  # make the increments matter (the init LayerScale is 1e-5)
+            blk.ls1.gamma.fill_(0.5)
+            blk.ls2.gamma.fill_(0.5)
+    return m
+
+
+def _run_approx(m, img):
+    x, (H, W) = m.prepare_tokens_with_masks(img)
+    rope = m.rope_embed(H=H, W=W)
+    cache = {}
+    for i, blk in enumerate(m.blocks):
+        x, cache = blk.approx(x, rope, cache, f"layer{i}")
+    return x, rope, cache
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("name,over", [("vits16", {}), ("vit7b16", dict(embed_dim=256, num_heads=2))])
+def test_approx_equals_stock_forward(name, over):
+    m = _model(name, **over)
+    img = torch.rand(2, 3, 64, 64)
+    x, _, cache = _run_approx(m, img)
+    ref = m.forward_features(img)["x_prenorm"]
+    assert torch.allclose(x, ref, atol=1e-5, rtol=1e-5)
+    assert cache["layer0_k"].shape == (2, 21, m.num_heads, m.embed_dim // m.num_heads)
+
+
+@torch.no_grad()
+def test_full_correction_recovers_true_forward():
+    """approx(blurred) + correct(every token of the true image) == stock(true image)."""
+    m = _model()
+    true = torch.rand(2, 3, 64, 64)
+    blur = torch.nn.functional.avg_pool2d(true, 2).repeat_interleave(2, -1).repeat_interleave(2, -2)
+    _, rope, cache = _run_approx(m, blur)
+    x, _ = m.prepare_tokens_with_masks(true)
+    B, N = x.shape[:2]
+    dindice = torch.arange(N).repeat(B, 1)
+    opts = dict(token_keep_ratio=1.0, server_pscore="cls_attn_prob")
+    for i, blk in enumerate(m.blocks):
+        x, cache = blk.correct(x, dindice, rope, cache, f"layer{i}", **opts)
+    ref = m.forward_features(true)["x_prenorm"]
+    assert torch.allclose(x, ref, atol=1e-4, rtol=1e-4)
+
+
+@torch.no_grad()
+def test_partial_correction_only_touches_selected_rows():
+    m = _model()
+    img0 = torch.rand(1, 3, 64, 64)
+    _, rope, cache = _run_approx(m, img0)
+    x, _ = m.prepare_tokens_with_masks(torch.rand(1, 3, 64, 64))
+    N = x.shape[1]
+    dindice = torch.arange(N).repeat(1, 1)
+    blk = m.blocks[0]
+    bos0 = cache["layer0_bos"].clone()
+    out, cache = blk.correct(x, dindice, rope, cache, "layer0", token_keep_ratio=0.25, server_pscore="cls_attn_prob")
+    upd = cache["layer0_plan"].update_indice[0]
+    assert upd.shape[0] == 5 + 4  # prefix + int(16 * 0.25)
+    assert torch.all(upd[5:].diff() > 0)
+    keep = torch.zeros(N, dtype=torch.bool)
+    keep[upd] = True
+    # untouched rows are x + approx increment
+    assert torch.allclose(out[0, ~keep], x[0, ~keep] + bos0[0, ~keep], atol=1e-6)
+    # selected rows' increment was persisted
+    assert torch.allclose(cache["layer0_bos"][0, keep], out[0, keep] - x[0, keep], atol=1e-5)
+
+
+@torch.no_grad()
+def test_topk_selects_highest_scores():
+    m = _model()
+    _, rope, cache = _run_approx(m, torch.rand(2, 3, 64, 64))
+    x, _ = m.prepare_tokens_with_masks(torch.rand(2, 3, 64, 64))
+    dindice = torch.arange(21).repeat(2, 1)
+    plan = m.blocks[1].make_plan(cache, "layer1", dindice, 5, dict(token_keep_ratio=0.5, server_pscore="cls_attn_prob"))
+    s = cache["layer1_server_pscore"][:, 5:]
+    top = torch.topk(s, 8, dim=1).indices.sort(1).values + 5
+    assert torch.equal(plan.update_indice[:, 5:], top)
+
+
+def test_group_index_strategies():
+    g = create_group_index(16, 4, "grid", token_hw=(4, 4))
+    assert g.tolist() == [1, 2, 1, 2, 3, 4, 3, 4, 1, 2, 1, 2, 3, 4, 3, 4]
+    bg = create_group_index(16, 4, "block_grid", token_hw=(4, 4))
+    assert bg.tolist() == [1, 1, 2, 2, 1, 1, 2, 2, 3, 3, 4, 4, 3, 3, 4, 4]
+    e = create_group_index(64, 4, "expansion", token_hw=(8, 8))
+    assert sorted(torch.bincount(e)[1:].tolist()) == [16, 16, 16, 16]
+    assert e.view(8, 8)[3, 3] == 1 and e.view(8, 8)[0, 0] == 4
+
+
+def test_state_dict_keys_match_dinov3_layout():
+    m = build_vit("vit7b16", depth=1, embed_dim=256, num_heads=2)
+    keys = set(m.state_dict().keys())
+    for k in ["cls_token", "storage_tokens", "mask_token", "patch_embed.proj.weight", "rope_embed.periods",
+              "blocks.0.attn.qkv.weight", "blocks.0.ls1.gamma",
+              "blocks.0.mlp.w1.weight", "blocks.0.mlp.w3.bias", "norm.weight", "local_cls_norm.weight"]:
+        assert k in keys, k
+    small = build_vit("vits16", depth=1)
+    assert "blocks.0.attn.qkv.bias_mask" in small.state_dict()
+    assert "blocks.0.mlp.fc1.weight" in small.state_dict()
