@@ -59,7 +59,8 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
     """qkv projection with RoPE on q/k (tokens >= n_prefix) split into three BTHD buffers.
 
     q row m is written at q_out[m]; k/v rows at kv_rows[m] (or m). `rope` = (sin, cos) fp32
-    tables [n_patch_tokens, head_dim].
+    tables [n_patch_tokens, head_dim] whose second half repeats the first (the DINOv3 angle
+    layout); the kernel reads only the first half.
     """
     dim = w.shape[0] // 3
     if bn is None:

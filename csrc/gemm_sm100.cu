@@ -188,16 +188,23 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
           add_bias(lo, ep.bias, n0 + hb + c);
           add_bias(hi, ep.bias, n0 + hb + half + c);
           if (rope) {
-            const float* sn = ep.rope_sin + (long)rrow * Dh;
-            const float* cs = ep.rope_cos + (long)rrow * Dh;
+            // DINOv3 RoPE tables repeat their first half (angles tiled twice), so the pair
+            // (d, d + half) shares one sin / cos value; read them as float4 vectors.
+            const float4* sn = reinterpret_cast<const float4*>(ep.rope_sin + (long)rrow * Dh + c);
+            const float4* cs = reinterpret_cast<const float4*>(ep.rope_cos + (long)rrow * Dh + c);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float xl = bf16_round(lo[j]);
-              const float xh = bf16_round(hi[j]);
-              const float sl = __ldg(sn + c + j), cl = __ldg(cs + c + j);
-              const float sh = __ldg(sn + half + c + j), ch = __ldg(cs + half + c + j);
-              lo[j] = xl * cl - xh * sl;
-              hi[j] = xh * ch + xl * sh;
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 s4 = __ldg(sn + j4), c4 = __ldg(cs + j4);
+              const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+              const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = 4 * j4 + e;
+                const float xl = bf16_round(lo[j]);
+                const float xh = bf16_round(hi[j]);
+                lo[j] = xl * cv[e] - xh * sv[e];
+                hi[j] = xh * cv[e] + xl * sv[e];
+              }
             }
           }
           store_bf16x32(dst + c0 + hb + c, lo);

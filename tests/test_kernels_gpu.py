@@ -139,8 +139,9 @@ def test_qkv_rope_scatter(Dh, H):
     a = _rand(M, K)
     w = _rand(3 * D, K, scale=K ** -0.5)
     bias = _rand(3 * D, scale=0.1)
-    sin = torch.randn(N - npre, Dh, device=DEV)
-    cos = torch.randn(N - npre, Dh, device=DEV)
+    # RoPE tables repeat their first half (angles tiled twice), as RopePositionEmbedding builds them
+    sin = torch.randn(N - npre, Dh // 2, device=DEV).repeat(1, 2).contiguous()
+    cos = torch.randn(N - npre, Dh // 2, device=DEV).repeat(1, 2).contiguous()
     q = torch.zeros(M, D, device=DEV, dtype=torch.bfloat16)
     k = torch.zeros(M, D, device=DEV, dtype=torch.bfloat16)
     v = torch.zeros(M, D, device=DEV, dtype=torch.bfloat16)
