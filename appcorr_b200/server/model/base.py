@@ -19,14 +19,26 @@ import torch
 class PyramidBatch:
     """Decoded-but-not-reconstructed Laplacian input of a batch.
 
-    base: uint8 [B, h, w, 3] coarsest level; residual: int16 [B, 2h, 2w, 3] (zeros where a patch
-    has not arrived) or None for the base-only approximation. The server reconstructs
-    clip(pyrUp(base) + residual) on the GPU (kernel `pyrup_add`).
+    base: uint8 [B, h, w, 3] coarsest level. residual: one int16 canvas [B, 2h, 2w, 3] (zeros
+    where a patch has not arrived), a list of them from coarse to fine (None entries for levels
+    with nothing received), or None for the base-only approximation. `levels` (coarse first)
+    fixes how many 2x steps reach full resolution; without it, one step per residual. The server
+    reconstructs clip(pyrUp(cur) + residual) level by level on the GPU (kernel `pyrup_add`).
     """
 
     base: Any
     residual: Any = None
     target_shapes: Optional[list] = None
+    levels: Optional[list] = None
+
+    def residual_steps(self) -> list:
+        res = self.residual
+        if res is None:
+            res = []
+        elif not isinstance(res, (list, tuple)):
+            res = [res]
+        n = self.levels[0] if self.levels else max(len(res), 1)  # always finish at level 0
+        return [res[i] if i < len(res) else None for i in range(n)]
 
 
 def resolve_device(device) -> torch.device:

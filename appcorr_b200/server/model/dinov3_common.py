@@ -78,27 +78,31 @@ class DINOv3BackboneMixin:
         """LOAD_INPUT: decoded images or a Laplacian PyramidBatch -> uint8 [B, H, W, 3] canvas."""
         dev = self.device
         if isinstance(batch_data, PyramidBatch):
-            base = to_device_uint8_images(batch_data.base, dev)
-            B, h, w, _ = base.shape
-            canvas = context.get("canvas")
-            if canvas is None or tuple(canvas.shape) != (B, 2 * h, 2 * w, 3):
-                canvas = torch.empty(B, 2 * h, 2 * w, 3, dtype=torch.uint8, device=dev)
-            res = None
-            if batch_data.residual is not None:
-                r = batch_data.residual
-                r = torch.from_numpy(np.ascontiguousarray(r)) if isinstance(r, np.ndarray) else r
-                if dev.type == "cuda" and not r.is_cuda and not r.is_pinned():
-                    r = r.pin_memory()
-                res = r.to(dev, non_blocking=True)
-            if dev.type == "cuda":
-                K.pyrup_add(base, res, canvas)
-            else:
-                from ...policies.transmission.pyramid import pyr_up
+            cur = to_device_uint8_images(batch_data.base, dev)
+            steps = batch_data.residual_steps()
+            for i, r in enumerate(steps):
+                B, h, w, _ = cur.shape
+                if r is not None:
+                    r = torch.from_numpy(np.ascontiguousarray(r)) if isinstance(r, np.ndarray) else r
+                    if dev.type == "cuda" and not r.is_cuda and not r.is_pinned():
+                        r = r.pin_memory()
+                    r = r.to(dev, non_blocking=True)
+                if dev.type == "cuda":
+                    key = f"canvas_l{len(steps) - 1 - i}"
+                    nxt = context.get(key)
+                    if nxt is None or tuple(nxt.shape) != (B, 2 * h, 2 * w, 3):
+                        nxt = torch.empty(B, 2 * h, 2 * w, 3, dtype=torch.uint8, device=dev)
+                        context[key] = nxt
+                    K.pyrup_add(cur, r, nxt)
+                else:
+                    from ...policies.transmission.pyramid import pyr_up
 
-                up = np.stack([pyr_up(b) for b in base.numpy()]).astype(np.int32)
-                if res is not None:
-                    up = up + res.numpy().astype(np.int32)
-                canvas = torch.from_numpy(np.clip(up, 0, 255).astype(np.uint8))
+                    up = np.stack([pyr_up(b) for b in cur.numpy()]).astype(np.int32)
+                    if r is not None:
+                        up = up + r.numpy().astype(np.int32)
+                    nxt = torch.from_numpy(np.clip(up, 0, 255).astype(np.uint8))
+                cur = nxt
+            canvas = cur
             context["target_shapes"] = batch_data.target_shapes
         else:
             canvas = to_device_uint8_images(batch_data, dev)
