@@ -37,8 +37,12 @@ class PyramidBatch:
             res = []
         elif not isinstance(res, (list, tuple)):
             res = [res]
-        n = self.levels[0] if self.levels else max(len(res), 1)  # always finish at level 0
-        return [res[i] if i < len(res) else None for i in range(n)]
+        if self.levels:
+            # one 2x step per level from the base down to level 0; a residual joins the step that
+            # lands on its level (residual[i] belongs to levels[i + 1])
+            by_level = {lvl: (res[i] if i < len(res) else None) for i, lvl in enumerate(self.levels[1:])}
+            return [by_level.get(t) for t in range(self.levels[0] - 1, -1, -1)]
+        return [res[i] if i < len(res) else None for i in range(max(len(res), 1))]
 
 
 def resolve_device(device) -> torch.device:
