@@ -282,8 +282,6 @@ class ExperimentConfig:
         name = self.input_profile_name or "fixed_image_shape"
         if name not in _INPUT_PROFILES:
             raise ValueError(f"Unknown input_profile_name: {name}")
-        if name == "fixed_image_shape":
-            return {"name": name}
         opts = {"name": name, **_INPUT_PROFILES[name]}
         opts.update(self.input_profile_kwargs)
         return opts

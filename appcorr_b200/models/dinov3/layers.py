@@ -433,10 +433,11 @@ class SelfAttentionBlock(nn.Module):
         )
 
     def correct(self, x: Tensor, dindice: Tensor, rope, cache: Dict, tag: str, *,
-                plan: Optional[PartialTokenPlan] = None, mobile_pscore_hint: Optional[Tensor] = None,
+                query_plan: Optional[PartialTokenPlan] = None, mobile_pscore_hint: Optional[Tensor] = None,
                 candidate_valid_mask: Optional[Tensor] = None, **opts) -> Tuple[Tensor, Dict]:
         B, N, C = x.shape
         n_prefix = int(opts.get("num_pretokens", N - rope[0].shape[0] if rope is not None else 0))
+        plan = query_plan
         if plan is None:
             plan = self.make_plan(cache, tag, dindice, n_prefix, opts, mobile_pscore_hint, candidate_valid_mask)
         upd = plan.update_indice                      # [B, T]

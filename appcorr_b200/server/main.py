@@ -1,0 +1,66 @@
+"""Server entry point: `python -m appcorr_b200.server.main` (or `python -m offload.server.main`).
+
+Starts four processes connected by queues (reference offload/server/main.py:13-119):
+receiver -> scheduler -> worker -> sender, with a feedback queue from the worker's reaper to the
+scheduler. `--device cuda:N` pins the worker to one GPU (one server per GPU for data-parallel
+serving); `--tp` > 1 launches tensor-parallel worker ranks (see appcorr_b200.parallel).
+"""
+from __future__ import annotations
+
+import argparse
+import multiprocessing
+import time
+
+
+def run_server(recv_port: int, send_port: int, reverse_connect: bool = False, mobile_ip: str = "127.0.0.1",
+               listen_host: str = "0.0.0.0", device: str | None = None, stop_event=None) -> None:
+    from .modules import ServerReceiver, ServerSender
+    from .scheduler import SchedulerModule
+    from .worker import WorkerModule
+
+    ctx = multiprocessing.get_context("spawn")
+    print("=== appcorr_b200 server ===", flush=True)
+    sched_q, worker_q, result_q, control_q, feedback_q = (ctx.Queue() for _ in range(5))
+    shutdown = ctx.Event()
+    host = mobile_ip if reverse_connect else None
+    procs = [ServerReceiver(recv_port, sched_q, control_q, shutdown, listen_host=listen_host, connect_host=host),
+             SchedulerModule(sched_q, worker_q, control_q, feedback_q),
+             WorkerModule(worker_q, result_q, feedback_q, device=device),
+             ServerSender(send_port, result_q, listen_host=listen_host, connect_host=host)]
+    try:
+        for p in procs:
+            p.start()
+        while not shutdown.is_set() and not (stop_event is not None and stop_event.is_set()):
+            time.sleep(0.2)
+    except KeyboardInterrupt:
+        print("[Main] interrupted", flush=True)
+    finally:
+        for q, item in ((control_q, ("STOP", None)), (worker_q, "STOP"), (result_q, "STOP")):
+            try:
+                q.put(item)
+            except Exception:
+                pass
+        for p in procs:
+            p.join(timeout=10)
+        for p in procs:
+            if p.is_alive():
+                p.terminate()
+                p.join()
+        print("server stopped", flush=True)
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description="appcorr_b200 server")
+    ap.add_argument("--recv-port", type=int, default=39990)
+    ap.add_argument("--send-port", type=int, default=39991)
+    ap.add_argument("--listen-host", type=str, default="0.0.0.0")
+    ap.add_argument("-rc", "--reverse-connect", action="store_true")
+    ap.add_argument("--mobile-ip", type=str, default="127.0.0.1")
+    ap.add_argument("--device", type=str, default=None)
+    a = ap.parse_args(argv)
+    run_server(a.recv_port, a.send_port, reverse_connect=a.reverse_connect, mobile_ip=a.mobile_ip,
+               listen_host=a.listen_host, device=a.device)
+
+
+if __name__ == "__main__":
+    main()

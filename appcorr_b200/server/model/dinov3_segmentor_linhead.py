@@ -92,7 +92,7 @@ class DINOv3SegmentorLinheadExecutor(DINOv3BackboneMixin, ModelExecutor):
         host = labels.cpu().numpy()
         idx = context.get("active_indices")
         order = list(range(host.shape[0])) if idx is None else [int(i) for i in idx]
-        return {orig: {"mask": np.ascontiguousarray(host[i])} for i, orig in enumerate(order)}
+        return {orig: {"mask": np.ascontiguousarray(host[orig])} for orig in order if orig < host.shape[0]}
 
     def cache_stats(self, context):
         return self.backbone_cache_stats(context)

@@ -97,7 +97,7 @@ def test_engine_correct_matches_oracle(name, over):
         plan = PartialTokenPlan(upd, torch.zeros(1), *(torch.zeros(()) for _ in range(5)))
         dind = torch.arange(N, device=DEV).repeat(B, 1)
         for i, blk in enumerate(m.blocks):
-            xr, cache = blk.correct(xr, dind, rope, cache, f"layer{i}", plan=plan, **opts)
+            xr, cache = blk.correct(xr, dind, rope, cache, f"layer{i}", query_plan=plan, **opts)
     assert _rel(x.view(B, -1, m.embed_dim), xr) < 3e-2
     for i in range(len(m.blocks)):
         assert _rel(sess.bos[i].view(B, -1, m.embed_dim), cache[f"layer{i}_bos"]) < 4e-2
