@@ -27,6 +27,15 @@ def run_server(recv_port: int, send_port: int, reverse_connect: bool = False, mo
              SchedulerModule(sched_q, worker_q, control_q, feedback_q),
              WorkerModule(worker_q, result_q, feedback_q, device=device),
              ServerSender(send_port, result_q, listen_host=listen_host, connect_host=host)]
+    import signal
+
+    def _term(signum, frame):  # SIGTERM: run the orderly shutdown below so no child is orphaned
+        raise KeyboardInterrupt
+
+    try:
+        signal.signal(signal.SIGTERM, _term)
+    except ValueError:  # not the main thread
+        pass
     try:
         for p in procs:
             p.start()

@@ -180,8 +180,10 @@ class WorkerModule(multiprocessing.Process):
                     if payload.device:
                         self.device = torch.device(payload.device)
                     self.sessions = {}
-                    self.load_model()
-                    self._config_ready.set()
+                    try:
+                        self.load_model()
+                    finally:
+                        self._config_ready.set()  # never leave the decoder waiting on a failed load
                     print(f"[Worker] configured: {payload.model_name} on {self.device}", flush=True)
                 elif kind == "TIME_SYNC":
                     self.output_queue.put(time.time())
@@ -222,6 +224,10 @@ class WorkerModule(multiprocessing.Process):
             print(f"!!! [Worker] pipeline error (req {task.request_id}): {exc}", flush=True)
             traceback.print_exc()
             self.sessions.pop(task.request_id, None)
+            # answer the client instead of leaving it to its result timeout
+            self.output_queue.put(InferenceResult(task.task_id, time.time(), [{"error": str(exc)}] * self.config.batch_size,
+                                                  [{"type": "ERROR", "start": time.time(), "end": time.time(),
+                                                    "params": {"message": str(exc)}}]))
 
     def dispatch(self, ins: Instruction, task: Task, ctx: Dict[str, Any]):
         ex, cfg, op = self.executor, self.config, ins.op_type
