@@ -1,0 +1,105 @@
+"""Symmetric device buffers and peer-memory collectives for one-process-per-GPU tensor parallelism.
+
+`TPComm` owns, per rank, buffers allocated with cudaMalloc and exported through CUDA IPC; every
+rank maps every peer's buffer, so the kernels in csrc/comm.cu can load from and store to other
+GPUs over NVLink / NVSwitch. torch.distributed (any backend) is used only to exchange the IPC
+handles at set-up. Device-side waits are bounded; `check()` raises if one expired.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..ops.native import check_errors, err_word, lib
+
+MAX_RANKS = 8
+
+
+@dataclass
+class SymTensor:
+    """A symmetric buffer: the local tensor and every rank's base pointer (index = rank)."""
+
+    local: torch.Tensor
+    ptrs: List[int]
+
+    def view_ptrs(self, offset_elems: int) -> List[int]:
+        es = self.local.element_size()
+        return [p + offset_elems * es for p in self.ptrs]
+
+
+class TPComm:
+    def __init__(self, group: Optional["dist.ProcessGroup"] = None, device: Optional[torch.device] = None):
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if self.world > MAX_RANKS:
+            raise ValueError(f"peer-memory TP supports at most {MAX_RANKS} ranks")
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self._owned: List[int] = []
+        self._opened: List[int] = []
+        self.epoch = 0
+        self.flags = self.empty((MAX_RANKS,), torch.int32)
+        self.err = err_word(self.device)
+
+    # ------------------------------------------------------------------ buffers
+    def empty(self, shape: Sequence[int], dtype: torch.dtype) -> SymTensor:
+        n = 1
+        for s in shape:
+            n *= int(s)
+        nbytes = max(n * torch.empty((), dtype=dtype).element_size(), 16)
+        nbytes = (nbytes + 255) // 256 * 256
+        with torch.cuda.device(self.device):
+            ptr, handle = lib().ipc_alloc(nbytes)
+        self._owned.append(ptr)
+        handles: List[bytes] = [None] * self.world  # type: ignore
+        if self.world > 1:
+            dist.all_gather_object(handles, handle, group=self.group)
+        else:
+            handles = [handle]
+        ptrs = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(ptr)
+                else:
+                    p = lib().ipc_open(h)
+                    self._opened.append(p)
+                    ptrs.append(p)
+        t = lib().tensor_from_ptr(ptr, [int(s) for s in shape], dtype, self.device.index)
+        return SymTensor(t, ptrs)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                lib().ipc_close(p)
+            for p in self._owned:
+                lib().ipc_free(p)
+        self._opened, self._owned = [], []
+
+    # ------------------------------------------------------------------ collectives
+    def barrier(self) -> None:
+        """Device-side barrier across the group on the current stream (bounded wait)."""
+        if self.world == 1:
+            return
+        self.epoch = (self.epoch + 1) & 0x7FFFFFFF
+        lib().tp_barrier(self.flags.ptrs, self.rank, self.epoch, self.err)
+
+    def allreduce_epilogue(self, part: SymTensor, out: SymTensor, M: int, N: int, *, out_rows=None,
+                           out_offset: int = 0, aux: Optional[SymTensor] = None, aux_offset: int = 0, aux_rows=None,
+                           aux_mode: int = 0, bias=None, gamma=None, resid=None, resid_rows=None, resid2=None) -> None:
+        """Sum of every rank's `part[:M, :N]`, fused with the residual / LayerScale epilogue,
+        stored into every rank's `out` (and `aux`). Caller brackets it with barriers."""
+        lib().tp_allreduce_epi(part.ptrs, part.local.stride(0), out.view_ptrs(out_offset), out.local.stride(-2),
+                               out_rows, aux.view_ptrs(aux_offset) if aux is not None else [],
+                               aux.local.stride(-2) if aux is not None else 0, aux_rows, aux_mode, bias, gamma, resid,
+                               resid_rows, resid2, M, N, self.rank)
+
+    def mean_f32(self, src: SymTensor, dst: torch.Tensor) -> None:
+        lib().tp_mean_f32(src.ptrs, dst)
+
+    def check(self) -> None:
+        check_errors(self.device)

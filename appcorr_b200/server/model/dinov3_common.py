@@ -53,7 +53,25 @@ class DINOv3BackboneMixin:
         seed = int(profile.get("seed", 0))
         self._sessions.clear()
         self._group_cache.clear()
-        if self.device.type == "cuda":
+        tp = int(getattr(config, "tp_size", 1) or 1)
+        if self.device.type == "cuda" and tp > 1:
+            import torch.distributed as dist
+
+            from ...models.engine import weights_from_module
+            from ...parallel.comm import TPComm
+            from ...parallel.tp import ViTEngineTP
+
+            if not dist.is_initialized() or dist.get_world_size() != tp:
+                raise RuntimeError(f"tp_size={tp} needs a torch.distributed group of {tp} ranks, one per GPU")
+            self.comm = TPComm(device=self.device)
+            if path is not None:
+                m = build_vit(self.arch)
+                m.load_state_dict(torch.load(path, map_location="cpu", mmap=True, weights_only=True), strict=True)
+                self.engine = ViTEngineTP.from_full(weights_from_module(m.eval(), self.device), self.comm)
+            else:
+                self.engine = ViTEngineTP.random_tp(PRESETS[self.arch], self.comm, seed=seed)
+            self.cfg = self.engine.cfg
+        elif self.device.type == "cuda":
             from ...models.engine import ViTEngine
 
             if path is not None:

@@ -53,6 +53,8 @@ def parse_args():
     ap.add_argument("--arch", default="vit7b16")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
+                    help="N > 1: tensor-parallel over N GPUs (one request batch) or N data-parallel replicas")
     return ap.parse_args()
 
 
@@ -160,11 +162,13 @@ def max_over_ranks(v: float, world: int) -> float:
 
 
 # ----------------------------------------------------------------------------- our implementation
-def make_config(args):
+def make_config(args, world: int = 1):
     sys.path.insert(0, ROOT)
     from appcorr_b200.common.protocol import ExperimentConfig
 
+    tp = world if (world > 1 and args.parallel == "tp") else 1
     return ExperimentConfig(
+        tp_size=tp,
         exp_id="bench", model_name="dinov3_segmentor_linhead", batch_size=args.batch,
         image_shape=(args.res, args.res, 3), input_profile_name="dinov3_ade20k_linhead_official",
         input_profile_kwargs={"backbone_arch": args.arch, "server_inference_mode": "whole"},
@@ -183,11 +187,13 @@ def run_mine(args, rank, world):
     from appcorr_b200.server.model import PyramidBatch, get_model_executor
 
     dev = torch.device("cuda", torch.cuda.current_device())
-    cfg = make_config(args)
+    cfg = make_config(args, world)
+    tp = cfg.tp_size > 1
     ex = get_model_executor(cfg.model_name, dev)
     ex.load_model(cfg.model_name, cfg)
     L = ex.cfg.depth
-    imgs, base, resid = synthetic_pyramid(args.batch, args.res, seed=rank)
+    # tensor parallel: every rank serves the same request; data parallel: independent requests
+    imgs, base, resid = synthetic_pyramid(args.batch, args.res, seed=0 if tp else rank)
     base_h = torch.from_numpy(base).pin_memory()
     res_h = torch.from_numpy(resid).pin_memory()
     task = Task(task_id=0, request_id=0, payload=[], instructions=[])
@@ -272,7 +278,7 @@ def run_mine(args, rank, world):
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / n_e2e, world)
         assert len(out) == args.batch and out[0]["mask"].shape == (args.res, args.res)
         lat.sort()
-        e2e = {"value": round(args.batch * world * 1e3 / e2e_ms, 3), "unit": "images/s",
+        e2e = {"value": round(args.batch * (1 if tp else world) * 1e3 / e2e_ms, 3), "unit": "images/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "p50_ms": round(lat[len(lat) // 2], 3), "p99_ms": round(lat[min(len(lat) - 1, int(0.99 * len(lat)))], 3),
                "ms_per_step": round(e2e_ms, 3)}
@@ -391,9 +397,10 @@ def main():
         print(json.dumps({"error": "for --gpus > 1 launch with torch.distributed.run"}))
         sys.exit(2)
     rank, world, local = dist_setup(args.gpus)
-    parallelism = f"dp{world}" if world > 1 else "single"
+    parallelism = (f"{args.parallel}{world}" if world > 1 else "single")
+    images_per_step = args.batch * (world if (world > 1 and args.parallel == "dp") else 1)
     cfg_out = {"model": "DINOv3 ViT-7B/16 + linear seg head (150 cls)" if args.arch == "vit7b16" else args.arch,
-               "global_batch": args.batch * world, "per_gpu_batch": args.batch, "seq_len": (args.res // 16) ** 2 + 5,
+               "global_batch": images_per_step, "per_gpu_batch": args.batch, "seq_len": (args.res // 16) ** 2 + 5,
                "image": f"{args.res}x{args.res}", "keep_ratio": args.keep, "pyramid_levels": [1, 0],
                "parallelism": parallelism,
                "l2": "working set > L2 each step (13.4 GB bf16 weights + 8 GB K/V/increment caches)"}
@@ -420,12 +427,12 @@ def main():
         return
     ms, per_step, launches, clk, e2e = run_mine(args, rank, world)
     if rank == 0:
-        value = args.batch * world * 1e3 / ms
+        value = images_per_step * 1e3 / ms
         line = {"metric": BASELINE_METRIC, "value": round(value, 3), "unit": "images/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
                 "p50_ms": round(per_step[len(per_step) // 2], 3),
                 "p99_ms": round(per_step[min(len(per_step) - 1, int(0.99 * len(per_step)))], 3),
-                "higher_is_better": True, "scaling": "weak",
+                "higher_is_better": True, "scaling": "strong" if parallelism.startswith("tp") else "weak",
                 "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
                 "dtype": "bf16", "data": "synthetic images (clipped N(128,60^2)), random-init weights",
                 "config": cfg_out, "gpu_launches": int(launches * args.steps), "clocks": clk, "e2e": e2e}

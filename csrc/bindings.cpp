@@ -79,9 +79,10 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
     TORCH_CHECK(q_out && k_out && v_out, "qkv epilogue needs q_out, k_out, v_out");
     TORCH_CHECK(N % 3 == 0, "qkv weight rows must be 3*dim");
     ep.dim = N / 3;
-    TORCH_CHECK(ep.dim % bn == 0, "qkv: dim must be a multiple of BN");
+    const int tile_n = bn == 512 ? 256 : static_cast<int>(bn);  // bn 512 = 2-CTA 256x256 tile
+    TORCH_CHECK(ep.dim % tile_n == 0, "qkv: dim must be a multiple of the tile width");
     TORCH_CHECK(head_dim == 64 || head_dim == 128, "qkv: head_dim must be 64 or 128");
-    TORCH_CHECK(bn % head_dim == 0, "qkv: BN must be a multiple of head_dim");
+    TORCH_CHECK(tile_n % head_dim == 0, "qkv: tile width must be a multiple of head_dim");
     TORCH_CHECK(tok_idx.has_value() || seq_len > 0, "qkv: need tok_idx or seq_len");
   } else {
     TORCH_CHECK(out.has_value(), "gemm: out is required");
@@ -125,4 +126,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("AUX_OUT_MINUS") = static_cast<int>(AUX_OUT_MINUS);
   register_elementwise_ops(m);
   register_attention_ops(m);
+  register_comm_ops(m);
 }

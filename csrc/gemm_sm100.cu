@@ -403,6 +403,154 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------ 2-CTA variant
+// Same structure, but a cluster of two CTAs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA stages its own 128 rows of A and 128 of the 256 B
+// rows, so per-SM shared-memory traffic per MMA is halved. The even CTA issues all MMAs; both CTAs
+// hold 128 accumulator rows in their TMEM and run their own epilogue. The odd CTA's TMA loads
+// complete on the even CTA's `full` barrier; MMA completion is committed separately to each CTA's
+// `empty` / `tfull` barrier; epilogue threads of both CTAs arrive on the even CTA's `tempty`.
+template <int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tn_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            GemmShape shp, GemmEpilogue ep) {
+  constexpr int BN = 256;                       // output tile width (both CTAs)
+  constexpr int BH = BN / 2;                    // B rows staged per CTA
+  constexpr uint32_t A_BYTES = kBM * kBK * 2;
+  constexpr uint32_t B_BYTES = BH * kBK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t IDESC = idesc_bf16_f32(2 * kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_addr(&tfull[a]), 1);
+      mbar_init(smem_addr(&tempty[a]), 256);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_addr(tmem_slot), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (shp.M + 2 * kBM - 1) / (2 * kBM);
+  const int num_n = (shp.N + BN - 1) / BN;
+  const int KB = (shp.K + kBK - 1) / kBK;
+  const int total = num_m * num_n;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = cluster_id; tile < total; tile += num_clusters) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) goto producer_done;
+          const uint32_t fb = mapa_shared(smem_addr(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx_cluster(fb, 2 * STAGE_BYTES);
+          const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
+          tma_load_2d_pair(sa, &tmA, fb, kb * kBK, mb * 2 * kBM + rank * kBM);
+          tma_load_2d_pair(sa + A_BYTES, &tmB, fb, kb * kBK, nb * BN + rank * BH);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+      }
+      for (int i = 0; i < STAGES; ++i) {
+        if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) break;
+        if (++s == STAGES) { s = 0; ph ^= 1; }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int t_local = 0;
+      for (int tile = cluster_id; tile < total; tile += num_clusters, ++t_local) {
+        const int acc = t_local & 1;
+        const uint32_t acc_ph = (t_local >> 1) & 1;
+        if (!mbar_wait(smem_addr(&tempty[acc]), acc_ph ^ 1, shp.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16_pair(d_tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
+                          (kb | k) != 0 ? 1u : 0u);
+#ifdef APPCORR_PAIR_COMMIT_SPLIT
+          umma_commit_pair(mapa_shared(smem_addr(&empty[s]), 0));
+          umma_commit_pair(mapa_shared(smem_addr(&empty[s]), 1));
+#else
+          umma_commit_pair_mask(smem_addr(&empty[s]), 0x3);
+#endif
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+#ifdef APPCORR_PAIR_COMMIT_SPLIT
+        umma_commit_pair(mapa_shared(smem_addr(&tfull[acc]), 0));
+        umma_commit_pair(mapa_shared(smem_addr(&tfull[acc]), 1));
+#else
+        umma_commit_pair_mask(smem_addr(&tfull[acc]), 0x3);
+#endif
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int t_local = 0;
+    for (int tile = cluster_id; tile < total; tile += num_clusters, ++t_local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int acc = t_local & 1;
+      const uint32_t acc_ph = (t_local >> 1) & 1;
+      if (!mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      run_epilogue<BN, EPI>(taddr, mb * 2 * kBM + rank * kBM + row_in_tile, nb * BN, shp, ep);
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(smem_addr(&tempty[acc]), 0));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------------------------ host side
 namespace {
 
@@ -470,13 +618,46 @@ void launch_gemm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+template <int STAGES, int EPI>
+void launch_gemm_2sm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const GemmEpilogue& ep,
+                     int* err, int max_ctas, cudaStream_t stream) {
+  constexpr uint32_t STAGE_BYTES = (kBM + 128) * kBK * 2;
+  constexpr size_t SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  auto kern = gemm_bf16_tn_2sm_kernel<STAGES, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM));
+    configured = true;
+  }
+  CUtensorMap ta = make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), kBM, kBK);
+  CUtensorMap tb = make_tmap_bf16_2d(B.data_ptr(), B.size(0), K, B.stride(0), 128, kBK);
+  GemmShape shp{M, N, K, err};
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + 255) / 256);
+  int clusters = std::min(tiles, (max_ctas > 0 ? max_ctas : num_sms()) / 2);
+  if (clusters <= 0) return;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, shp, ep));
+}
+
 // Dispatch on (epilogue, BN). STAGES chosen to fill ~192 KB of shared memory.
 void gemm_dispatch(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
                    const GemmEpilogue& ep, int* err, int max_ctas) {
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
 #define APPCORR_GEMM_CASE(E)                                                              \
   case E:                                                                                 \
-    if (bn == 256) launch_gemm<256, 4, E>(A, B, M, N, K, ep, err, max_ctas, st);          \
+    if (bn == 512) launch_gemm_2sm<6, E>(A, B, M, N, K, ep, err, max_ctas, st);           \
+    else if (bn == 256) launch_gemm<256, 4, E>(A, B, M, N, K, ep, err, max_ctas, st);     \
     else if (bn == 128) launch_gemm<128, 6, E>(A, B, M, N, K, ep, err, max_ctas, st);     \
     else if (bn == 64) launch_gemm<64, 8, E>(A, B, M, N, K, ep, err, max_ctas, st);       \
     else TORCH_CHECK(false, "unsupported BN ", bn);                                       \
@@ -487,11 +668,13 @@ void gemm_dispatch(int epi, int bn, const at::Tensor& A, const at::Tensor& B, in
     APPCORR_GEMM_CASE(EPI_GELU)
     APPCORR_GEMM_CASE(EPI_RESID)
     case EPI_SWIGLU:
-      TORCH_CHECK(bn == 256, "swiglu epilogue uses BN=256");
-      launch_gemm<256, 4, EPI_SWIGLU>(A, B, M, N, K, ep, err, max_ctas, st);
+      TORCH_CHECK(bn == 256 || bn == 512, "swiglu epilogue uses BN=256 (512: 2-CTA)");
+      if (bn == 512) launch_gemm_2sm<6, EPI_SWIGLU>(A, B, M, N, K, ep, err, max_ctas, st);
+      else launch_gemm<256, 4, EPI_SWIGLU>(A, B, M, N, K, ep, err, max_ctas, st);
       break;
     case EPI_QKV:
-      if (bn == 256) launch_gemm<256, 4, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
+      if (bn == 512) launch_gemm_2sm<6, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
+      else if (bn == 256) launch_gemm<256, 4, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
       else if (bn == 128) launch_gemm<128, 6, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
       else TORCH_CHECK(false, "qkv epilogue uses BN=128 or 256");
       break;

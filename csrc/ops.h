@@ -52,5 +52,6 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, int64_t rows, int64_t cols, int64
 int num_sms();
 void register_elementwise_ops(pybind11::module_& m);
 void register_attention_ops(pybind11::module_& m);
+void register_comm_ops(pybind11::module_& m);
 
 }  // namespace appcorr

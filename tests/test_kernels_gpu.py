@@ -269,3 +269,54 @@ def test_patch_im2col():
     cols = torch.nn.functional.unfold(x, 16, stride=16)  # B, C*256, L
     ref = cols.transpose(1, 2).reshape(-1, 768)
     _close(out, ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (300, 512, 1024), (1029, 1024, 4096), (2496, 768, 256), (255, 256, 128)])
+def test_gemm_2cta_bias(M, N, K):
+    """bn=512 selects the cluster-of-two (cta_group::2, 256x256 tile) kernel."""
+    K_ = _k()
+    torch.manual_seed(10)
+    a = _rand(M, K)
+    w = _rand(N, K, scale=K ** -0.5)
+    bias = _rand(N, scale=0.1)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K_.gemm(a, w, out, bias=bias, bn=512)
+    _close(out, a.float() @ w.float().T + bias.float())
+
+
+def test_gemm_2cta_epilogues():
+    K_ = _k()
+    from appcorr_b200.models.weights import pack_swiglu
+
+    torch.manual_seed(11)
+    M, Hd, K = 333, 512, 256
+    a = _rand(M, K)
+    w1, w2 = _rand(Hd, K, scale=K ** -0.5), _rand(Hd, K, scale=K ** -0.5)
+    b1, b2 = _rand(Hd, scale=0.1), _rand(Hd, scale=0.1)
+    wp, bp = pack_swiglu(w1, w2, b1, b2)
+    out = torch.empty(M, Hd, device=DEV, dtype=torch.bfloat16)
+    K_.gemm(a, wp, out, epi=K_.EPI_SWIGLU, bias=bp, bn=512)
+    ref = torch.nn.functional.silu(a.float() @ w1.float().T + b1.float()) * (a.float() @ w2.float().T + b2.float())
+    _close(out, ref, rtol=3e-2, atol=3e-2)
+    N = 512
+    w = _rand(N, K, scale=K ** -0.5)
+    gamma, resid = _rand(N, scale=0.5), _rand(M, N)
+    aux = _rand(M, N)
+    aux0 = aux.clone()
+    out2 = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K_.gemm(a, w, out2, epi=K_.EPI_RESID, gamma=gamma, resid=resid, aux=aux, aux_mode=K_.AUX_ADD, bn=512)
+    delta = (a.float() @ w.float().T) * gamma.float()
+    _close(out2, resid.float() + delta)
+    _close(aux, aux0.float() + delta)
+    # qkv with RoPE on the 2-CTA path equals the 1-CTA path
+    H, Dh, B, Nt, npre = 4, 128, 2, 37, 5
+    D = H * Dh
+    a3 = _rand(B * Nt, K)
+    w3 = _rand(3 * D, K, scale=K ** -0.5)
+    sin = torch.randn(Nt - npre, Dh // 2, device=DEV).repeat(1, 2).contiguous()
+    cos = torch.randn(Nt - npre, Dh // 2, device=DEV).repeat(1, 2).contiguous()
+    bufs = [[torch.zeros(B * Nt, D, device=DEV, dtype=torch.bfloat16) for _ in range(3)] for _ in range(2)]
+    for bn, (q, k, v) in zip((256, 512), bufs):
+        K_.qkv_gemm(a3, w3, None, q, k, v, head_dim=Dh, seq_len=Nt, rope=(sin, cos), n_prefix=npre, bn=bn)
+    for x, y in zip(*bufs):
+        _close(x, y, rtol=1e-2, atol=1e-2)
