@@ -86,14 +86,21 @@ def add_(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     return x
 
 
+ATTENTION_IMPL = ["tcgen05"]  # "tcgen05" (sm_100a tensor cores + TMEM) or "mma" (mma.sync kernel)
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, *, B: int, Tq: int,
               Tk: int, H: int, Dh: int, scale: Optional[float] = None,
-              lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+              lse: Optional[torch.Tensor] = None, impl: Optional[str] = None) -> torch.Tensor:
     """Non-causal attention on BTHD tensors: q/o [B*Tq, H*Dh], k/v [B*Tk, H*Dh]."""
     if scale is None:
         scale = Dh ** -0.5
+    impl = impl or ATTENTION_IMPL[0]
     _count()
-    lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
+    if impl == "tcgen05":
+        lib().attention_sm100(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse, err_word(q.device))
+    else:
+        lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
     return o
 
 

@@ -13,6 +13,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 import torch.distributed as dist
 
+from ..ops.kernels import _count
 from ..ops.native import check_errors, err_word, lib
 
 MAX_RANKS = 8
@@ -86,6 +87,7 @@ class TPComm:
         if self.world == 1:
             return
         self.epoch = (self.epoch + 1) & 0x7FFFFFFF
+        _count()
         lib().tp_barrier(self.flags.ptrs, self.rank, self.epoch, self.err)
 
     def allreduce_epilogue(self, part: SymTensor, out: SymTensor, M: int, N: int, *, out_rows=None,
@@ -93,12 +95,14 @@ class TPComm:
                            aux_mode: int = 0, bias=None, gamma=None, resid=None, resid_rows=None, resid2=None) -> None:
         """Sum of every rank's `part[:M, :N]`, fused with the residual / LayerScale epilogue,
         stored into every rank's `out` (and `aux`). Caller brackets it with barriers."""
+        _count()
         lib().tp_allreduce_epi(part.ptrs, part.local.stride(0), out.view_ptrs(out_offset), out.local.stride(-2),
                                out_rows, aux.view_ptrs(aux_offset) if aux is not None else [],
                                aux.local.stride(-2) if aux is not None else 0, aux_rows, aux_mode, bias, gamma, resid,
                                resid_rows, resid2, M, N, self.rank)
 
     def mean_f32(self, src: SymTensor, dst: torch.Tensor) -> None:
+        _count()
         lib().tp_mean_f32(src.ptrs, dst)
 
     def check(self) -> None:

@@ -127,4 +127,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_elementwise_ops(m);
   register_attention_ops(m);
   register_comm_ops(m);
+  register_attention_sm100_ops(m);
 }

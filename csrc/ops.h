@@ -53,5 +53,6 @@ int num_sms();
 void register_elementwise_ops(pybind11::module_& m);
 void register_attention_ops(pybind11::module_& m);
 void register_comm_ops(pybind11::module_& m);
+void register_attention_sm100_ops(pybind11::module_& m);
 
 }  // namespace appcorr

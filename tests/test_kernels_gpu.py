@@ -168,8 +168,10 @@ def test_qkv_rope_scatter(Dh, H):
     _close(k2, k, rtol=1e-2, atol=1e-2)
 
 
-@pytest.mark.parametrize("Dh,H,Tq,Tk", [(128, 4, 1029, 1029), (64, 6, 197, 197), (128, 2, 312, 1029), (64, 3, 5, 70)])
-def test_attention(Dh, H, Tq, Tk):
+@pytest.mark.parametrize("impl", ["tcgen05", "mma"])
+@pytest.mark.parametrize("Dh,H,Tq,Tk", [(128, 4, 1029, 1029), (64, 6, 197, 197), (128, 2, 312, 1029), (64, 3, 5, 70),
+                                        (128, 2, 130, 260)])
+def test_attention(Dh, H, Tq, Tk, impl):
     K_ = _k()
     torch.manual_seed(6)
     B = 2
@@ -178,7 +180,11 @@ def test_attention(Dh, H, Tq, Tk):
     v = _rand(B * Tk, H * Dh)
     o = torch.empty_like(q)
     lse = torch.empty(B, H, Tq, device=DEV)
-    K_.attention(q, k, v, o, B=B, Tq=Tq, Tk=Tk, H=H, Dh=Dh, lse=lse)
+    K_.attention(q, k, v, o, B=B, Tq=Tq, Tk=Tk, H=H, Dh=Dh, lse=lse, impl=impl)
+    torch.cuda.synchronize()
+    from appcorr_b200.ops.native import check_errors
+
+    check_errors(q.device)
     qf = q.float().view(B, Tq, H, Dh).transpose(1, 2)
     kf = k.float().view(B, Tk, H, Dh).transpose(1, 2)
     vf = v.float().view(B, Tk, H, Dh).transpose(1, 2)
