@@ -268,9 +268,7 @@ class ViTEngine:
         K.layernorm(x, lw.norm1_w, lw.norm1_b, c.norm_eps, sess.xn)
         K.qkv_gemm(sess.xn, lw.qkv_w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
                    rope=sess.rope, n_prefix=c.n_prefix)
-        if server_pscore not in ("none", "disabled"):
-            K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=sess.pscore[l])
-        K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh)
+        self._attention_with_score(sess, l, H, server_pscore not in ("none", "disabled"), sess.pscore[l])
         # x_out = x + ls1 * proj(o); bos[l] = ls1 * proj(o)
         K.gemm(sess.o, lw.proj_w, x_out, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x,
                aux=sess.bos[l], aux_mode=K.AUX_SET)
@@ -279,6 +277,18 @@ class ViTEngine:
         # x_out += ls2 * mlp (in place: each output element reads only its own residual); bos[l] += same
         K.gemm(sess.h, lw.fc2_w, x_out, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_out,
                aux=sess.bos[l], aux_mode=K.AUX_ADD)
+
+    def _attention_with_score(self, sess: Session, l: int, H: int, score: bool, score_out: torch.Tensor) -> None:
+        """Full attention of layer l; with `score`, the CLS softmax row (server patch score)
+        comes out of the same attention pass and is averaged over the heads into score_out."""
+        B, N, Dh = sess.B, sess.N, self.cfg.head_dim
+        fused = score and K.ATTENTION_IMPL[0] == "tcgen05"
+        if score and not fused:
+            K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out)
+        K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh,
+                    cls_probs=sess.ps_scratch if fused else None)
+        if fused:
+            K.head_mean(sess.ps_scratch, B, H, N, score_out)
 
     def approx(self, sess: Session, start: int, end: int, server_pscore: str = "cls_attn_prob") -> torch.Tensor:
         """Approximate pass over layers [start, end) on the running features."""

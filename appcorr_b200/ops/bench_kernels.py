@@ -1,0 +1,112 @@
+"""Kernel micro-benchmarks (CUDA-event timing after warm-up) and single-launch drivers for ncu.
+
+    python -m appcorr_b200.ops.bench_kernels gemm --M 8232 --N 12288 --K 4096 [--bn 256] [--epi bf16]
+    python -m appcorr_b200.ops.bench_kernels attention --B 8 --H 32 --Dh 128 --Tq 1029 --Tk 1029
+    python -m appcorr_b200.ops.bench_kernels layernorm --M 8232 --D 4096
+    ... --once    launch the kernel exactly once (for `ncu -k ... -c 1`)
+
+Prints one JSON line: time per launch (ms), achieved TFLOP/s or GB/s, and the library
+reference (cuBLAS / cuDNN through PyTorch) for the same shape when --ref is given.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import kernels as K
+
+
+def _time(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op", choices=["gemm", "attention", "layernorm"])
+    ap.add_argument("--M", type=int, default=8232)
+    ap.add_argument("--N", type=int, default=12288)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--D", type=int, default=4096)
+    ap.add_argument("--bn", type=int, default=None)
+    ap.add_argument("--epi", default="bf16", choices=["bf16", "f32", "gelu"])
+    ap.add_argument("--B", type=int, default=8)
+    ap.add_argument("--H", type=int, default=32)
+    ap.add_argument("--Dh", type=int, default=128)
+    ap.add_argument("--Tq", type=int, default=1029)
+    ap.add_argument("--Tk", type=int, default=1029)
+    ap.add_argument("--impl", default="tcgen05")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--once", action="store_true")
+    ap.add_argument("--ref", action="store_true")
+    a = ap.parse_args(argv)
+    torch.manual_seed(0)
+    dev = "cuda"
+    res = {"op": a.op}
+    if a.op == "gemm":
+        x = torch.randn(a.M, a.K, device=dev).to(torch.bfloat16)
+        w = (torch.randn(a.N, a.K, device=dev) * a.K ** -0.5).to(torch.bfloat16)
+        epi = {"bf16": K.EPI_BF16, "f32": K.EPI_F32, "gelu": K.EPI_GELU}[a.epi]
+        out = torch.empty(a.M, a.N, device=dev, dtype=torch.float32 if a.epi == "f32" else torch.bfloat16)
+        fn = lambda: K.gemm(x, w, out, epi=epi, bn=a.bn)  # noqa: E731
+        flops = 2.0 * a.M * a.N * a.K
+        ref = (lambda: torch.matmul(x, w.T)) if a.ref else None  # noqa: E731
+        res.update(M=a.M, N=a.N, K=a.K, bn=a.bn)
+    elif a.op == "attention":
+        q = torch.randn(a.B * a.Tq, a.H * a.Dh, device=dev).to(torch.bfloat16)
+        k = torch.randn(a.B * a.Tk, a.H * a.Dh, device=dev).to(torch.bfloat16)
+        v = torch.randn(a.B * a.Tk, a.H * a.Dh, device=dev).to(torch.bfloat16)
+        o = torch.empty_like(q)
+        fn = lambda: K.attention(q, k, v, o, B=a.B, Tq=a.Tq, Tk=a.Tk, H=a.H, Dh=a.Dh, impl=a.impl)  # noqa: E731
+        flops = 4.0 * a.B * a.H * a.Tq * a.Tk * a.Dh
+        if a.ref:
+            qq = q.view(a.B, a.Tq, a.H, a.Dh).transpose(1, 2)
+            kk = k.view(a.B, a.Tk, a.H, a.Dh).transpose(1, 2)
+            vv = v.view(a.B, a.Tk, a.H, a.Dh).transpose(1, 2)
+            ref = lambda: torch.nn.functional.scaled_dot_product_attention(qq, kk, vv)  # noqa: E731
+        else:
+            ref = None
+        res.update(B=a.B, H=a.H, Dh=a.Dh, Tq=a.Tq, Tk=a.Tk, impl=a.impl)
+    else:
+        x = torch.randn(a.M, a.D, device=dev).to(torch.bfloat16)
+        wt = torch.ones(a.D, device=dev, dtype=torch.bfloat16)
+        bt = torch.zeros(a.D, device=dev, dtype=torch.bfloat16)
+        out = torch.empty_like(x)
+        fn = lambda: K.layernorm(x, wt, bt, 1e-5, out)  # noqa: E731
+        flops = 0.0
+        res.update(M=a.M, D=a.D, bytes=2 * x.numel() * 2)
+        ref = (lambda: torch.nn.functional.layer_norm(x, (a.D,), wt, bt, 1e-5)) if a.ref else None  # noqa: E731
+    if a.once:
+        fn()
+        torch.cuda.synchronize()
+        from .native import check_errors
+
+        check_errors(torch.device(dev))
+        print(json.dumps({**res, "launched": 1}))
+        return
+    ms = _time(fn, a.iters)
+    res["ms"] = round(ms, 4)
+    if flops:
+        res["tflops"] = round(flops / ms / 1e9, 1)
+    else:
+        res["gbps"] = round(res["bytes"] / ms / 1e6, 1)
+    if ref is not None:
+        rms = _time(ref, a.iters)
+        res["ref_ms"] = round(rms, 4)
+        if flops:
+            res["ref_tflops"] = round(flops / rms / 1e9, 1)
+    print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()

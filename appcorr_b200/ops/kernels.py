@@ -91,14 +91,19 @@ ATTENTION_IMPL = ["tcgen05"]  # "tcgen05" (sm_100a tensor cores + TMEM) or "mma"
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, *, B: int, Tq: int,
               Tk: int, H: int, Dh: int, scale: Optional[float] = None,
-              lse: Optional[torch.Tensor] = None, impl: Optional[str] = None) -> torch.Tensor:
-    """Non-causal attention on BTHD tensors: q/o [B*Tq, H*Dh], k/v [B*Tk, H*Dh]."""
+              lse: Optional[torch.Tensor] = None, impl: Optional[str] = None,
+              cls_probs: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Non-causal attention on BTHD tensors: q/o [B*Tq, H*Dh], k/v [B*Tk, H*Dh].
+
+    cls_probs (tcgen05 path): fp32 [B, H, Tk] receives the softmax row of query 0 (the CLS
+    token) of every (batch, head), computed in the same pass.
+    """
     if scale is None:
         scale = Dh ** -0.5
     impl = impl or ATTENTION_IMPL[0]
     _count()
     if impl == "tcgen05":
-        lib().attention_sm100(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse, err_word(q.device))
+        lib().attention_sm100(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse, err_word(q.device), cls_probs)
     else:
         lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
     return o
@@ -134,6 +139,13 @@ def cls_attn_pscore(q: torch.Tensor, k: torch.Tensor, *, B: int, N: int, H: int,
         scale = Dh ** -0.5
     _count(2)
     lib().cls_attn_pscore(q, k, B, N, H, Dh, float(scale), scratch, out)
+    return out
+
+
+def head_mean(probs: torch.Tensor, B: int, H: int, N: int, out: torch.Tensor) -> torch.Tensor:
+    """out[b, j] = mean over heads of probs[b, h, j]."""
+    _count()
+    lib().head_mean(probs, B, H, N, out)
     return out
 
 

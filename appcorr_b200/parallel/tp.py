@@ -127,10 +127,7 @@ class ViTEngineTP(ViTEngine):
         K.qkv_gemm(sess.xn, lw.qkv_w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
                    rope=sess.rope, n_prefix=c.n_prefix)
         score = server_pscore not in ("none", "disabled")
-        if score:
-            K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=self.local_heads, Dh=Dh, scratch=sess.ps_scratch,
-                              out=sym["sym_ps"].local)
-        K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=self.local_heads, Dh=Dh)
+        self._attention_with_score(sess, l, self.local_heads, score, sym["sym_ps"].local)
         K.gemm(sess.o, lw.proj_w, part)
         bos = sym["sym_bos"]
         off = l * M * c.embed_dim

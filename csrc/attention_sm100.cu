@@ -62,6 +62,7 @@ struct FaParams {
   bf16* o;
   long ldo;
   float* lse;      // [B, H, Tq] natural-log LSE or nullptr
+  float* cls;      // [B, H, Tk] softmax probabilities of query row 0 (CLS) or nullptr
   int* err;
 };
 
@@ -187,6 +188,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
     float m_run = -FLT_MAX, l_run = 0.f;
     bool ok = true;
+    const bool cls_row = p.cls != nullptr && qt == 0 && row == 0;
     uint8_t* prow = sP + row * 128;
     const int rsw = row & 7;
     for (int j = 0; j < nkb; ++j) {
@@ -210,6 +212,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       for (int t = 0; t < kFaBN; ++t) {
         if (kbase + t >= p.Tk) sv[t] = -FLT_MAX;
         mx = fmaxf(mx, sv[t]);
+      }
+      if (cls_row) {  // keep the CLS row's scaled logits; normalised once the row's max / sum are final
+        float* dst = p.cls + ((long)b * p.H + h) * p.Tk + kbase;
+        const int n = min(kFaBN, p.Tk - kbase);
+#pragma unroll
+        for (int t = 0; t < kFaBN; ++t)
+          if (t < n) dst[t] = sv[t];
       }
       // rescale decision (warp-uniform because tcgen05.ld/st are warp-collective)
       const bool grow = mx > m_run + kRescaleThreshold;
@@ -281,6 +290,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       if (p.lse != nullptr && qrow < p.Tq)
         p.lse[((long)b * p.H + h) * p.Tq + qrow] = (m_run + log2f(l_run)) * 0.69314718055994531f;
     }
+    if (p.cls != nullptr && qt == 0 && qd == 0) {  // the warp holding row 0 normalises the CLS row
+      __syncwarp();
+      const float m0 = __shfl_sync(0xffffffffu, m_run, 0);
+      const float inv0 = 1.f / __shfl_sync(0xffffffffu, l_run, 0);
+      float* src = p.cls + ((long)b * p.H + h) * p.Tk;
+      for (int t = lane; t < p.Tk; t += 32) src[t] = exp2f(src[t] - m0) * inv0;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -292,7 +308,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
 void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, int64_t B,
                         int64_t Tq, int64_t Tk, int64_t H, int64_t Dh, double scale, c10::optional<at::Tensor> lse,
-                        const at::Tensor& err) {
+                        const at::Tensor& err, c10::optional<at::Tensor> cls) {
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &o}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->stride(-1) == 1, "attention: bf16 CUDA tensors");
     TORCH_CHECK(t->stride(-2) % 8 == 0 && (reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) == 0, "attention: 16B-aligned rows");
@@ -307,7 +323,12 @@ void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tens
   CUtensorMap tv = make_tmap_bf16_2d(v.data_ptr(), B * Tk, H * Dh, v.stride(-2), kFaBN, 64);
   FaParams p{static_cast<int>(B), static_cast<int>(Tq), static_cast<int>(Tk), static_cast<int>(H),
              static_cast<float>(scale * 1.4426950408889634), reinterpret_cast<bf16*>(o.data_ptr()), o.stride(-2),
-             nullptr, err.data_ptr<int>()};
+             nullptr, nullptr, err.data_ptr<int>()};
+  if (cls.has_value()) {
+    TORCH_CHECK(cls->scalar_type() == at::kFloat && cls->is_contiguous() && cls->numel() >= B * H * Tk,
+                "attention: cls fp32 [B,H,Tk]");
+    p.cls = cls->data_ptr<float>();
+  }
   if (lse.has_value()) {
     TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->numel() >= B * H * Tq, "attention: lse fp32 [B,H,Tq]");
     p.lse = lse->data_ptr<float>();
@@ -329,7 +350,8 @@ void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tens
 void register_attention_sm100_ops(pybind11::module_& m) {
   namespace py = pybind11;
   m.def("attention_sm100", &attention_sm100_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("B"),
-        py::arg("Tq"), py::arg("Tk"), py::arg("H"), py::arg("Dh"), py::arg("scale"), py::arg("lse"), py::arg("err"));
+        py::arg("Tq"), py::arg("Tk"), py::arg("H"), py::arg("Dh"), py::arg("scale"), py::arg("lse"), py::arg("err"),
+        py::arg("cls") = py::none());
 }
 
 }  // namespace appcorr

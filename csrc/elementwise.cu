@@ -689,7 +689,17 @@ void mean_rows_op(const at::Tensor& x, int64_t B, int64_t N, int64_t start, at::
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void head_mean_op(const at::Tensor& probs, int64_t B, int64_t H, int64_t N, at::Tensor& out) {
+  TORCH_CHECK(probs.scalar_type() == at::kFloat && probs.numel() >= B * H * N, "head_mean: fp32 [B,H,N]");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() == B * N, "head_mean: out fp32 [B,N]");
+  c10::cuda::CUDAGuard g(probs.device());
+  head_mean_kernel<<<static_cast<int>(std::max<long>(1, (B * N + 255) / 256)), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      probs.data_ptr<float>(), static_cast<int>(B), static_cast<int>(H), static_cast<int>(N), out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void register_elementwise_ops(pybind11::module_& m) {
+  m.def("head_mean", &head_mean_op);
   namespace py = pybind11;
   m.def("layernorm", &layernorm_op, py::arg("x"), py::arg("rows"), py::arg("w"), py::arg("b"), py::arg("eps"),
         py::arg("out"), py::arg("copy_out") = py::none());

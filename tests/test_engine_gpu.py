@@ -126,3 +126,18 @@ def test_engine_full_correction_recovers_true_forward():
     x2 = eng.approx(s2, 0, 3)
     torch.cuda.synchronize()
     assert _rel(x1, x2) < 1e-2
+
+
+def test_detr_decoder_gpu_matches_module():
+    from appcorr_b200.models.detr import DetrDecoder, DetrDecoderGPU
+
+    torch.manual_seed(0)
+    dec = DetrDecoder(384, d_model=256, heads=4, layers=2, num_queries=50, num_classes=80).to(DEV).eval()
+    B, hw = 2, (8, 12)
+    feat = torch.randn(B * 96, 384, device=DEV)
+    with torch.no_grad():
+        ref = dec(feat.view(B, 96, 384), hw)
+    out = DetrDecoderGPU(dec, DEV).forward(feat.to(torch.bfloat16), B, hw)
+    torch.cuda.synchronize()
+    assert _rel(out["pred_logits"], ref["pred_logits"]) < 3e-2
+    assert _rel(out["pred_boxes"], ref["pred_boxes"]) < 2e-2

@@ -326,3 +326,21 @@ def test_gemm_2cta_epilogues():
         K_.qkv_gemm(a3, w3, None, q, k, v, head_dim=Dh, seq_len=Nt, rope=(sin, cos), n_prefix=npre, bn=bn)
     for x, y in zip(*bufs):
         _close(x, y, rtol=1e-2, atol=1e-2)
+
+
+def test_attention_fused_cls_score():
+    """The tcgen05 attention's CLS softmax row equals the standalone CLS score kernel."""
+    K_ = _k()
+    torch.manual_seed(12)
+    B, N, H, Dh = 2, 300, 4, 128
+    q = _rand(B * N, H * Dh)
+    k = _rand(B * N, H * Dh)
+    v = _rand(B * N, H * Dh)
+    o = torch.empty_like(q)
+    probs = torch.empty(B, H, N, device=DEV)
+    K_.attention(q, k, v, o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, impl="tcgen05", cls_probs=probs)
+    fused = torch.empty(B, N, device=DEV)
+    K_.head_mean(probs, B, H, N, fused)
+    ref = torch.empty(B, N, device=DEV)
+    K_.cls_attn_pscore(q, k, B=B, N=N, H=H, Dh=Dh, scratch=torch.empty(B, H, N, device=DEV), out=ref)
+    _close(fused, ref, rtol=1e-3, atol=1e-5)
