@@ -52,6 +52,8 @@ class LayerW:
     fc2_w: torch.Tensor           # fc2 / w3 [D, hidden]
     fc2_b: Optional[torch.Tensor]
     ls2: torch.Tensor
+    # e4m3 copies (w8 [N, K], per-output-channel fp32 scale [N]) for the fp8 GEMM path
+    q8: Optional[Dict[str, Tuple[torch.Tensor, torch.Tensor]]] = None
 
 
 @dataclass
@@ -201,21 +203,84 @@ class Session:
     extra: Dict[str, torch.Tensor] = field(default_factory=dict)
 
 
+PRECISIONS = ("bf16", "fp8")
+_Q8_NAMES = ("qkv", "proj", "fc1", "fc2")
+
+
+def quantize_layer_e4m3(lw: LayerW) -> None:
+    """Attach per-output-channel e4m3 copies of the four GEMM weights of a layer."""
+    lw.q8 = {n: K.quantize_weight_e4m3(getattr(lw, n + "_w")) for n in _Q8_NAMES}
+
+
 class ViTEngine:
-    def __init__(self, weights: EngineWeights, device=None):
+    """precision: "bf16" everywhere, "fp8" (e4m3 activations with per-row scales x e4m3 weights
+    with per-channel scales on the tcgen05 kind::f8f6f4 GEMM, fp32 accumulation, bf16 residual
+    stream), or a dict {"approx": ..., "correct": ...} to choose per pass (reference
+    dinov3_precision.py keeps separate approx / correct precisions)."""
+
+    def __init__(self, weights: EngineWeights, device=None, precision="bf16"):
         self.w = weights
         self.cfg = weights.cfg
         self.device = torch.device(device) if device is not None else weights.patch_w.device
         if self.cfg.head_dim not in (64, 128):
             raise ValueError("the sm_100a engine supports head_dim 64 or 128")
+        if isinstance(precision, str):
+            precision = {"approx": precision, "correct": precision}
+        for v in precision.values():
+            if v not in PRECISIONS:
+                raise ValueError(f"engine precision must be one of {PRECISIONS}, got {v!r}")
+        self.precision = dict(precision)
+        if "fp8" in self.precision.values():
+            for lw in self.w.layers:
+                if lw.q8 is None:
+                    quantize_layer_e4m3(lw)
+        self._fp8 = False  # precision of the pass being run
 
     @classmethod
-    def from_module(cls, model: DinoVisionTransformer, device) -> "ViTEngine":
-        return cls(weights_from_module(model, device), device)
+    def from_module(cls, model: DinoVisionTransformer, device, precision="bf16") -> "ViTEngine":
+        return cls(weights_from_module(model, device), device, precision)
 
     @classmethod
-    def random(cls, cfg: ViTConfig, device, seed: int = 0) -> "ViTEngine":
-        return cls(random_weights(cfg, device, seed), device)
+    def random(cls, cfg: ViTConfig, device, seed: int = 0, precision="bf16") -> "ViTEngine":
+        return cls(random_weights(cfg, device, seed), device, precision)
+
+    # -------------------------------------------------------------- precision helpers
+    def _norm(self, sess: Session, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, out: torch.Tensor,
+              rows: Optional[torch.Tensor] = None, copy_out: Optional[torch.Tensor] = None):
+        """LayerNorm feeding a GEMM: returns (operand, row scale or None)."""
+        if not self._fp8:
+            K.layernorm(x, w, b, self.cfg.norm_eps, out, rows=rows, copy_out=copy_out)
+            return out, None
+        n = out.shape[0]
+        q8, s = sess.extra["a8"][:n, : out.shape[1]], sess.extra["a8_scale"][:n]
+        K.layernorm(x, w, b, self.cfg.norm_eps, q8, rows=rows, copy_out=copy_out, scale8=s)
+        return q8, s
+
+    def _act(self, sess: Session, t: torch.Tensor):
+        """bf16 activation feeding a GEMM: returns (operand, row scale or None)."""
+        if not self._fp8:
+            return t, None
+        n, k = t.shape
+        q8, s = sess.extra["a8"][:n, :k], sess.extra["a8_scale"][:n]
+        K.quant_rows_e4m3(t, q8, s)
+        return q8, s
+
+    def _w(self, lw: LayerW, name: str):
+        if self._fp8:
+            return lw.q8[name]
+        return getattr(lw, name + "_w"), None
+
+    def _ensure_fp8_scratch(self, sess: Session) -> None:
+        if "a8" not in sess.extra:
+            M = sess.x.shape[0]
+            width = max(self.cfg.embed_dim, sess.h.shape[1])
+            sess.extra["a8"] = torch.empty(M, width, device=self.device, dtype=torch.float8_e4m3fn)
+            sess.extra["a8_scale"] = torch.empty(M, device=self.device, dtype=torch.float32)
+
+    def _set_pass(self, sess: Session, which: str) -> None:
+        self._fp8 = self.precision[which] == "fp8"
+        if self._fp8:
+            self._ensure_fp8_scratch(sess)
 
     # -------------------------------------------------------------- sessions
     def new_session(self, B: int, H: int, W: int) -> Session:
@@ -255,28 +320,32 @@ class ViTEngine:
         return out
 
     # -------------------------------------------------------------- approximate pass
-    def _mlp(self, lw: LayerW, xin: torch.Tensor, hbuf: torch.Tensor) -> torch.Tensor:
-        if self.cfg.is_swiglu:
-            K.gemm(xin, lw.fc1_w, hbuf, epi=K.EPI_SWIGLU, bias=lw.fc1_b)
-        else:
-            K.gemm(xin, lw.fc1_w, hbuf, epi=K.EPI_GELU, bias=lw.fc1_b)
+    def _mlp(self, lw: LayerW, xin: torch.Tensor, hbuf: torch.Tensor, a_scale=None) -> torch.Tensor:
+        w, ws = self._w(lw, "fc1")
+        epi = K.EPI_SWIGLU if self.cfg.is_swiglu else K.EPI_GELU
+        K.gemm(xin, w, hbuf, epi=epi, bias=lw.fc1_b, a_scale=a_scale, b_scale=ws)
         return hbuf
 
     def approx_layer(self, sess: Session, l: int, x: torch.Tensor, x_out: torch.Tensor, server_pscore: str) -> None:
         c, lw = self.cfg, self.w.layers[l]
         B, N, H, Dh = sess.B, sess.N, c.num_heads, c.head_dim
-        K.layernorm(x, lw.norm1_w, lw.norm1_b, c.norm_eps, sess.xn)
-        K.qkv_gemm(sess.xn, lw.qkv_w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
-                   rope=sess.rope, n_prefix=c.n_prefix)
+        a, sa = self._norm(sess, x, lw.norm1_w, lw.norm1_b, sess.xn)
+        w, ws = self._w(lw, "qkv")
+        K.qkv_gemm(a, w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
+                   rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         self._attention_with_score(sess, l, H, server_pscore not in ("none", "disabled"), sess.pscore[l])
         # x_out = x + ls1 * proj(o); bos[l] = ls1 * proj(o)
-        K.gemm(sess.o, lw.proj_w, x_out, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x,
-               aux=sess.bos[l], aux_mode=K.AUX_SET)
-        K.layernorm(x_out, lw.norm2_w, lw.norm2_b, c.norm_eps, sess.xn)
-        self._mlp(lw, sess.xn, sess.h)
+        a, sa = self._act(sess, sess.o)
+        w, ws = self._w(lw, "proj")
+        K.gemm(a, w, x_out, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x,
+               aux=sess.bos[l], aux_mode=K.AUX_SET, a_scale=sa, b_scale=ws)
+        a, sa = self._norm(sess, x_out, lw.norm2_w, lw.norm2_b, sess.xn)
+        self._mlp(lw, a, sess.h, sa)
         # x_out += ls2 * mlp (in place: each output element reads only its own residual); bos[l] += same
-        K.gemm(sess.h, lw.fc2_w, x_out, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_out,
-               aux=sess.bos[l], aux_mode=K.AUX_ADD)
+        a, sa = self._act(sess, sess.h)
+        w, ws = self._w(lw, "fc2")
+        K.gemm(a, w, x_out, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_out,
+               aux=sess.bos[l], aux_mode=K.AUX_ADD, a_scale=sa, b_scale=ws)
 
     def _attention_with_score(self, sess: Session, l: int, H: int, score: bool, score_out: torch.Tensor) -> None:
         """Full attention of layer l; with `score`, the CLS softmax row (server patch score)
@@ -294,6 +363,7 @@ class ViTEngine:
         """Approximate pass over layers [start, end) on the running features."""
         if start == 0:
             sess.x.copy_(sess.x_in)
+        self._set_pass(sess, "approx")
         for l in range(start, end):
             self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
         sess.approx_done = max(sess.approx_done, end)
@@ -322,17 +392,22 @@ class ViTEngine:
         x_act, x_att = sess.x_act[:MT], sess.x_att[:MT]
         xn = sess.xn[:MT]
         q, o, h = sess.q[:MT], sess.o[:MT], sess.h[:MT]
-        K.layernorm(x, lw.norm1_w, lw.norm1_b, c.norm_eps, xn, rows=rows, copy_out=x_act)
+        a, sa = self._norm(sess, x, lw.norm1_w, lw.norm1_b, xn, rows=rows, copy_out=x_act)
         K.add_(x, sess.bos[l])
-        K.qkv_gemm(xn, lw.qkv_w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
-                   kv_rows=rows, rope=sess.rope, n_prefix=c.n_prefix)
+        w, ws = self._w(lw, "qkv")
+        K.qkv_gemm(a, w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
+                   kv_rows=rows, rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh)
-        K.gemm(o, lw.proj_w, x_att, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x_act)
-        K.layernorm(x_att, lw.norm2_w, lw.norm2_b, c.norm_eps, xn)
-        self._mlp(lw, xn, h)
+        a, sa = self._act(sess, o)
+        w, ws = self._w(lw, "proj")
+        K.gemm(a, w, x_att, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x_act, a_scale=sa, b_scale=ws)
+        a, sa = self._norm(sess, x_att, lw.norm2_w, lw.norm2_b, xn)
+        self._mlp(lw, a, h, sa)
         # x[rows] = x_att + ls2 * mlp; bos[l][rows] = (x_att - x_act) + ls2 * mlp
-        K.gemm(h, lw.fc2_w, x, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_att, out_rows=rows,
-               aux=sess.bos[l], aux_mode=K.AUX_OUT_MINUS, resid2=x_act)
+        a, sa = self._act(sess, h)
+        w, ws = self._w(lw, "fc2")
+        K.gemm(a, w, x, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_att, out_rows=rows,
+               aux=sess.bos[l], aux_mode=K.AUX_OUT_MINUS, resid2=x_act, a_scale=sa, b_scale=ws)
 
     def correct(self, sess: Session, start: int, end: int, pre: torch.Tensor, cand: torch.Tensor, opts: Dict,
                 mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -349,6 +424,7 @@ class ViTEngine:
         kind = str(opts.get("server_pscore", "cls_attn_prob"))
         if start == 0:
             sess.x.copy_(sess.x_in)
+        self._set_pass(sess, "correct")
         x = sess.x
         shared = None
         if kind in LAYERMEAN_SERVER_PSCORES:

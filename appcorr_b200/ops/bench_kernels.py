@@ -40,6 +40,7 @@ def main(argv=None) -> None:
     ap.add_argument("--D", type=int, default=4096)
     ap.add_argument("--bn", type=int, default=None)
     ap.add_argument("--epi", default="bf16", choices=["bf16", "f32", "gelu"])
+    ap.add_argument("--fp8", action="store_true", help="e4m3 operands (kind::f8f6f4); --ref times torch._scaled_mm")
     ap.add_argument("--B", type=int, default=8)
     ap.add_argument("--H", type=int, default=32)
     ap.add_argument("--Dh", type=int, default=128)
@@ -58,10 +59,19 @@ def main(argv=None) -> None:
         w = (torch.randn(a.N, a.K, device=dev) * a.K ** -0.5).to(torch.bfloat16)
         epi = {"bf16": K.EPI_BF16, "f32": K.EPI_F32, "gelu": K.EPI_GELU}[a.epi]
         out = torch.empty(a.M, a.N, device=dev, dtype=torch.float32 if a.epi == "f32" else torch.bfloat16)
-        fn = lambda: K.gemm(x, w, out, epi=epi, bn=a.bn)  # noqa: E731
         flops = 2.0 * a.M * a.N * a.K
-        ref = (lambda: torch.matmul(x, w.T)) if a.ref else None  # noqa: E731
-        res.update(M=a.M, N=a.N, K=a.K, bn=a.bn)
+        if a.fp8:
+            x8 = torch.empty(a.M, a.K, device=dev, dtype=torch.float8_e4m3fn)
+            sx = torch.empty(a.M, device=dev)
+            K.quant_rows_e4m3(x, x8, sx)
+            w8, sw = K.quantize_weight_e4m3(w)
+            fn = lambda: K.gemm(x8, w8, out, epi=epi, bn=a.bn, a_scale=sx, b_scale=sw)  # noqa: E731
+            one = torch.ones((), device=dev)
+            ref = (lambda: torch._scaled_mm(x8, w8.T, one, one, out_dtype=torch.bfloat16)) if a.ref else None  # noqa: E731
+        else:
+            fn = lambda: K.gemm(x, w, out, epi=epi, bn=a.bn)  # noqa: E731
+            ref = (lambda: torch.matmul(x, w.T)) if a.ref else None  # noqa: E731
+        res.update(M=a.M, N=a.N, K=a.K, bn=a.bn, fp8=a.fp8)
     elif a.op == "attention":
         q = torch.randn(a.B * a.Tq, a.H * a.Dh, device=dev).to(torch.bfloat16)
         k = torch.randn(a.B * a.Tk, a.H * a.Dh, device=dev).to(torch.bfloat16)

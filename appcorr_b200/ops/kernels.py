@@ -40,14 +40,20 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
          resid_rows: Optional[torch.Tensor] = None, aux: Optional[torch.Tensor] = None,
          aux_rows: Optional[torch.Tensor] = None, aux_mode: int = AUX_NONE,
          resid2: Optional[torch.Tensor] = None, bn: Optional[int] = None,
-         max_ctas: int = 0) -> torch.Tensor:
-    """out = epilogue(a @ w^T). `a` [M, K] bf16, `w` [N, K] bf16 (nn.Linear layout)."""
+         max_ctas: int = 0, a_scale: Optional[torch.Tensor] = None,
+         b_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = epilogue(a @ w^T). `a` [M, K], `w` [N, K] (nn.Linear layout), both bf16 or both
+    e4m3; e4m3 operands carry fp32 scales a_scale [M] (per row) and b_scale [N] (per output
+    channel) that the epilogue applies to the fp32 accumulator before bias / activation."""
+    fp8 = a.dtype == torch.float8_e4m3fn
     if bn is None:
         bn = 256 if epi == EPI_SWIGLU else _pick_bn(w.shape[0], a.shape[0])
+        if fp8 and bn == 64:
+            bn = 128
     _count()
     lib().gemm(a, w, epi, bn, err_word(a.device), out=out, out_rows=out_rows, bias=bias, gamma=gamma,
                resid=resid, resid_rows=resid_rows, aux=aux, aux_rows=aux_rows, aux_mode=aux_mode,
-               resid2=resid2, max_ctas=max_ctas)
+               resid2=resid2, max_ctas=max_ctas, a_scale=a_scale, b_scale=b_scale)
     return out
 
 
@@ -55,29 +61,49 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
              k_out: torch.Tensor, v_out: torch.Tensor, *, head_dim: int, seq_len: int = 0,
              tok_idx: Optional[torch.Tensor] = None, kv_rows: Optional[torch.Tensor] = None,
              rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, n_prefix: int = 0,
-             bn: Optional[int] = None) -> None:
+             bn: Optional[int] = None, a_scale: Optional[torch.Tensor] = None,
+             b_scale: Optional[torch.Tensor] = None, kv_dim: int = 0) -> None:
     """qkv projection with RoPE on q/k (tokens >= n_prefix) split into three BTHD buffers.
 
     q row m is written at q_out[m]; k/v rows at kv_rows[m] (or m). `rope` = (sin, cos) fp32
     tables [n_patch_tokens, head_dim] whose second half repeats the first (the DINOv3 angle
-    layout); the kernel reads only the first half.
+    layout); the kernel reads only the first half. kv_dim > 0: grouped-query weight rows
+    [q (N - 2 kv_dim) | k (kv_dim) | v (kv_dim)].
     """
-    dim = w.shape[0] // 3
+    dim = w.shape[0] - 2 * kv_dim if kv_dim else w.shape[0] // 3
     if bn is None:
-        bn = 256 if dim % 256 == 0 else 128
+        bn = 256 if dim % 256 == 0 and (kv_dim or dim) % 256 == 0 else 128
     sin, cos = rope if rope is not None else (None, None)
     _count()
     lib().gemm(a, w, EPI_QKV, bn, err_word(a.device), bias=bias, q_out=q_out, k_out=k_out, v_out=v_out,
                kv_rows=kv_rows, tok_idx=tok_idx, seq_len=seq_len, rope_sin=sin, rope_cos=cos,
-               n_prefix=n_prefix, head_dim=head_dim)
+               n_prefix=n_prefix, head_dim=head_dim, a_scale=a_scale, b_scale=b_scale, kv_dim=kv_dim)
 
 
 def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, out: torch.Tensor,
-              rows: Optional[torch.Tensor] = None, copy_out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """out[i] = LN(x[rows[i]]) (rows=None: every row). copy_out[i] receives the raw gathered row."""
+              rows: Optional[torch.Tensor] = None, copy_out: Optional[torch.Tensor] = None,
+              scale8: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[i] = LN(x[rows[i]]) (rows=None: every row). copy_out[i] receives the raw gathered row.
+    An e4m3 `out` receives the bf16-rounded LN row divided by scale8[i] = amax_i / 448."""
     _count()
-    lib().layernorm(x, rows, w, b, float(eps), out, copy_out)
+    lib().layernorm(x, rows, w, b, float(eps), out, copy_out, scale8)
     return out
+
+
+def quant_rows_e4m3(x: torch.Tensor, out: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """out = x / scale[:, None] in e4m3 with scale = row amax / 448 (fp32)."""
+    _count()
+    lib().quant_rows_e4m3(x, out, scale)
+    return out
+
+
+def quantize_weight_e4m3(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel e4m3 weight: (w8 [N, K], scale [N] fp32) with w ~= w8 * scale[:, None].
+    One-time weight preparation (any device)."""
+    wf = w.float()
+    sc = (wf.abs().amax(dim=1).clamp_min(1e-12) / 448.0).contiguous()
+    w8 = (wf / sc[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).contiguous()
+    return w8, sc
 
 
 def add_(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:

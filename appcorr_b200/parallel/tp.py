@@ -66,24 +66,24 @@ class ViTEngineTP(ViTEngine):
     """ViTEngine whose layers run split over `comm.world` GPUs. Construct from full weights
     (`from_full`) or generate random shards directly (`random`)."""
 
-    def __init__(self, weights: EngineWeights, comm: TPComm, device=None):
-        super().__init__(weights, device)
+    def __init__(self, weights: EngineWeights, comm: TPComm, device=None, precision="bf16"):
+        super().__init__(weights, device, precision)
         self.comm = comm
         self.world, self.rank = comm.world, comm.rank
         self.local_heads = self.cfg.num_heads // self.world
         self.local_dim = self.cfg.embed_dim // self.world
 
     @classmethod
-    def from_full(cls, full: EngineWeights, comm: TPComm) -> "ViTEngineTP":
-        return cls(shard_weights(full, comm.rank, comm.world), comm, comm.device)
+    def from_full(cls, full: EngineWeights, comm: TPComm, precision="bf16") -> "ViTEngineTP":
+        return cls(shard_weights(full, comm.rank, comm.world), comm, comm.device, precision)
 
     @classmethod
-    def random_tp(cls, cfg: ViTConfig, comm: TPComm, seed: int = 0) -> "ViTEngineTP":
+    def random_tp(cls, cfg: ViTConfig, comm: TPComm, seed: int = 0, precision="bf16") -> "ViTEngineTP":
         full = random_weights(cfg, comm.device, seed)  # identical on every rank (same seed)
         w = shard_weights(full, comm.rank, comm.world)
         del full
         torch.cuda.empty_cache()
-        return cls(w, comm, comm.device)
+        return cls(w, comm, comm.device, precision)
 
     # -------------------------------------------------------------- sessions
     def new_session(self, B: int, H: int, W: int) -> Session:
@@ -123,27 +123,33 @@ class ViTEngineTP(ViTEngine):
         M = B * N
         sym = sess.extra
         part = sym["sym_part"].local
-        K.layernorm(x, lw.norm1_w, lw.norm1_b, c.norm_eps, sess.xn)
-        K.qkv_gemm(sess.xn, lw.qkv_w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
-                   rope=sess.rope, n_prefix=c.n_prefix)
+        a, sa = self._norm(sess, x, lw.norm1_w, lw.norm1_b, sess.xn)
+        w, ws = self._w(lw, "qkv")
+        K.qkv_gemm(a, w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
+                   rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         score = server_pscore not in ("none", "disabled")
         self._attention_with_score(sess, l, self.local_heads, score, sym["sym_ps"].local)
-        K.gemm(sess.o, lw.proj_w, part)
+        a, sa = self._act(sess, sess.o)
+        w, ws = self._w(lw, "proj")
+        K.gemm(a, w, part, a_scale=sa, b_scale=ws)
         bos = sym["sym_bos"]
         off = l * M * c.embed_dim
         self._reduce(sess, M, out=sym["sym_x"], aux=bos, aux_offset=off, aux_mode=K.AUX_SET, bias=lw.proj_b,
                      gamma=lw.ls1, resid=x)
         if score:  # every rank's local-head mean is ready (barrier above): average them
             self.comm.mean_f32(sym["sym_ps"], sess.pscore[l])
-        K.layernorm(x, lw.norm2_w, lw.norm2_b, c.norm_eps, sess.xn)
-        self._mlp(lw, sess.xn, sess.h)
-        K.gemm(sess.h, lw.fc2_w, part)
+        a, sa = self._norm(sess, x, lw.norm2_w, lw.norm2_b, sess.xn)
+        self._mlp(lw, a, sess.h, sa)
+        a, sa = self._act(sess, sess.h)
+        w, ws = self._w(lw, "fc2")
+        K.gemm(a, w, part, a_scale=sa, b_scale=ws)
         self._reduce(sess, M, out=sym["sym_x"], aux=bos, aux_offset=off, aux_mode=K.AUX_ADD, bias=lw.fc2_b,
                      gamma=lw.ls2, resid=x)
 
     def approx(self, sess: Session, start: int, end: int, server_pscore: str = "cls_attn_prob") -> torch.Tensor:
         if start == 0:
             sess.x.copy_(sess.x_in)
+        self._set_pass(sess, "approx")
         for l in range(start, end):
             self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
         sess.approx_done = max(sess.approx_done, end)
@@ -159,16 +165,21 @@ class ViTEngineTP(ViTEngine):
         part = sym["sym_part"].local[:MT]
         x_act, x_att = sess.x_act[:MT], sess.x_att[:MT]
         xn, q, o, h = sess.xn[:MT], sess.q[:MT], sess.o[:MT], sess.h[:MT]
-        K.layernorm(x, lw.norm1_w, lw.norm1_b, c.norm_eps, xn, rows=rows, copy_out=x_act)
+        a, sa = self._norm(sess, x, lw.norm1_w, lw.norm1_b, xn, rows=rows, copy_out=x_act)
         K.add_(x, sess.bos[l])
-        K.qkv_gemm(xn, lw.qkv_w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
-                   kv_rows=rows, rope=sess.rope, n_prefix=c.n_prefix)
+        w, ws = self._w(lw, "qkv")
+        K.qkv_gemm(a, w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
+                   kv_rows=rows, rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=self.local_heads, Dh=Dh)
-        K.gemm(o, lw.proj_w, part)
+        a, sa = self._act(sess, o)
+        w, ws = self._w(lw, "proj")
+        K.gemm(a, w, part, a_scale=sa, b_scale=ws)
         self._reduce(sess, MT, out=sym["sym_x_att"], bias=lw.proj_b, gamma=lw.ls1, resid=x_act)
-        K.layernorm(x_att, lw.norm2_w, lw.norm2_b, c.norm_eps, xn)
-        self._mlp(lw, xn, h)
-        K.gemm(h, lw.fc2_w, part)
+        a, sa = self._norm(sess, x_att, lw.norm2_w, lw.norm2_b, xn)
+        self._mlp(lw, a, h, sa)
+        a, sa = self._act(sess, h)
+        w, ws = self._w(lw, "fc2")
+        K.gemm(a, w, part, a_scale=sa, b_scale=ws)
         self._reduce(sess, MT, out=sym["sym_x"], out_rows=rows, aux=sym["sym_bos"],
                      aux_offset=l * B * N * c.embed_dim, aux_mode=K.AUX_OUT_MINUS, bias=lw.fc2_b, gamma=lw.ls2,
                      resid=x_att, resid2=x_act)

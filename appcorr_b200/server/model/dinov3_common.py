@@ -46,6 +46,16 @@ class DINOv3BackboneMixin:
         self._group_cache: Dict[Tuple, Tuple[torch.Tensor, torch.Tensor]] = {}
 
     # ------------------------------------------------------------------ loading
+    @staticmethod
+    def engine_precision(config: Any) -> Dict[str, str]:
+        """Config precision -> engine precision per pass. "auto" selects e4m3 (the reference
+        picks FP8 at >= 3072 rows, dinov3_precision.py:172-200, which every batched approx pass
+        of the served models reaches). NVFP4 ("fp4") runs on the e4m3 GEMM path."""
+        m = {"bf16": "bf16", "fp8": "fp8", "auto": "fp8", "fp4": "fp8"}
+        ap = m.get(str(getattr(config, "precision", "bf16")).lower(), "bf16")
+        cp = m.get(str(getattr(config, "correct_precision", "bf16")).lower(), "bf16")
+        return {"approx": ap, "correct": cp}
+
     def load_backbone(self, model_name: str, config: Any) -> None:
         profile = config.get_input_profile_config()
         self.arch = arch_for(model_name, profile, self.default_arch)
@@ -54,6 +64,7 @@ class DINOv3BackboneMixin:
         self._sessions.clear()
         self._group_cache.clear()
         tp = int(getattr(config, "tp_size", 1) or 1)
+        prec = self.engine_precision(config)
         if self.device.type == "cuda" and tp > 1:
             import torch.distributed as dist
 
@@ -67,9 +78,9 @@ class DINOv3BackboneMixin:
             if path is not None:
                 m = build_vit(self.arch)
                 m.load_state_dict(torch.load(path, map_location="cpu", mmap=True, weights_only=True), strict=True)
-                self.engine = ViTEngineTP.from_full(weights_from_module(m.eval(), self.device), self.comm)
+                self.engine = ViTEngineTP.from_full(weights_from_module(m.eval(), self.device), self.comm, prec)
             else:
-                self.engine = ViTEngineTP.random_tp(PRESETS[self.arch], self.comm, seed=seed)
+                self.engine = ViTEngineTP.random_tp(PRESETS[self.arch], self.comm, seed=seed, precision=prec)
             self.cfg = self.engine.cfg
         elif self.device.type == "cuda":
             from ...models.engine import ViTEngine
@@ -77,10 +88,10 @@ class DINOv3BackboneMixin:
             if path is not None:
                 m = build_vit(self.arch)
                 m.load_state_dict(torch.load(path, map_location="cpu", mmap=True, weights_only=True), strict=True)
-                self.engine = ViTEngine.from_module(m.eval(), self.device)
+                self.engine = ViTEngine.from_module(m.eval(), self.device, prec)
                 self.backbone = None
             else:
-                self.engine = ViTEngine.random(PRESETS[self.arch], self.device, seed=seed)
+                self.engine = ViTEngine.random(PRESETS[self.arch], self.device, seed=seed, precision=prec)
             self.cfg = self.engine.cfg
         else:
             m = build_vit(self.arch)
@@ -171,7 +182,7 @@ class DINOv3BackboneMixin:
                                                           server_pscore_weight=opts["server_pscore_weight"])
             context["x"] = x
         context["approx_frontier"] = max(context.get("approx_frontier", 0), end)
-        return {"precision": "bf16" if self.engine is not None else "fp32"}
+        return {"precision": self.engine.precision["approx"] if self.engine is not None else "fp32"}
 
     def group_candidates(self, B: int, grid_hw: Tuple[int, int], group_id: int, config: Any,
                          device) -> Tuple[torch.Tensor, torch.Tensor]:

@@ -53,6 +53,9 @@ def parse_args():
     ap.add_argument("--arch", default="vit7b16")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--precision", default="fp8", choices=["bf16", "fp8"],
+                    help="GEMM operand precision of the approx and correct passes (ours; the reference arm "
+                         "runs its default bf16 path: its fp8/fp4 approx controllers need torchao)")
     ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
                     help="N > 1: tensor-parallel over N GPUs (one request batch) or N data-parallel replicas")
     return ap.parse_args()
@@ -168,7 +171,7 @@ def make_config(args, world: int = 1):
 
     tp = world if (world > 1 and args.parallel == "tp") else 1
     return ExperimentConfig(
-        tp_size=tp,
+        tp_size=tp, precision=args.precision, correct_precision=args.precision,
         exp_id="bench", model_name="dinov3_segmentor_linhead", batch_size=args.batch,
         image_shape=(args.res, args.res, 3), input_profile_name="dinov3_ade20k_linhead_official",
         input_profile_kwargs={"backbone_arch": args.arch, "server_inference_mode": "whole"},
@@ -402,7 +405,7 @@ def main():
     cfg_out = {"model": "DINOv3 ViT-7B/16 + linear seg head (150 cls)" if args.arch == "vit7b16" else args.arch,
                "global_batch": images_per_step, "per_gpu_batch": args.batch, "seq_len": (args.res // 16) ** 2 + 5,
                "image": f"{args.res}x{args.res}", "keep_ratio": args.keep, "pyramid_levels": [1, 0],
-               "parallelism": parallelism,
+               "parallelism": parallelism, "precision": args.precision if args.impl == "mine" else "bf16",
                "l2": "working set > L2 each step (13.4 GB bf16 weights + 8 GB K/V/increment caches)"}
     if args.impl == "reference":
         try:
@@ -434,7 +437,10 @@ def main():
                 "p99_ms": round(per_step[min(len(per_step) - 1, int(0.99 * len(per_step)))], 3),
                 "higher_is_better": True, "scaling": "strong" if parallelism.startswith("tp") else "weak",
                 "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
-                "dtype": "bf16", "data": "synthetic images (clipped N(128,60^2)), random-init weights",
+                "dtype": ("bf16" if args.precision == "bf16" else
+                          "fp8-e4m3 GEMM operands (per-row activation / per-channel weight scales, fp32 "
+                          "accumulate), bf16 attention and residual stream"),
+                "data": "synthetic images (clipped N(128,60^2)), random-init weights",
                 "config": cfg_out, "gpu_launches": int(launches * args.steps), "clocks": clk, "e2e": e2e}
         print(json.dumps(line))
     if world > 1:

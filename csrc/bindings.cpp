@@ -36,10 +36,15 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
              optional<Tensor> aux_rows, int64_t aux_mode, optional<Tensor> resid2, optional<Tensor> q_out,
              optional<Tensor> k_out, optional<Tensor> v_out, optional<Tensor> kv_rows,
              optional<Tensor> tok_idx, int64_t seq_len, optional<Tensor> rope_sin, optional<Tensor> rope_cos,
-             int64_t n_prefix, int64_t head_dim, int64_t max_ctas) {
+             int64_t n_prefix, int64_t head_dim, int64_t max_ctas, optional<Tensor> a_scale,
+             optional<Tensor> b_scale, int64_t kv_dim) {
   check_cuda(A, "A");
   check_cuda(B, "B");
-  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm expects bf16 operands");
+  const bool fp8 = A.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK((A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16) ||
+                  (fp8 && B.scalar_type() == at::kFloat8_e4m3fn),
+              "gemm expects bf16 x bf16 or e4m3 x e4m3 operands");
+  TORCH_CHECK(fp8 == (a_scale.has_value() && b_scale.has_value()), "e4m3 operands need a_scale [M] and b_scale [N]");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm: A [M,K], B [N,K]");
   TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm operands must have unit inner stride");
   TORCH_CHECK(err.scalar_type() == at::kInt && err.is_cuda(), "err must be a CUDA int32 tensor");
@@ -47,7 +52,14 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
   const int M = static_cast<int>(A.size(0));
   const int K = static_cast<int>(A.size(1));
   int N = static_cast<int>(B.size(0));
-  TORCH_CHECK(K % 8 == 0, "gemm: K must be a multiple of 8");
+  TORCH_CHECK(K % (fp8 ? 16 : 8) == 0, "gemm: K rows must be a multiple of 16 bytes");
+  if (fp8) {
+    TORCH_CHECK(a_scale->scalar_type() == at::kFloat && a_scale->is_contiguous() && a_scale->numel() >= M,
+                "a_scale: fp32 [M]");
+    TORCH_CHECK(b_scale->scalar_type() == at::kFloat && b_scale->is_contiguous() && b_scale->numel() >= N &&
+                    (reinterpret_cast<uintptr_t>(b_scale->data_ptr()) & 15) == 0,
+                "b_scale: fp32 [N], 16-byte aligned");
+  }
   for (auto* t : {&out_rows, &resid_rows, &aux_rows, &kv_rows, &tok_idx}) check_rows_i32(*t, "row map");
   GemmEpilogue ep{};
   ep.out = opt_ptr(out);
@@ -75,12 +87,23 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
   ep.rope_cos = opt_ptr<const float>(rope_cos);
   ep.n_prefix = static_cast<int>(n_prefix);
   ep.head_dim = static_cast<int>(head_dim);
+  ep.a_scale = fp8 ? a_scale->data_ptr<float>() : nullptr;
+  ep.b_scale = fp8 ? b_scale->data_ptr<float>() : nullptr;
   if (epi == EPI_QKV) {
     TORCH_CHECK(q_out && k_out && v_out, "qkv epilogue needs q_out, k_out, v_out");
-    TORCH_CHECK(N % 3 == 0, "qkv weight rows must be 3*dim");
-    ep.dim = N / 3;
+    if (kv_dim > 0) {  // grouped-query: rows are [q (dim) | k (kv_dim) | v (kv_dim)]
+      ep.dim = N - 2 * static_cast<int>(kv_dim);
+      ep.kv_dim = static_cast<int>(kv_dim);
+      TORCH_CHECK(ep.dim > 0, "qkv: kv_dim too large");
+      TORCH_CHECK(k_out->stride(0) == v_out->stride(0), "qkv: k_out and v_out need one row stride");
+      ep.ld_kv = k_out->stride(0);
+    } else {
+      TORCH_CHECK(N % 3 == 0, "qkv weight rows must be 3*dim");
+      ep.dim = N / 3;
+    }
     const int tile_n = bn == 512 ? 256 : static_cast<int>(bn);  // bn 512 = 2-CTA 256x256 tile
-    TORCH_CHECK(ep.dim % tile_n == 0, "qkv: dim must be a multiple of the tile width");
+    TORCH_CHECK(ep.dim % tile_n == 0 && (ep.kv_dim == 0 || ep.kv_dim % tile_n == 0),
+                "qkv: q and kv widths must be multiples of the tile width");
     TORCH_CHECK(head_dim == 64 || head_dim == 128, "qkv: head_dim must be 64 or 128");
     TORCH_CHECK(tile_n % head_dim == 0, "qkv: tile width must be a multiple of head_dim");
     TORCH_CHECK(tok_idx.has_value() || seq_len > 0, "qkv: need tok_idx or seq_len");
@@ -98,7 +121,7 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
   }
   if (M == 0) return;
   gemm_dispatch(static_cast<int>(epi), static_cast<int>(bn), A, B, M, N, K, ep, err.data_ptr<int>(),
-                static_cast<int>(max_ctas));
+                static_cast<int>(max_ctas), fp8);
 }
 
 }  // namespace appcorr
@@ -113,7 +136,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("resid2") = py::none(), py::arg("q_out") = py::none(), py::arg("k_out") = py::none(),
         py::arg("v_out") = py::none(), py::arg("kv_rows") = py::none(), py::arg("tok_idx") = py::none(),
         py::arg("seq_len") = 0, py::arg("rope_sin") = py::none(), py::arg("rope_cos") = py::none(),
-        py::arg("n_prefix") = 0, py::arg("head_dim") = 128, py::arg("max_ctas") = 0);
+        py::arg("n_prefix") = 0, py::arg("head_dim") = 128, py::arg("max_ctas") = 0,
+        py::arg("a_scale") = py::none(), py::arg("b_scale") = py::none(), py::arg("kv_dim") = 0);
   m.attr("EPI_BF16") = static_cast<int>(EPI_BF16);
   m.attr("EPI_F32") = static_cast<int>(EPI_F32);
   m.attr("EPI_GELU") = static_cast<int>(EPI_GELU);

@@ -21,6 +21,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cfloat>
+#include <cuda_fp8.h>
 
 #include "sm100_common.cuh"
 #include "ops.h"
@@ -67,10 +68,22 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 constexpr int kLnThreads = 128;
 constexpr int kLnMaxVec = 8;
 
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+
+// e4m3 row quantisation of 8 values per vector slot: q = y / scale, scale = amax / 448.
+constexpr float kE4m3Max = 448.f;
+
+// FP8 = true: the normalised row is emitted as e4m3 (out8, stride ldo bytes) with one fp32
+// scale per row (scale8[r]) instead of bf16, ready for the e4m3 GEMM.
+template <bool FP8>
 __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
     const bf16* __restrict__ x, long ldx, const int* __restrict__ rows, const bf16* __restrict__ w,
     const bf16* __restrict__ b, float eps, bf16* __restrict__ out, long ldo, bf16* __restrict__ copy_out,
-    long ldc, int D, int nrows) {
+    long ldc, int D, int nrows, uint8_t* __restrict__ out8, float* __restrict__ scale8) {
   __shared__ float red[kLnThreads / 32];
   const int r = blockIdx.x;
   if (r >= nrows) return;
@@ -106,9 +119,9 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
     }
   }
   const float rstd = rsqrtf(block_sum<kLnThreads>(q, red) / D + eps);
-  uint4* orow = reinterpret_cast<uint4*>(out + (long)r * ldo);
   const uint4* wv = reinterpret_cast<const uint4*>(w);
   const uint4* bv = reinterpret_cast<const uint4*>(b);
+  float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < kLnMaxVec; ++i) {
     const int c = threadIdx.x + i * kLnThreads;
@@ -116,21 +129,100 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
       uint4 wu = __ldg(wv + c), bu = __ldg(bv + c);
       const uint32_t* wp = &wu.x;
       const uint32_t* bp = &bu.x;
-      uint32_t o[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float2 ww = unpack_bf16x2(wp[j]), bb = unpack_bf16x2(bp[j]);
-        const float y0 = (v[i][2 * j] - mean) * rstd * ww.x + bb.x;
-        const float y1 = (v[i][2 * j + 1] - mean) * rstd * ww.y + bb.y;
-        o[j] = pack_bf16x2(y0, y1);
+        // the bf16 rounding matches the bf16 path, so both precisions quantise the same values
+        v[i][2 * j] = bf16_round((v[i][2 * j] - mean) * rstd * ww.x + bb.x);
+        v[i][2 * j + 1] = bf16_round((v[i][2 * j + 1] - mean) * rstd * ww.y + bb.y);
+        amax = fmaxf(amax, fmaxf(fabsf(v[i][2 * j]), fabsf(v[i][2 * j + 1])));
       }
-      orow[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  if constexpr (FP8) {
+    amax = block_max<kLnThreads>(amax, red);
+    const float sc = fmaxf(amax, 1e-12f) / kE4m3Max;
+    const float inv = 1.f / sc;
+    if (threadIdx.x == 0) scale8[r] = sc;
+    uint2* orow = reinterpret_cast<uint2*>(out8 + (long)r * ldo);
+#pragma unroll
+    for (int i = 0; i < kLnMaxVec; ++i) {
+      const int c = threadIdx.x + i * kLnThreads;
+      if (c < nvec)
+        orow[c] = make_uint2(pack_e4m3x4(v[i][0] * inv, v[i][1] * inv, v[i][2] * inv, v[i][3] * inv),
+                             pack_e4m3x4(v[i][4] * inv, v[i][5] * inv, v[i][6] * inv, v[i][7] * inv));
+    }
+  } else {
+    uint4* orow = reinterpret_cast<uint4*>(out + (long)r * ldo);
+#pragma unroll
+    for (int i = 0; i < kLnMaxVec; ++i) {
+      const int c = threadIdx.x + i * kLnThreads;
+      if (c < nvec)
+        orow[c] = make_uint4(pack_bf16x2(v[i][0], v[i][1]), pack_bf16x2(v[i][2], v[i][3]),
+                             pack_bf16x2(v[i][4], v[i][5]), pack_bf16x2(v[i][6], v[i][7]));
     }
   }
 }
 
+// bf16 rows -> e4m3 rows + one fp32 scale per row (amax / 448). One CTA per row, K <= 8192.
+__global__ void __launch_bounds__(kLnThreads) quant_rows_e4m3_kernel(const bf16* __restrict__ x, long ldx,
+                                                                     uint8_t* __restrict__ out, long ldo,
+                                                                     float* __restrict__ scale, int K) {
+  __shared__ float red[kLnThreads / 32];
+  const int r = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (long)r * ldx);
+  const int nvec = K >> 3;
+  uint4 u[kLnMaxVec];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int c = threadIdx.x + i * kLnThreads;
+    if (c < nvec) {
+      u[i] = xr[c];
+      const uint32_t* p = &u[i].x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(p[j]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  }
+  amax = block_max<kLnThreads>(amax, red);
+  const float sc = fmaxf(amax, 1e-12f) / kE4m3Max;
+  const float inv = 1.f / sc;
+  if (threadIdx.x == 0) scale[r] = sc;
+  uint2* orow = reinterpret_cast<uint2*>(out + (long)r * ldo);
+#pragma unroll
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int c = threadIdx.x + i * kLnThreads;
+    if (c < nvec) {
+      const uint32_t* p = &u[i].x;
+      const float2 a = unpack_bf16x2(p[0]), b = unpack_bf16x2(p[1]), cc = unpack_bf16x2(p[2]), d = unpack_bf16x2(p[3]);
+      orow[c] = make_uint2(pack_e4m3x4(a.x * inv, a.y * inv, b.x * inv, b.y * inv),
+                           pack_e4m3x4(cc.x * inv, cc.y * inv, d.x * inv, d.y * inv));
+    }
+  }
+}
+
+void quant_rows_e4m3_op(const at::Tensor& x, at::Tensor& out, at::Tensor& scale) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
+              "quant_rows_e4m3: bf16 [M,K] CUDA x");
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1));
+  TORCH_CHECK(K % 16 == 0 && K <= kLnThreads * kLnMaxVec * 8, "quant_rows_e4m3: K % 16 == 0 and K <= 8192");
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && out.size(0) >= M && out.size(1) == K && out.stride(1) == 1,
+              "quant_rows_e4m3: out e4m3 [M,K]");
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.numel() >= M, "quant_rows_e4m3: scale fp32 [M]");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && out.stride(0) % 16 == 0, "quant_rows_e4m3: 16-byte aligned rows");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard g(x.device());
+  quant_rows_e4m3_kernel<<<M, kLnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), reinterpret_cast<uint8_t*>(out.data_ptr()),
+      out.stride(0), scale.data_ptr<float>(), K);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at::Tensor& w, const at::Tensor& b,
-                  double eps, at::Tensor& out, c10::optional<at::Tensor> copy_out) {
+                  double eps, at::Tensor& out, c10::optional<at::Tensor> copy_out, c10::optional<at::Tensor> scale8) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "layernorm: bf16 CUDA x");
   const int D = static_cast<int>(x.size(-1));
   TORCH_CHECK(D % 8 == 0 && D <= kLnThreads * kLnMaxVec * 8, "layernorm: D % 8 == 0 and D <= 8192");
@@ -150,12 +242,26 @@ void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at:
     cp = reinterpret_cast<bf16*>(copy_out->data_ptr());
     ldc = copy_out->stride(0);
   }
+  const bool fp8 = out.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK(fp8 || out.scalar_type() == at::kBFloat16, "layernorm: out bf16 or e4m3");
+  TORCH_CHECK(fp8 == scale8.has_value(), "layernorm: e4m3 output needs scale8 [nrows]");
+  if (fp8) {
+    TORCH_CHECK(scale8->scalar_type() == at::kFloat && scale8->numel() >= nrows, "layernorm: scale8 fp32 [nrows]");
+    TORCH_CHECK(out.stride(0) % 8 == 0, "layernorm: e4m3 rows must be 8-byte aligned");
+  }
   if (nrows == 0) return;
   c10::cuda::CUDAGuard g(x.device());
-  layernorm_kernel<<<nrows, kLnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
-      reinterpret_cast<const bf16*>(b.data_ptr()), static_cast<float>(eps), reinterpret_cast<bf16*>(out.data_ptr()),
-      out.stride(0), cp, ldc, D, nrows);
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (fp8)
+    layernorm_kernel<true><<<nrows, kLnThreads, 0, st>>>(
+        reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
+        reinterpret_cast<const bf16*>(b.data_ptr()), static_cast<float>(eps), nullptr, out.stride(0), cp, ldc, D,
+        nrows, reinterpret_cast<uint8_t*>(out.data_ptr()), scale8->data_ptr<float>());
+  else
+    layernorm_kernel<false><<<nrows, kLnThreads, 0, st>>>(
+        reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
+        reinterpret_cast<const bf16*>(b.data_ptr()), static_cast<float>(eps), reinterpret_cast<bf16*>(out.data_ptr()),
+        out.stride(0), cp, ldc, D, nrows, nullptr, nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -702,7 +808,8 @@ void register_elementwise_ops(pybind11::module_& m) {
   m.def("head_mean", &head_mean_op);
   namespace py = pybind11;
   m.def("layernorm", &layernorm_op, py::arg("x"), py::arg("rows"), py::arg("w"), py::arg("b"), py::arg("eps"),
-        py::arg("out"), py::arg("copy_out") = py::none());
+        py::arg("out"), py::arg("copy_out") = py::none(), py::arg("scale8") = py::none());
+  m.def("quant_rows_e4m3", &quant_rows_e4m3_op, py::arg("x"), py::arg("out"), py::arg("scale"));
   m.def("add_", &add_inplace_op);
   m.def("patch_im2col", &patch_im2col_op);
   m.def("set_prefix", &set_prefix_op);

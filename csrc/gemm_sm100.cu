@@ -110,11 +110,25 @@ __device__ __forceinline__ void add_bias(float (&v)[32], const __nv_bfloat16* bi
   for (int j = 0; j < 32; ++j) v[j] += b[j];
 }
 
+// FP8 operands: fold the per-row activation scale and per-column weight scale into the accumulator.
+__device__ __forceinline__ void scale_acc(float (&v)[32], const GemmEpilogue& ep, float row_scale, int n) {
+  if (ep.a_scale == nullptr) return;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 w = __ldg(reinterpret_cast<const float4*>(ep.b_scale + n) + i);
+    v[4 * i + 0] *= row_scale * w.x;
+    v[4 * i + 1] *= row_scale * w.y;
+    v[4 * i + 2] *= row_scale * w.z;
+    v[4 * i + 3] *= row_scale * w.w;
+  }
+}
+
 // Epilogue for one 128 x BN accumulator; each thread owns one row (`m`, possibly >= M).
 template <int BN, int EPI>
 __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, const GemmShape& shp,
                                              const GemmEpilogue& ep) {
   const bool row_ok = m < shp.M;
+  const float rs = (ep.a_scale != nullptr && row_ok) ? ep.a_scale[m] : 1.f;
   if constexpr (EPI == EPI_SWIGLU) {
     // Tile columns [0,BN/2) hold w1 rows, [BN/2,BN) the matching w2 rows.
     constexpr int H = BN / 2;
@@ -130,6 +144,8 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
       float a[32], g[32];
       acc_to_float(r1, a);
       acc_to_float(r2, g);
+      scale_acc(a, ep, rs, n0 + c * 32);
+      scale_acc(g, ep, rs, n0 + H + c * 32);
       add_bias(a, ep.bias, n0 + c * 32);
       add_bias(g, ep.bias, n0 + H + c * 32);
       float h[32];
@@ -142,8 +158,10 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
       store_bf16x32(reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + nout0 + c * 32, h);
     }
   } else if constexpr (EPI == EPI_QKV) {
-    const int which = n0 / ep.dim;          // 0 = q, 1 = k, 2 = v (tiles never straddle)
-    const int c0 = n0 - which * ep.dim;     // column inside q / k / v
+    const int kvd = ep.kv_dim > 0 ? ep.kv_dim : ep.dim;
+    const int which = n0 < ep.dim ? 0 : (n0 < ep.dim + kvd ? 1 : 2);  // q / k / v (tiles never straddle)
+    const int c0 = which == 0 ? n0 : (which == 1 ? n0 - ep.dim : n0 - ep.dim - kvd);
+    const long ldkv = ep.ld_kv > 0 ? ep.ld_kv : ep.ld_qkv;
     int tok = 0, kvrow = 0;
     if (row_ok) {
       tok = ep.tok_idx ? ep.tok_idx[m] : (m % ep.seq_len);
@@ -152,8 +170,8 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
     __nv_bfloat16* dst = nullptr;
     if (row_ok) {
       if (which == 0) dst = ep.q_out + (long)m * ep.ld_qkv;
-      else if (which == 1) dst = ep.k_out + (long)kvrow * ep.ld_qkv;
-      else dst = ep.v_out + (long)kvrow * ep.ld_qkv;
+      else if (which == 1) dst = ep.k_out + (long)kvrow * ldkv;
+      else dst = ep.v_out + (long)kvrow * ldkv;
       if (kvrow < 0 && which != 0) dst = nullptr;
     }
     if (which == 2) {
@@ -165,6 +183,7 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
         if (dst == nullptr) continue;
         float v[32];
         acc_to_float(r, v);
+        scale_acc(v, ep, rs, n0 + c * 32);
         add_bias(v, ep.bias, n0 + c * 32);
         store_bf16x32(dst + c0 + c * 32, v);
       }
@@ -185,6 +204,8 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
           float lo[32], hi[32];
           acc_to_float(rl, lo);
           acc_to_float(rh, hi);
+          scale_acc(lo, ep, rs, n0 + hb + c);
+          scale_acc(hi, ep, rs, n0 + hb + half + c);
           add_bias(lo, ep.bias, n0 + hb + c);
           add_bias(hi, ep.bias, n0 + hb + half + c);
           if (rope) {
@@ -230,6 +251,7 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
       if (orow < 0 || n >= shp.N) continue;
       float v[32];
       acc_to_float(r, v);
+      scale_acc(v, ep, rs, n);
       add_bias(v, ep.bias, n);
       if constexpr (EPI == EPI_F32) {
         store_f32x32(reinterpret_cast<float*>(ep.out) + (long)orow * ep.ldo + n, v);
@@ -273,7 +295,23 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
   }
 }
 
-template <int BN, int STAGES, int EPI>
+// KIND 0: bf16 x bf16 (kind::f16, 64-element K blocks); KIND 1: e4m3 x e4m3 (kind::f8f6f4,
+// 128-element K blocks). Both stage 128-byte rows, so the shared-memory layout is identical.
+__device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+template <int BN, int STAGES, int EPI, int KIND = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmShape shp, GemmEpilogue ep) {
@@ -281,7 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t B_BYTES = BN * kBK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = TmemCols<BN>::value;
-  constexpr uint32_t IDESC = idesc_bf16_f32(kBM, BN);
+  constexpr uint32_t IDESC = KIND == 1 ? idesc_e4m3_f32(kBM, BN) : idesc_bf16_f32(kBM, BN);
+  constexpr int BKE = KIND == 1 ? 128 : kBK;  // K elements per stage (128 bytes per row)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -318,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int num_m = (shp.M + kBM - 1) / kBM;
   const int num_n = (shp.N + BN - 1) / BN;
-  const int KB = (shp.K + kBK - 1) / kBK;
+  const int KB = (shp.K + BKE - 1) / BKE;
   const int total = num_m * num_n;
 
   if (warp == 0) {
@@ -333,8 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb = smem_addr(&full[s]);
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
-          tma_load_2d(sa, &tmA, fb, kb * kBK, mb * kBM);
-          tma_load_2d(sa + A_BYTES, &tmB, fb, kb * kBK, nb * BN);
+          tma_load_2d(sa, &tmA, fb, kb * BKE, mb * kBM);
+          tma_load_2d(sa + A_BYTES, &tmB, fb, kb * BKE, nb * BN);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
       }
@@ -364,9 +403,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            umma_f16(d_tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
-                     (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {  // 4 MMAs of 32 bytes of K per 128-byte stage row
+            if constexpr (KIND == 1)
+              umma_f8(d_tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
+                      (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f16(d_tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
+                       (kb | k) != 0 ? 1u : 0u);
           }
           issued = true;
           umma_commit(smem_addr(&empty[s]));
@@ -587,6 +630,21 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, int64_t rows, int64_t cols, int64
   return m;
 }
 
+CUtensorMap make_tmap_u8_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK(ld % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (u8) failed: ", static_cast<int>(r));
+  return m;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -597,19 +655,25 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, int KIND = 0>
 void launch_gemm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const GemmEpilogue& ep,
                  int* err, int max_ctas, cudaStream_t stream) {
   constexpr uint32_t STAGE_BYTES = (kBM + BN) * kBK * 2;
   constexpr size_t SMEM = STAGES * STAGE_BYTES + 1024 + 256;
-  auto kern = gemm_bf16_tn_kernel<BN, STAGES, EPI>;
+  auto kern = gemm_bf16_tn_kernel<BN, STAGES, EPI, KIND>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM));
     configured = true;
   }
-  CUtensorMap ta = make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), kBM, kBK);
-  CUtensorMap tb = make_tmap_bf16_2d(B.data_ptr(), B.size(0), K, B.stride(0), BN, kBK);
+  CUtensorMap ta, tb;
+  if constexpr (KIND == 1) {
+    ta = make_tmap_u8_2d(A.data_ptr(), M, K, A.stride(0), kBM, 128);
+    tb = make_tmap_u8_2d(B.data_ptr(), B.size(0), K, B.stride(0), BN, 128);
+  } else {
+    ta = make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), kBM, kBK);
+    tb = make_tmap_bf16_2d(B.data_ptr(), B.size(0), K, B.stride(0), BN, kBK);
+  }
   GemmShape shp{M, N, K, err};
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
@@ -651,8 +715,37 @@ void launch_gemm_2sm(const at::Tensor& A, const at::Tensor& B, int M, int N, int
 }
 
 // Dispatch on (epilogue, BN). STAGES chosen to fill ~192 KB of shared memory.
+void gemm_dispatch_fp8(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
+                       const GemmEpilogue& ep, int* err, int max_ctas) {
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(bn == 256 || bn == 128, "fp8 gemm: BN 128 or 256");
+  switch (epi) {
+#define APPCORR_GEMM8_CASE(E)                                                                     \
+  case E:                                                                                         \
+    if (bn == 256) launch_gemm<256, 4, E, 1>(A, B, M, N, K, ep, err, max_ctas, st);               \
+    else launch_gemm<128, 6, E, 1>(A, B, M, N, K, ep, err, max_ctas, st);                         \
+    break;
+    APPCORR_GEMM8_CASE(EPI_BF16)
+    APPCORR_GEMM8_CASE(EPI_F32)
+    APPCORR_GEMM8_CASE(EPI_GELU)
+    APPCORR_GEMM8_CASE(EPI_RESID)
+    APPCORR_GEMM8_CASE(EPI_QKV)
+#undef APPCORR_GEMM8_CASE
+    case EPI_SWIGLU:
+      TORCH_CHECK(bn == 256, "swiglu epilogue uses BN=256");
+      launch_gemm<256, 4, EPI_SWIGLU, 1>(A, B, M, N, K, ep, err, max_ctas, st);
+      break;
+    default:
+      TORCH_CHECK(false, "unknown epilogue ", epi);
+  }
+}
+
 void gemm_dispatch(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
-                   const GemmEpilogue& ep, int* err, int max_ctas) {
+                   const GemmEpilogue& ep, int* err, int max_ctas, bool fp8) {
+  if (fp8) {
+    gemm_dispatch_fp8(epi, bn, A, B, M, N, K, ep, err, max_ctas);
+    return;
+  }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
 #define APPCORR_GEMM_CASE(E)                                                              \
   case E:                                                                                 \

@@ -36,7 +36,12 @@ struct GemmEpilogue {
   const float* rope_cos;
   int n_prefix;
   int head_dim;
-  int dim;
+  int dim;             // q width (= k/v width unless kv_dim is set)
+  int kv_dim;          // k / v width (grouped-query attention); 0: same as dim
+  long ld_kv;          // row stride of k_out / v_out (0: ld_qkv)
+  // FP8 operands: acc * a_scale[m] * b_scale[n] before the epilogue (nullptr: no scaling)
+  const float* a_scale;
+  const float* b_scale;
 };
 
 struct GemmShape {
@@ -46,9 +51,10 @@ struct GemmShape {
 
 
 void gemm_dispatch(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
-                   const GemmEpilogue& ep, int* err, int max_ctas);
+                   const GemmEpilogue& ep, int* err, int max_ctas, bool fp8);
 CUtensorMap make_tmap_bf16_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
                               int box_cols);
+CUtensorMap make_tmap_u8_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols);
 int num_sms();
 void register_elementwise_ops(pybind11::module_& m);
 void register_attention_ops(pybind11::module_& m);

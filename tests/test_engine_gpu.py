@@ -141,3 +141,39 @@ def test_detr_decoder_gpu_matches_module():
     torch.cuda.synchronize()
     assert _rel(out["pred_logits"], ref["pred_logits"]) < 3e-2
     assert _rel(out["pred_boxes"], ref["pred_boxes"]) < 2e-2
+
+
+@pytest.mark.parametrize("name,over", CASES)
+def test_engine_fp8_tracks_oracle(name, over):
+    """e4m3 activations x e4m3 weights (fp32 accumulate): approx and correct passes stay close
+    to the fp32 oracle, and the correction pass of the full token set still recovers the
+    image's true forward."""
+    from appcorr_b200.models.engine import ViTEngine
+
+    torch.manual_seed(2)
+    m = _model(name, **over)
+    eng = ViTEngine.from_module(m, DEV, precision="fp8")
+    B, H, W = 2, 96, 128
+    img = torch.randint(0, 256, (B, H, W, 3), dtype=torch.uint8, device=DEV)
+    sess = eng.new_session(B, H, W)
+    eng.prepare_tokens(sess, img)
+    with torch.no_grad():
+        x_ref, (gh, gw) = m.prepare_tokens_with_masks(_float_img(img))
+        x = eng.approx(sess, 0, len(m.blocks)).clone()
+        rope = m.rope_embed(H=gh, W=gw)
+        cache = {}
+        xr = x_ref
+        for i, blk in enumerate(m.blocks):
+            xr, cache = blk.approx(xr, rope, cache, f"layer{i}")
+    torch.cuda.synchronize()
+    assert _rel(x.view(B, -1, m.embed_dim), xr) < 6e-2
+    for i in range(len(m.blocks)):
+        assert _rel(sess.pscore[i], cache[f"layer{i}_server_pscore"]) < 5e-2
+    # correction with every patch token kept == full forward on the same image
+    npre = m.n_storage_tokens + 1
+    N = sess.N
+    pre = torch.arange(npre, device=DEV, dtype=torch.int32)[None].repeat(B, 1).contiguous()
+    cand = torch.arange(npre, N, device=DEV, dtype=torch.int32)[None].repeat(B, 1).contiguous()
+    xc = eng.correct(sess, 0, len(m.blocks), pre, cand, {"token_keep_ratio": 1.0})
+    torch.cuda.synchronize()
+    assert _rel(xc.view(B, -1, m.embed_dim), xr) < 6e-2
