@@ -80,14 +80,19 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
                n_prefix=n_prefix, head_dim=head_dim, a_scale=a_scale, b_scale=b_scale, kv_dim=kv_dim)
 
 
-def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, out: torch.Tensor,
+def layernorm(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], eps: float, out: torch.Tensor,
               rows: Optional[torch.Tensor] = None, copy_out: Optional[torch.Tensor] = None,
-              scale8: Optional[torch.Tensor] = None) -> torch.Tensor:
+              scale8: Optional[torch.Tensor] = None, rms: bool = False) -> torch.Tensor:
     """out[i] = LN(x[rows[i]]) (rows=None: every row). copy_out[i] receives the raw gathered row.
-    An e4m3 `out` receives the bf16-rounded LN row divided by scale8[i] = amax_i / 448."""
+    An e4m3 `out` receives the bf16-rounded LN row divided by scale8[i] = amax_i / 448.
+    rms=True: RMSNorm x * rsqrt(mean(x^2) + eps) * w (b must be None)."""
     _count()
-    lib().layernorm(x, rows, w, b, float(eps), out, copy_out, scale8)
+    lib().layernorm(x, rows, w, b, float(eps), out, copy_out, scale8, rms)
     return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor, **kw) -> torch.Tensor:
+    return layernorm(x, w, None, eps, out, rms=True, **kw)
 
 
 def quant_rows_e4m3(x: torch.Tensor, out: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
@@ -118,33 +123,51 @@ ATTENTION_IMPL = ["tcgen05"]  # "tcgen05" (sm_100a tensor cores + TMEM) or "mma"
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, *, B: int, Tq: int,
               Tk: int, H: int, Dh: int, scale: Optional[float] = None,
               lse: Optional[torch.Tensor] = None, impl: Optional[str] = None,
-              cls_probs: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Non-causal attention on BTHD tensors: q/o [B*Tq, H*Dh], k/v [B*Tk, H*Dh].
+              cls_probs: Optional[torch.Tensor] = None, Hkv: int = 0, causal: bool = False,
+              q_pos: Optional[torch.Tensor] = None, block_table: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention on BTHD tensors: q/o [B*Tq, H*Dh], k/v [B*Tk, Hkv*Dh].
 
     cls_probs (tcgen05 path): fp32 [B, H, Tk] receives the softmax row of query 0 (the CLS
     token) of every (batch, head), computed in the same pass.
+    Hkv: key/value heads (grouped-query attention; 0 = H). causal: query row i sees keys up to
+    q_pos[i] (int32 [B*Tq]; default i + Tk - Tq), so a packed, non-contiguous query set attends
+    with its own causal frontier. block_table: int32 [B, blocks] of 128-row pages in a paged
+    K/V pool (k/v are then the pools).
     """
     if scale is None:
         scale = Dh ** -0.5
     impl = impl or ATTENTION_IMPL[0]
+    if Hkv or causal or q_pos is not None or block_table is not None:
+        impl = "tcgen05"
     _count()
     if impl == "tcgen05":
-        lib().attention_sm100(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse, err_word(q.device), cls_probs)
+        lib().attention_sm100(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse, err_word(q.device), cls_probs,
+                              Hkv, causal, q_pos, block_table)
     else:
         lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
     return o
 
 
 def patch_im2col(img: torch.Tensor, patch: int, out: torch.Tensor,
-                 mean: Sequence[float] = IMAGENET_MEAN, std: Sequence[float] = IMAGENET_STD) -> torch.Tensor:
+                 mean: Sequence[float] = IMAGENET_MEAN, std: Sequence[float] = IMAGENET_STD,
+                 perm: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """uint8 [B,H,W,3] -> normalised patch rows [B*P, >= 3*p*p] (pad columns untouched); row r of
+    an image holds patch perm[r] (row-major patch index) when perm is given."""
     _count()
-    lib().patch_im2col(img, patch, list(mean), list(std), out)
+    lib().patch_im2col(img, patch, list(mean), list(std), out, perm)
     return out
 
 
 def set_prefix(x: torch.Tensor, prefix: torch.Tensor, B: int, N: int) -> None:
     _count()
     lib().set_prefix(x, prefix, B, N)
+
+
+def row_sqdist(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[r] = ||a[r] - b[r]||^2 (fp32)."""
+    _count()
+    lib().row_sqdist(a, b, out)
+    return out
 
 
 def gather_rows(src: torch.Tensor, rows: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

@@ -56,6 +56,9 @@ def parse_args():
     ap.add_argument("--precision", default="fp8", choices=["bf16", "fp8"],
                     help="GEMM operand precision of the approx and correct passes (ours; the reference arm "
                          "runs its default bf16 path: its fp8/fp4 approx controllers need torchao)")
+    ap.add_argument("--workload", default="vit7b_seg", choices=["vit7b_seg", "vlm"],
+                    help="vit7b_seg: the headline ViT-7B linear-head segmentation config; vlm: Qwen2.5-VL-7B-shaped "
+                         "prefill with KV rewrite (1 image 1024^2 + 128 text tokens, keep 0.25; ranks data-parallel)")
     ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
                     help="N > 1: tensor-parallel over N GPUs (one request batch) or N data-parallel replicas")
     return ap.parse_args()
@@ -288,6 +291,107 @@ def run_mine(args, rank, world):
     return ms_max, per_step, launches_per_step, clk, e2e
 
 
+# ----------------------------------------------------------------------------- VLM workload
+def run_vlm(args, rank, world):
+    """Qwen2.5-VL-shaped prefill: approx round on the pyramid base, correction round with the
+    full image (K/V rewrite of the top 25% image tokens + the text), first token. One request
+    per rank per step (data parallel)."""
+    import torch
+
+    sys.path.insert(0, ROOT)
+    from appcorr_b200.common.protocol import ExperimentConfig, Task
+    from appcorr_b200.ops import kernels as K
+    from appcorr_b200.ops.native import check_errors
+    from appcorr_b200.server.model import PyramidBatch, get_model_executor
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    res = 1024
+    cfg = ExperimentConfig(
+        exp_id="bench_vlm", model_name="qwen25vl", batch_size=1, image_shape=(res, res, 3),
+        input_profile_kwargs={"vlm_arch": "qwen25vl7b", "n_text": 128, "n_text_before": 16, "seed": 0},
+        scheduler_policy_name="GroupTrigger", transmission_policy_name="ProgressiveLaplacian",
+        transmission_kwargs={"pyramid_levels": [1, 0], "num_groups": 1, "grouping_strategy": "grid"},
+        appcorr_kwargs={"token_keep_ratio": 0.25})
+    ex = get_model_executor("qwen25vl", dev)
+    ex.load_model("qwen25vl", cfg)
+    _, base, resid = synthetic_pyramid(1, res, seed=rank)
+    base_h = torch.from_numpy(base).pin_memory()
+    res_h = torch.from_numpy(resid).pin_memory()
+    task = Task(task_id=0, request_id=0, payload=[], instructions=[])
+
+    def step(b, r, ctx):
+        ex.preprocess(PyramidBatch(b, None), task, ctx, cfg)
+        ex.prepare_tokens(task, ctx, cfg)
+        ex.approx_forward({}, ctx, cfg)
+        ex.preprocess(PyramidBatch(b, r), task, ctx, cfg)
+        ex.prepare_tokens(task, ctx, cfg)
+        ex.correct_forward({}, ctx, cfg)
+        ex.head_inference(task, ctx, cfg)
+
+    base_d, res_d = base_h.to(dev), res_h.to(dev)
+    ctx = {}
+    for _ in range(args.warmup):
+        step(base_d, res_d, ctx)
+    torch.cuda.synchronize()
+    check_errors(dev)
+    n0 = K.LAUNCHES[0]
+    step(base_d, res_d, ctx)
+    launches = K.LAUNCHES[0] - n0
+    clocks = ClockSampler() if rank == 0 else None
+    torch.cuda.synchronize()
+    barrier(world)
+    if clocks:
+        clocks.start()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    ev[0].record()
+    for i in range(args.steps):
+        step(base_d, res_d, ctx)
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop(None) if clocks else None
+    check_errors(dev)
+    ms = max_over_ranks(ev[0].elapsed_time(ev[-1]) / args.steps, world)
+    per = sorted(ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps))
+    e2e = None
+    if not args.no_e2e:
+        ctx2 = {}
+
+        def e2e_step():
+            step(base_h, res_h, ctx2)
+            return ex.get_final_results(task, ctx2, cfg)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(3, args.steps)
+        e0.record()
+        for _ in range(n):
+            out = e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / n, world)
+        assert "first_token" in out[0]
+        e2e = {"value": round(world * 1e3 / e2e_ms, 3), "unit": "requests/s",
+               "h2d_bytes_per_step": int(base_h.numel() + res_h.numel() * 2), "d2h_bytes_per_step": 8,
+               "ms_per_step": round(e2e_ms, 3)}
+    if rank == 0:
+        c = ex.cfg
+        print(json.dumps({
+            "metric": "VLM prefill approx+correct with KV rewrite (requests/s)", "value": round(world * 1e3 / ms, 3),
+            "unit": "requests/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "p50_ms": round(per[len(per) // 2], 3), "p99_ms": round(per[-1], 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic 1024x1024 image + 128 random text ids, random-init weights",
+            "config": {"model": "Qwen2.5-VL-7B-shaped (LLM 28x3584, GQA 28/4, FFN 18944; ViT 32x1280)",
+                       "image_tokens": ex._sessions and next(iter(ex._sessions.values())).n_img,
+                       "text_tokens": 128, "keep_ratio": 0.25, "kv_cache": "paged, 128-row pages",
+                       "parallelism": f"dp{world}" if world > 1 else "single", "llm_layers": c.depth},
+            "gpu_launches": int(launches * args.steps), "clocks": clk, "e2e": e2e}))
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     """Reference executor (baseline/_ref, unmodified) on the same synthetic workload.
@@ -400,6 +504,18 @@ def main():
         print(json.dumps({"error": "for --gpus > 1 launch with torch.distributed.run"}))
         sys.exit(2)
     rank, world, local = dist_setup(args.gpus)
+    if args.workload == "vlm":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference's Qwen2.5-VL executor loads "
+                                  "HF checkpoints (transformers from_pretrained); none exist offline"}))
+        else:
+            run_vlm(args, rank, world)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     parallelism = (f"{args.parallel}{world}" if world > 1 else "single")
     images_per_step = args.batch * (world if (world > 1 and args.parallel == "dp") else 1)
     cfg_out = {"model": "DINOv3 ViT-7B/16 + linear seg head (150 cls)" if args.arch == "vit7b16" else args.arch,

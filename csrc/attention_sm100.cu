@@ -8,10 +8,13 @@
 //               tensor core works on the next scores while the softmax warps handle the current
 //               ones. V is consumed as an MN-major operand straight from its TMA tile.
 //   warps 2..5  softmax, one query row per thread: tcgen05.ld of the S row, running max / sum in
-//               base 2, P (bf16) written to shared memory in the K-major swizzled layout the MMA
-//               reads. O is rescaled in TMEM only when a row's running max grows by more than
+//               base 2 (scale folded into one FFMA before ex2.approx), P (bf16) written to one of
+//               two shared-memory buffers in the K-major swizzled layout the MMA reads, so the
+//               exponentials of block j+1 overlap PV_j. Max and sum use 8 independent partial
+//               chains. O is rescaled in TMEM only when a row's running max grows by more than
 //               2^8 (otherwise the stale max is kept; the final 1/l normalisation is exact either
-//               way). Finally O is read from TMEM, divided by l and stored.
+//               way); only then does the softmax wait for PV_{j-1}. Finally O is read from TMEM,
+//               divided by l and stored.
 // All waits are bounded (error word, no hang).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -64,7 +67,18 @@ struct FaParams {
   float* lse;      // [B, H, Tq] natural-log LSE or nullptr
   float* cls;      // [B, H, Tk] softmax probabilities of query row 0 (CLS) or nullptr
   int* err;
+  int Hkv;                  // key/value heads (grouped-query attention: head h reads kv head h / (H / Hkv))
+  int causal;               // 1: query row i sees keys 0..qpos(i) only
+  const int* q_pos;         // [B * Tq] key-axis position of each query row (causal; nullptr: i + Tk - Tq)
+  const int* block_table;   // [B, max_blocks] physical 128-row page of each key block (nullptr: b * Tk + j * 128)
+  int max_blocks;
 };
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <int DH>
 __global__ void __launch_bounds__(kFaThreads, 1)
@@ -74,7 +88,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   constexpr uint32_t CHUNK_BYTES = 128 * 128;           // one [128 rows x 64 cols] bf16 box
   constexpr uint32_t Q_BYTES = NCH * CHUNK_BYTES;
   constexpr uint32_t KV_BYTES = NCH * CHUNK_BYTES;      // per K (or V) stage
-  constexpr uint32_t P_BYTES = 2 * CHUNK_BYTES;         // [128 q x 128 keys]
+  constexpr uint32_t P_BYTES = 2 * CHUNK_BYTES;         // [128 q x 128 keys], two buffers
   constexpr uint32_t IDESC_S = idesc_bf16_f32(kFaBM, kFaBN);
   constexpr uint32_t IDESC_O = idesc_bf16_f32_b(kFaBM, DH, true);
   constexpr uint32_t TMEM_COLS = 512;
@@ -86,21 +100,22 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   uint8_t* sK = sQ + Q_BYTES;          // 2 stages
   uint8_t* sV = sK + 2 * KV_BYTES;     // 2 stages
   uint8_t* sP = sV + 2 * KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_BYTES);
   uint64_t* q_full = bars;           // 1
   uint64_t* kv_full = bars + 1;      // 2
   uint64_t* kv_empty = bars + 3;     // 2
   uint64_t* s_full = bars + 5;       // 2
   uint64_t* s_free = bars + 7;       // 2
-  uint64_t* p_full = bars + 9;       // 1
-  uint64_t* p_empty = bars + 10;     // 1
-  uint64_t* o_full = bars + 11;      // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* p_full = bars + 9;       // 2
+  uint64_t* p_empty = bars + 11;     // 2 (completes when PV of that buffer is done)
+  uint64_t* o_full = bars + 13;      // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int q0 = qt * kFaBM;
-  const int nkb = (p.Tk + kFaBN - 1) / kFaBN;
+  const int kvh = h / (p.H / p.Hkv);
+  __shared__ int s_nkb;
 
   if (warp == 0 && lane == 0) {
     mbar_init(smem_addr(q_full), 1);
@@ -109,9 +124,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       mbar_init(smem_addr(&kv_empty[i]), 1);
       mbar_init(smem_addr(&s_full[i]), 1);
       mbar_init(smem_addr(&s_free[i]), 128);
+      mbar_init(smem_addr(&p_full[i]), 128);
+      mbar_init(smem_addr(&p_empty[i]), 1);
     }
-    mbar_init(smem_addr(p_full), 128);
-    mbar_init(smem_addr(p_empty), 1);
     mbar_init(smem_addr(o_full), 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
@@ -122,10 +137,25 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     tmem_alloc(smem_addr(tmem_slot), TMEM_COLS);
     tmem_relinquish();
   }
+  if (warp == 2) {  // key blocks this tile needs: all of them, or (causal) up to its last query's position
+    int nk = (p.Tk + kFaBN - 1) / kFaBN;
+    if (p.causal) {
+      int mq = 0;
+      for (int r = lane; r < kFaBM; r += 32) {
+        const int qi = min(q0 + r, p.Tq - 1);
+        mq = max(mq, p.q_pos ? p.q_pos[(long)b * p.Tq + qi] : qi + p.Tk - p.Tq);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mq = max(mq, __shfl_xor_sync(0xffffffffu, mq, o));
+      nk = max(1, min(nk, mq / kFaBN + 1));
+    }
+    if (lane == 0) s_nkb = nk;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int nkb = s_nkb;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -139,10 +169,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (!mbar_wait(smem_addr(&kv_empty[s]), ph ^ 1, p.err, kErrTimeoutProducer)) break;
         const uint32_t fb = smem_addr(&kv_full[s]);
         mbar_arrive_expect_tx(fb, 2 * KV_BYTES);
-        const int row = b * p.Tk + j * kFaBN;
+        const int row = p.block_table ? p.block_table[(long)b * p.max_blocks + j] * kFaBN : b * p.Tk + j * kFaBN;
         for (int c = 0; c < NCH; ++c) {
-          tma_load_2d(smem_addr(sK + s * KV_BYTES + c * CHUNK_BYTES), &tmK, fb, h * DH + c * 64, row);
-          tma_load_2d(smem_addr(sV + s * KV_BYTES + c * CHUNK_BYTES), &tmV, fb, h * DH + c * 64, row);
+          tma_load_2d(smem_addr(sK + s * KV_BYTES + c * CHUNK_BYTES), &tmK, fb, kvh * DH + c * 64, row);
+          tma_load_2d(smem_addr(sV + s * KV_BYTES + c * CHUNK_BYTES), &tmV, fb, kvh * DH + c * 64, row);
         }
       }
     }
@@ -167,17 +197,17 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < nkb; ++j) {
         if (j + 1 < nkb && !issue_s(j + 1)) { ok = false; break; }
-        if (!mbar_wait(smem_addr(p_full), j & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
-        tc_fence_after();
         const int s = j & 1;
-        const uint32_t pa = smem_addr(sP), va = smem_addr(sV + s * KV_BYTES);
+        if (!mbar_wait(smem_addr(&p_full[s]), (j >> 1) & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t pa = smem_addr(sP + s * P_BYTES), va = smem_addr(sV + s * KV_BYTES);
 #pragma unroll
         for (int k = 0; k < kFaBN / 16; ++k) {
           const uint32_t aoff = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
           umma_f16(tmem + O_COL, sw128_kmajor_desc(pa + aoff), sw128_mnmajor_desc(va + k * 2048, CHUNK_BYTES, 1024),
                    IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(smem_addr(p_empty));
+        umma_commit(smem_addr(&p_empty[s]));
         umma_commit(smem_addr(&kv_empty[s]));
       }
       if (ok) umma_commit(smem_addr(o_full));
@@ -189,8 +219,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     float m_run = -FLT_MAX, l_run = 0.f;
     bool ok = true;
     const bool cls_row = p.cls != nullptr && qt == 0 && row == 0;
-    uint8_t* prow = sP + row * 128;
     const int rsw = row & 7;
+    const float sl2 = p.scale_log2;
+    int qpos = 0x7FFFFFFF;  // last key this row may see
+    if (p.causal) {
+      const int qi = min(q0 + row, p.Tq - 1);
+      qpos = p.q_pos ? p.q_pos[(long)b * p.Tq + qi] : qi + p.Tk - p.Tq;
+    }
+    // m_run: running max of the raw scores; exponent = S * sl2 - m_run * sl2 (one FFMA)
     for (int j = 0; j < nkb; ++j) {
       const int s = j & 1;
       if (!mbar_wait(smem_addr(&s_full[s]), (j >> 1) & 1, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
@@ -202,38 +238,46 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         tmem_ld32(tmem + lane_base + s * kFaBN + c * 32, r);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) sv[c * 32 + t] = __uint_as_float(r[t]) * p.scale_log2;
+        for (int t = 0; t < 32; ++t) sv[c * 32 + t] = __uint_as_float(r[t]);
       }
       tc_fence_before();
       mbar_arrive(smem_addr(&s_free[s]));
       const int kbase = j * kFaBN;
-      float mx = -FLT_MAX;
+      const int klim = min(p.Tk - 1, qpos);  // keys past Tk do not exist; causal rows stop at qpos
+      if (kbase + kFaBN - 1 > klim) {
 #pragma unroll
-      for (int t = 0; t < kFaBN; ++t) {
-        if (kbase + t >= p.Tk) sv[t] = -FLT_MAX;
-        mx = fmaxf(mx, sv[t]);
+        for (int t = 0; t < kFaBN; ++t)
+          if (kbase + t > klim) sv[t] = -FLT_MAX;
       }
+      float mx8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mx8[u] = sv[u];
+#pragma unroll
+      for (int t = 8; t < kFaBN; ++t) mx8[t & 7] = fmaxf(mx8[t & 7], sv[t]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       if (cls_row) {  // keep the CLS row's scaled logits; normalised once the row's max / sum are final
         float* dst = p.cls + ((long)b * p.H + h) * p.Tk + kbase;
         const int n = min(kFaBN, p.Tk - kbase);
 #pragma unroll
         for (int t = 0; t < kFaBN; ++t)
-          if (t < n) dst[t] = sv[t];
+          if (t < n) dst[t] = sv[t] * sl2;
       }
       // rescale decision (warp-uniform because tcgen05.ld/st are warp-collective)
-      const bool grow = mx > m_run + kRescaleThreshold;
+      const bool grow = (mx - m_run) * sl2 > kRescaleThreshold;
       const bool any_grow = __any_sync(0xffffffffu, grow) && j > 0;
       float corr = 1.f;
       if (grow || j == 0) {
         const float mnew = fmaxf(m_run, mx);
-        corr = (j == 0) ? 0.f : exp2f(m_run - mnew);
+        corr = (j == 0) ? 0.f : ex2_approx((m_run - mnew) * sl2);
         m_run = mnew;
       }
-      if (j > 0) {  // P buffer and O are busy until PV_{j-1} completes
-        if (!mbar_wait(smem_addr(p_empty), (j - 1) & 1, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+      if (any_grow) {  // O is being accumulated by PV_{j-1}: wait for it, then rescale in TMEM
+        if (!mbar_wait(smem_addr(&p_empty[(j - 1) & 1]), ((j - 1) >> 1) & 1, p.err, kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-      }
-      if (any_grow) {
 #pragma unroll 1
         for (int c = 0; c < DH / 32; ++c) {
           uint32_t r[32];
@@ -245,8 +289,17 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
         tmem_wait_st();
       }
+      if (j >= 2) {  // P buffer s is free once PV_{j-2} completed
+        if (!mbar_wait(smem_addr(&p_empty[s]), ((j >> 1) & 1) ^ 1, p.err, kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
       l_run *= (j == 0) ? 0.f : corr;
-      float lsum = 0.f;
+      const float moff = m_run * sl2;
+      uint8_t* prow = sP + s * P_BYTES + row * 128;
+      float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < kFaBN / 64; ++c) {
 #pragma unroll
@@ -254,18 +307,18 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           float e[8];
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
-            e[t] = exp2f(sv[c * 64 + v * 8 + t] - m_run);
-            lsum += e[t];
+            e[t] = ex2_approx(fmaf(sv[c * 64 + v * 8 + t], sl2, -moff));
+            ls8[t] += e[t];
           }
           const uint4 pk = make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
                                       pack_bf16x2(e[6], e[7]));
           *reinterpret_cast<uint4*>(prow + c * CHUNK_BYTES + ((v ^ rsw) << 4)) = pk;
         }
       }
-      l_run += lsum;
+      l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(smem_addr(p_full));
+      mbar_arrive(smem_addr(&p_full[s]));
     }
     if (ok && mbar_wait(smem_addr(o_full), 0, p.err, kErrTimeoutEpilogue)) {
       tc_fence_after();
@@ -288,11 +341,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
       }
       if (p.lse != nullptr && qrow < p.Tq)
-        p.lse[((long)b * p.H + h) * p.Tq + qrow] = (m_run + log2f(l_run)) * 0.69314718055994531f;
+        p.lse[((long)b * p.H + h) * p.Tq + qrow] = (m_run * sl2 + log2f(l_run)) * 0.69314718055994531f;
     }
     if (p.cls != nullptr && qt == 0 && qd == 0) {  // the warp holding row 0 normalises the CLS row
       __syncwarp();
-      const float m0 = __shfl_sync(0xffffffffu, m_run, 0);
+      const float m0 = __shfl_sync(0xffffffffu, m_run, 0) * sl2;
       const float inv0 = 1.f / __shfl_sync(0xffffffffu, l_run, 0);
       float* src = p.cls + ((long)b * p.H + h) * p.Tk;
       for (int t = lane; t < p.Tk; t += 32) src[t] = exp2f(src[t] - m0) * inv0;
@@ -308,7 +361,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
 void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, int64_t B,
                         int64_t Tq, int64_t Tk, int64_t H, int64_t Dh, double scale, c10::optional<at::Tensor> lse,
-                        const at::Tensor& err, c10::optional<at::Tensor> cls) {
+                        const at::Tensor& err, c10::optional<at::Tensor> cls, int64_t Hkv, bool causal,
+                        c10::optional<at::Tensor> q_pos, c10::optional<at::Tensor> block_table) {
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &o}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->stride(-1) == 1, "attention: bf16 CUDA tensors");
     TORCH_CHECK(t->stride(-2) % 8 == 0 && (reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) == 0, "attention: 16B-aligned rows");
@@ -319,11 +373,29 @@ void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tens
   c10::cuda::CUDAGuard g(q.device());
   // 2-D views [rows, H*Dh] with 128-row x 64-column boxes.
   CUtensorMap tq = make_tmap_bf16_2d(q.data_ptr(), B * Tq, H * Dh, q.stride(-2), kFaBM, 64);
-  CUtensorMap tk = make_tmap_bf16_2d(k.data_ptr(), B * Tk, H * Dh, k.stride(-2), kFaBN, 64);
-  CUtensorMap tv = make_tmap_bf16_2d(v.data_ptr(), B * Tk, H * Dh, v.stride(-2), kFaBN, 64);
+  if (Hkv <= 0) Hkv = H;
+  TORCH_CHECK(H % Hkv == 0, "attention: H must be a multiple of Hkv");
+  int64_t kv_rows = B * Tk;
+  int max_blocks = 0;
+  if (block_table.has_value()) {
+    TORCH_CHECK(block_table->scalar_type() == at::kInt && block_table->dim() == 2 && block_table->size(0) == B &&
+                    block_table->is_contiguous(),
+                "attention: block_table int32 [B, max_blocks]");
+    max_blocks = static_cast<int>(block_table->size(1));
+    TORCH_CHECK(max_blocks * 128 >= Tk, "attention: block_table too short for Tk");
+    kv_rows = k.size(0);  // the page pool
+    TORCH_CHECK(kv_rows % 128 == 0, "attention: paged K/V pool rows must be a multiple of 128");
+  }
+  if (q_pos.has_value())
+    TORCH_CHECK(q_pos->scalar_type() == at::kInt && q_pos->numel() == B * Tq && q_pos->is_contiguous(),
+                "attention: q_pos int32 [B*Tq]");
+  CUtensorMap tk = make_tmap_bf16_2d(k.data_ptr(), kv_rows, Hkv * Dh, k.stride(-2), kFaBN, 64);
+  CUtensorMap tv = make_tmap_bf16_2d(v.data_ptr(), kv_rows, Hkv * Dh, v.stride(-2), kFaBN, 64);
   FaParams p{static_cast<int>(B), static_cast<int>(Tq), static_cast<int>(Tk), static_cast<int>(H),
              static_cast<float>(scale * 1.4426950408889634), reinterpret_cast<bf16*>(o.data_ptr()), o.stride(-2),
-             nullptr, nullptr, err.data_ptr<int>()};
+             nullptr, nullptr, err.data_ptr<int>(), static_cast<int>(Hkv), causal ? 1 : 0,
+             q_pos.has_value() ? q_pos->data_ptr<int>() : nullptr,
+             block_table.has_value() ? block_table->data_ptr<int>() : nullptr, max_blocks};
   if (cls.has_value()) {
     TORCH_CHECK(cls->scalar_type() == at::kFloat && cls->is_contiguous() && cls->numel() >= B * H * Tk,
                 "attention: cls fp32 [B,H,Tk]");
@@ -336,7 +408,7 @@ void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tens
   dim3 grid((Tq + kFaBM - 1) / kFaBM, H, B);
   auto st = at::cuda::getCurrentCUDAStream();
   const int nch = static_cast<int>(Dh / 64);
-  const int smem = nch * 16384 * 5 + 2 * 16384 + 1024 + 256;
+  const int smem = nch * 16384 * 5 + 4 * 16384 + 1024 + 256;
   if (Dh == 128) {
     cudaFuncSetAttribute(fa_fwd_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     fa_fwd_sm100_kernel<128><<<grid, kFaThreads, smem, st>>>(tq, tk, tv, p);
@@ -351,7 +423,8 @@ void register_attention_sm100_ops(pybind11::module_& m) {
   namespace py = pybind11;
   m.def("attention_sm100", &attention_sm100_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("B"),
         py::arg("Tq"), py::arg("Tk"), py::arg("H"), py::arg("Dh"), py::arg("scale"), py::arg("lse"), py::arg("err"),
-        py::arg("cls") = py::none());
+        py::arg("cls") = py::none(), py::arg("Hkv") = 0, py::arg("causal") = false, py::arg("q_pos") = py::none(),
+        py::arg("block_table") = py::none());
 }
 
 }  // namespace appcorr

@@ -83,7 +83,7 @@ template <bool FP8>
 __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
     const bf16* __restrict__ x, long ldx, const int* __restrict__ rows, const bf16* __restrict__ w,
     const bf16* __restrict__ b, float eps, bf16* __restrict__ out, long ldo, bf16* __restrict__ copy_out,
-    long ldc, int D, int nrows, uint8_t* __restrict__ out8, float* __restrict__ scale8) {
+    long ldc, int D, int nrows, uint8_t* __restrict__ out8, float* __restrict__ scale8, int rms) {
   __shared__ float red[kLnThreads / 32];
   const int r = blockIdx.x;
   if (r >= nrows) return;
@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
       for (int j = 0; j < 8; ++j) s += v[i][j];
     }
   }
-  const float mean = block_sum<kLnThreads>(s, red) / D;
+  // rms: RMSNorm (no centring, no bias)
+  const float mean = rms ? 0.f : block_sum<kLnThreads>(s, red) / D;
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < kLnMaxVec; ++i) {
@@ -121,12 +122,13 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
   const float rstd = rsqrtf(block_sum<kLnThreads>(q, red) / D + eps);
   const uint4* wv = reinterpret_cast<const uint4*>(w);
   const uint4* bv = reinterpret_cast<const uint4*>(b);
+  const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < kLnMaxVec; ++i) {
     const int c = threadIdx.x + i * kLnThreads;
     if (c < nvec) {
-      uint4 wu = __ldg(wv + c), bu = __ldg(bv + c);
+      uint4 wu = __ldg(wv + c), bu = b ? __ldg(bv + c) : zero4;
       const uint32_t* wp = &wu.x;
       const uint32_t* bp = &bu.x;
 #pragma unroll
@@ -221,12 +223,16 @@ void quant_rows_e4m3_op(const at::Tensor& x, at::Tensor& out, at::Tensor& scale)
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at::Tensor& w, const at::Tensor& b,
-                  double eps, at::Tensor& out, c10::optional<at::Tensor> copy_out, c10::optional<at::Tensor> scale8) {
+void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at::Tensor& w,
+                  c10::optional<at::Tensor> b_opt, double eps, at::Tensor& out, c10::optional<at::Tensor> copy_out, c10::optional<at::Tensor> scale8,
+                  bool rms) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "layernorm: bf16 CUDA x");
   const int D = static_cast<int>(x.size(-1));
   TORCH_CHECK(D % 8 == 0 && D <= kLnThreads * kLnMaxVec * 8, "layernorm: D % 8 == 0 and D <= 8192");
-  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && w.numel() == D, "layernorm: bf16 affine");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.numel() == D, "layernorm: bf16 weight [D]");
+  const at::Tensor b = b_opt.has_value() ? *b_opt : at::Tensor();
+  TORCH_CHECK(!b.defined() || (b.scalar_type() == at::kBFloat16 && b.numel() == D), "layernorm: bf16 bias [D]");
+  const bf16* bptr = b.defined() ? reinterpret_cast<const bf16*>(b.data_ptr()) : nullptr;
   const long ldx = x.stride(-2);
   const int nrows = static_cast<int>(out.size(0));
   const int* rp = nullptr;
@@ -255,13 +261,13 @@ void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at:
   if (fp8)
     layernorm_kernel<true><<<nrows, kLnThreads, 0, st>>>(
         reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
-        reinterpret_cast<const bf16*>(b.data_ptr()), static_cast<float>(eps), nullptr, out.stride(0), cp, ldc, D,
-        nrows, reinterpret_cast<uint8_t*>(out.data_ptr()), scale8->data_ptr<float>());
+        bptr, static_cast<float>(eps), nullptr, out.stride(0), cp, ldc, D,
+        nrows, reinterpret_cast<uint8_t*>(out.data_ptr()), scale8->data_ptr<float>(), rms ? 1 : 0);
   else
     layernorm_kernel<false><<<nrows, kLnThreads, 0, st>>>(
         reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
-        reinterpret_cast<const bf16*>(b.data_ptr()), static_cast<float>(eps), reinterpret_cast<bf16*>(out.data_ptr()),
-        out.stride(0), cp, ldc, D, nrows, nullptr, nullptr);
+        bptr, static_cast<float>(eps), reinterpret_cast<bf16*>(out.data_ptr()),
+        out.stride(0), cp, ldc, D, nrows, nullptr, nullptr, rms ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -297,8 +303,11 @@ void add_inplace_op(at::Tensor& x, const at::Tensor& y) {
 // img: uint8 [B, H, W, 3] (HWC as decoded). out: bf16 [B * (H/p) * (W/p), 3*p*p], column index
 // c*p*p + ky*p + kx (the Conv2d weight flattening order). Pixels are normalised as
 // (v / 255 - mean[c]) / std[c].
+// Output row r of image b holds patch perm[r] (row-major patch index; perm == nullptr: r), in a
+// buffer of row stride ldo >= 3*p*p (columns past 3*p*p are left untouched).
 __global__ void patch_im2col_kernel(const uint8_t* __restrict__ img, int H, int W, int p, float3 mean,
-                                    float3 inv_std, bf16* __restrict__ out, long total) {
+                                    float3 inv_std, bf16* __restrict__ out, long total, long ldo,
+                                    const int* __restrict__ perm) {
   const int gw = W / p, gh = H / p;
   const int K = 3 * p * p;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
@@ -308,29 +317,82 @@ __global__ void patch_im2col_kernel(const uint8_t* __restrict__ img, int H, int 
     const int rem = col - c * p * p;
     const int ky = rem / p, kx = rem - (rem / p) * p;
     const long b = row / (gh * gw);
-    const int t = static_cast<int>(row - b * gh * gw);
+    const int r = static_cast<int>(row - b * gh * gw);
+    const int t = perm ? perm[r] : r;
     const int py = t / gw, px = t - (t / gw) * gw;
     const int y = py * p + ky, x = px * p + kx;
     const float v = img[((b * H + y) * W + x) * 3 + c] * (1.0f / 255.0f);
     const float m = c == 0 ? mean.x : (c == 1 ? mean.y : mean.z);
     const float s = c == 0 ? inv_std.x : (c == 1 ? inv_std.y : inv_std.z);
-    out[i] = __float2bfloat16_rn((v - m) * s);
+    out[row * ldo + col] = __float2bfloat16_rn((v - m) * s);
   }
 }
 
 void patch_im2col_op(const at::Tensor& img, int64_t patch, std::vector<double> mean, std::vector<double> std_,
-                     at::Tensor& out) {
+                     at::Tensor& out, c10::optional<at::Tensor> perm) {
   TORCH_CHECK(img.is_cuda() && img.scalar_type() == at::kByte && img.dim() == 4 && img.size(3) == 3 && img.is_contiguous(),
               "patch_im2col: uint8 [B,H,W,3] contiguous");
   const int H = static_cast<int>(img.size(1)), W = static_cast<int>(img.size(2)), p = static_cast<int>(patch);
   TORCH_CHECK(H % p == 0 && W % p == 0, "patch_im2col: H, W multiples of patch");
   const long total = img.size(0) * (long)(H / p) * (W / p) * 3 * p * p;
-  TORCH_CHECK(out.numel() == total && out.is_contiguous() && out.scalar_type() == at::kBFloat16, "patch_im2col: out shape");
+  const long rows = img.size(0) * (long)(H / p) * (W / p);
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == rows && out.size(1) >= 3 * p * p && out.stride(1) == 1 &&
+                  out.scalar_type() == at::kBFloat16,
+              "patch_im2col: out bf16 [B*patches, >= 3*p*p]");
+  const int* pp = nullptr;
+  if (perm.has_value()) {
+    TORCH_CHECK(perm->scalar_type() == at::kInt && perm->numel() == (H / p) * (W / p) && perm->is_cuda(),
+                "patch_im2col: perm int32 [patches]");
+    pp = perm->data_ptr<int>();
+  }
   c10::cuda::CUDAGuard g(img.device());
   const int grid = static_cast<int>(std::min<long>((total + 255) / 256, num_sms() * 16L));
   patch_im2col_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       img.data_ptr<uint8_t>(), H, W, p, make_float3(mean[0], mean[1], mean[2]),
-      make_float3(1.0 / std_[0], 1.0 / std_[1], 1.0 / std_[2]), reinterpret_cast<bf16*>(out.data_ptr()), total);
+      make_float3(1.0 / std_[0], 1.0 / std_[1], 1.0 / std_[2]), reinterpret_cast<bf16*>(out.data_ptr()), total,
+      out.stride(0), pp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------ row distance
+// out[r] = sum_c (a[r,c] - b[r,c])^2 in fp32; one warp per row (D % 8 == 0). The VLM correction
+// ranks image tokens by how much their embedding moved between the approximate and the current
+// canvas.
+__global__ void row_sqdist_kernel(const bf16* __restrict__ a, long lda, const bf16* __restrict__ b, long ldb,
+                                  float* __restrict__ out, int M, int D) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const uint4* pa = reinterpret_cast<const uint4*>(a + (long)row * lda);
+  const uint4* pb = reinterpret_cast<const uint4*>(b + (long)row * ldb);
+  float acc = 0.f;
+  for (int c = lane; c < (D >> 3); c += 32) {
+    const uint4 ua = pa[c], ub = pb[c];
+    const uint32_t* xa = &ua.x;
+    const uint32_t* xb = &ub.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fa = unpack_bf16x2(xa[j]), fb = unpack_bf16x2(xb[j]);
+      const float d0 = fa.x - fb.x, d1 = fa.y - fb.y;
+      acc = fmaf(d0, d0, fmaf(d1, d1, acc));
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) out[row] = acc;
+}
+
+void row_sqdist_op(const at::Tensor& a, const at::Tensor& b, at::Tensor& out) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && a.dim() == 2 &&
+                  b.sizes() == a.sizes() && a.stride(1) == 1 && b.stride(1) == 1,
+              "row_sqdist: bf16 [M, D] a, b");
+  const int M = static_cast<int>(a.size(0)), D = static_cast<int>(a.size(1));
+  TORCH_CHECK(D % 8 == 0 && a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "row_sqdist: 16-byte rows");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.numel() == M && out.is_contiguous(), "row_sqdist: out fp32 [M]");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard g(a.device());
+  row_sqdist_kernel<<<(M + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(a.data_ptr()), a.stride(0), reinterpret_cast<const bf16*>(b.data_ptr()),
+      b.stride(0), out.data_ptr<float>(), M, D);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -808,10 +870,12 @@ void register_elementwise_ops(pybind11::module_& m) {
   m.def("head_mean", &head_mean_op);
   namespace py = pybind11;
   m.def("layernorm", &layernorm_op, py::arg("x"), py::arg("rows"), py::arg("w"), py::arg("b"), py::arg("eps"),
-        py::arg("out"), py::arg("copy_out") = py::none(), py::arg("scale8") = py::none());
+        py::arg("out"), py::arg("copy_out") = py::none(), py::arg("scale8") = py::none(), py::arg("rms") = false);
   m.def("quant_rows_e4m3", &quant_rows_e4m3_op, py::arg("x"), py::arg("out"), py::arg("scale"));
   m.def("add_", &add_inplace_op);
-  m.def("patch_im2col", &patch_im2col_op);
+  m.def("row_sqdist", &row_sqdist_op, py::arg("a"), py::arg("b"), py::arg("out"));
+  m.def("patch_im2col", &patch_im2col_op, py::arg("img"), py::arg("patch"), py::arg("mean"), py::arg("std"),
+        py::arg("out"), py::arg("perm") = py::none());
   m.def("set_prefix", &set_prefix_op);
   m.def("gather_rows", &gather_rows_op);
   m.def("scatter_rows", &scatter_rows_op);

@@ -106,3 +106,34 @@ def test_state_dict_keys_match_dinov3_layout():
     small = build_vit("vits16", depth=1)
     assert "blocks.0.attn.qkv.bias_mask" in small.state_dict()
     assert "blocks.0.mlp.fc1.weight" in small.state_dict()
+
+
+def test_qwen_oracle_window_order_and_full_correction():
+    """Window-major order is a permutation whose merge units are contiguous; correcting every
+    row of the VLM LLM reproduces its approximate (full) forward exactly."""
+    from appcorr_b200.models.qwen25vl import (PRESETS, Qwen25VL, merge_raster_index, mrope_positions,
+                                              mrope_tables, window_order)
+
+    order = window_order(16, 24, 8, 2)
+    assert sorted(order.tolist()) == list(range(16 * 24))
+    units = order.view(-1, 4)
+    ys, xs = units // 24, units % 24
+    assert bool(((ys // 2) == (ys[:, :1] // 2)).all()) and bool(((xs // 2) == (xs[:, :1] // 2)).all())
+    inv = merge_raster_index(PRESETS["tiny"], 16, 24)
+    assert sorted(inv.tolist()) == list(range(8 * 12))
+    cfg = PRESETS["tiny"]
+    torch.manual_seed(0)
+    m = Qwen25VL(cfg).init_weights(0)
+    img = torch.randint(0, 256, (224, 224, 3), dtype=torch.uint8)
+    with torch.no_grad():
+        emb = m.visual(img)
+        s, c = mrope_tables(cfg, mrope_positions(8, 8, 8, 24))
+        x0 = m.embed(torch.arange(8), emb, torch.arange(24))
+        cache = {}
+        x = x0
+        for i, ly in enumerate(m.layers):
+            x = ly.approx(x, s, c, cache, f"l{i}")
+        x2 = x0
+        for i, ly in enumerate(m.layers):
+            x2 = ly.correct(x2, torch.arange(x0.shape[0]), s, c, cache, f"l{i}")
+    assert torch.allclose(x, x2, atol=1e-5)
