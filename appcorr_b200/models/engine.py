@@ -440,6 +440,15 @@ class ViTEngine:
         return x
 
     # -------------------------------------------------------------- outputs
+    def normed_tokens(self, sess: Session) -> torch.Tensor:
+        """Final LayerNorm of every token (CLS, storage and patch) -> [B*N, D]."""
+        c = self.cfg
+        buf = sess.extra.get("normed")
+        if buf is None:
+            buf = sess.extra["normed"] = torch.empty_like(sess.x)
+        K.layernorm(sess.x, self.w.norm_w, self.w.norm_b, c.norm_eps, buf)
+        return buf
+
     def patch_features(self, sess: Session, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Final LayerNorm of the patch tokens -> [B*P, D]."""
         c = self.cfg

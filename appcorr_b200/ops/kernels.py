@@ -41,10 +41,12 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
          aux_rows: Optional[torch.Tensor] = None, aux_mode: int = AUX_NONE,
          resid2: Optional[torch.Tensor] = None, bn: Optional[int] = None,
          max_ctas: int = 0, a_scale: Optional[torch.Tensor] = None,
-         b_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+         b_scale: Optional[torch.Tensor] = None, rs: Optional[tuple] = None) -> torch.Tensor:
     """out = epilogue(a @ w^T). `a` [M, K], `w` [N, K] (nn.Linear layout), both bf16 or both
     e4m3; e4m3 operands carry fp32 scales a_scale [M] (per row) and b_scale [N] (per output
-    channel) that the epilogue applies to the fp32 accumulator before bias / activation."""
+    channel) that the epilogue applies to the fp32 accumulator before bias / activation.
+    rs = (slot_ptrs, rows_per_rank, rank, slot_rows, ld): reduce-scatter epilogue; row m goes to
+    rank (out_rows[m] or m) // rows_per_rank, slot row rank * slot_rows + m (`out` unused)."""
     fp8 = a.dtype == torch.float8_e4m3fn
     if bn is None:
         bn = 256 if epi == EPI_SWIGLU else _pick_bn(w.shape[0], a.shape[0])
@@ -53,7 +55,9 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
     _count()
     lib().gemm(a, w, epi, bn, err_word(a.device), out=out, out_rows=out_rows, bias=bias, gamma=gamma,
                resid=resid, resid_rows=resid_rows, aux=aux, aux_rows=aux_rows, aux_mode=aux_mode,
-               resid2=resid2, max_ctas=max_ctas, a_scale=a_scale, b_scale=b_scale)
+               resid2=resid2, max_ctas=max_ctas, a_scale=a_scale, b_scale=b_scale,
+               **({} if rs is None else dict(rs_out=list(rs[0]), rs_rows_per_rank=int(rs[1]), rs_rank=int(rs[2]),
+                                             rs_slot_rows=int(rs[3]), rs_ld=int(rs[4]))))
     return out
 
 

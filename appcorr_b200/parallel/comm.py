@@ -90,16 +90,21 @@ class TPComm:
         _count()
         lib().tp_barrier(self.flags.ptrs, self.rank, self.epoch, self.err)
 
-    def allreduce_epilogue(self, part: SymTensor, out: SymTensor, M: int, N: int, *, out_rows=None,
-                           out_offset: int = 0, aux: Optional[SymTensor] = None, aux_offset: int = 0, aux_rows=None,
-                           aux_mode: int = 0, bias=None, gamma=None, resid=None, resid_rows=None, resid2=None) -> None:
-        """Sum of every rank's `part[:M, :N]`, fused with the residual / LayerScale epilogue,
-        stored into every rank's `out` (and `aux`). Caller brackets it with barriers."""
+    def sp_row(self, M: int, D: int, rows_per_rank: int, *, tok=None, src: Optional[Tuple[List[int], List[int]]] = None,
+               bias=None, gamma=None, resid=None, resid_tok: bool = True, resid2=None,
+               out=None, out_tok: bool = True, aux=None, aux_mode: int = 0, x=None, copy_out=None,
+               ln_w=None, ln_b=None, eps: float = 1e-6, rms: bool = False, ag: Optional[SymTensor] = None,
+               ag_scale: Optional[SymTensor] = None) -> None:
+        """Owner-side row kernel of the sequence-parallel layout (csrc/tp_sp.cu): finish the
+        reduce-scatter of the partial rows `src` = (base pointers, row offsets), one per rank (or
+        load x[tok]) on the rows this rank owns, then LayerNorm and all-gather the normalised
+        rows into every rank's `ag` (e4m3 + scales when ag_scale)."""
         _count()
-        lib().tp_allreduce_epi(part.ptrs, part.local.stride(0), out.view_ptrs(out_offset), out.local.stride(-2),
-                               out_rows, aux.view_ptrs(aux_offset) if aux is not None else [],
-                               aux.local.stride(-2) if aux is not None else 0, aux_rows, aux_mode, bias, gamma, resid,
-                               resid_rows, resid2, M, N, self.rank)
+        fp8 = ag_scale is not None
+        lib().sp_row(M, tok, rows_per_rank, self.rank, self.world, D, list(src[0]) if src else [],
+                     list(src[1]) if src else [], bias, gamma, resid, resid_tok, resid2, out, out_tok, aux, aux_mode, x, copy_out,
+                     ln_w, ln_b, float(eps), rms, fp8, ag.ptrs if ag is not None else [],
+                     (ag.local.stride(0) if ag is not None else 0), ag_scale.ptrs if fp8 else [])
 
     def mean_f32(self, src: SymTensor, dst: torch.Tensor) -> None:
         _count()

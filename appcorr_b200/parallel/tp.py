@@ -1,33 +1,42 @@
-"""Tensor-parallel ViT engine (Megatron split, one process per GPU, peer-memory collectives).
+"""Tensor-parallel ViT engine, sequence-parallel layout (one process per GPU, collectives fused
+into the kernels that produce and consume them, over NVLink / NVSwitch peer memory).
 
 Weights: qkv and fc1 / w1||w2 are split by output (heads / hidden units), proj and fc2 / w3 by
-input, so each rank computes its heads' attention and its slice of the MLP for every token and
-produces a partial product of proj and of fc2. The residual stream, the per-layer increment
-cache and the correction plan are replicated; the K/V cache is split by head (no K/V traffic).
+input. The residual stream and the per-layer increment cache are split by ROWS: rank r owns token
+rows [r*R, (r+1)*R), R = ceil(M / T). The K/V cache is split by head (no K/V traffic).
 
 Per layer (approximate pass):
-    LN1 -> qkv (local heads) -> CLS score (local heads) -> attention (local heads)
-        -> proj partial -> barrier -> all-reduce + residual/LayerScale epilogue -> barrier
-        -> LN2 -> fc1 slice -> fc2 partial -> barrier -> all-reduce + epilogue -> barrier
-The all-reduce is csrc/comm.cu `tp_allreduce_epi`: each rank reduces its own row block from every
-peer's partial over NVLink and writes the finished rows into every replica, so the block's
-residual add, LayerScale and increment bookkeeping ride on the collective. The correction pass
-is the same on the packed selected rows; the final epilogue scatters them into every replica.
+    [gather buffer xg holds LN1(x) of every row, e4m3 + row scales (or bf16)]
+    qkv GEMM (local heads) -> CLS score + attention (local heads) -> proj GEMM (partial product)
+    -> barrier -> owner row kernel: sum of the T partials (the reduce-scatter: peer loads of
+    each rank's partial rows, or with APPCORR_TP_RS=push local loads of rows that the GEMM
+    epilogue already stored into the owner's slots over NVLink) + bias, LayerScale, residual,
+    increment := delta, then LN2 of the finished row quantised and stored into every rank's xg
+    (fused all-gather) -> barrier -> w1||w2 GEMM (local hidden) -> fc2 GEMM (partial)
+    -> barrier -> owner row kernel (reduce-scatter, residual, increment += delta, LN1 of
+    the next layer + all-gather) -> barrier
+Bytes per layer and rank: (T-1)/T * M * D * (2 + 2) for the two reduce-scatters (bf16 partials)
+plus (T-1)/T * M * D * (1 + 1) for the two all-gathers (e4m3 rows), against 8 * (T-1)/T * M * D
+for two bf16 all-reduces of a replicated stream.
+The correction pass is the same on the packed selected rows: the owner of a selected token runs
+its LN (gather), the partial rows of the packed GEMM outputs are routed to the owners of their
+tokens, and the increments are updated on the owners.
 Reference: none (the reference is single-GPU); semantics are those of models/engine.py.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import replace
 from typing import Dict, Optional
 
 import torch
 
-from ..common.protocol import LAYERMEAN_SERVER_PSCORES
 from ..models.dinov3.vit import ViTConfig
 from ..models.engine import BF16, EngineWeights, LayerW, Session, ViTEngine, random_weights
 from ..models.weights import SWIGLU_BLOCK, pack_swiglu, unpack_swiglu
 from ..ops import kernels as K
-from .comm import TPComm
+from ..utils.tracing import PhaseTimer
+from .comm import SymTensor, TPComm
 
 
 def shard_layer(cfg: ViTConfig, lw: LayerW, rank: int, world: int) -> LayerW:
@@ -64,7 +73,7 @@ def shard_weights(w: EngineWeights, rank: int, world: int) -> EngineWeights:
 
 class ViTEngineTP(ViTEngine):
     """ViTEngine whose layers run split over `comm.world` GPUs. Construct from full weights
-    (`from_full`) or generate random shards directly (`random`)."""
+    (`from_full`) or generate random shards directly (`random_tp`)."""
 
     def __init__(self, weights: EngineWeights, comm: TPComm, device=None, precision="bf16"):
         super().__init__(weights, device, precision)
@@ -72,6 +81,12 @@ class ViTEngineTP(ViTEngine):
         self.world, self.rank = comm.world, comm.rank
         self.local_heads = self.cfg.num_heads // self.world
         self.local_dim = self.cfg.embed_dim // self.world
+        self.timer = PhaseTimer.from_env()
+        # reduce-scatter of the row-parallel GEMMs: "pull" (owner loads peers' partials in the row
+        # kernel) or "push" (GEMM epilogue stores partial rows into the owner's slots)
+        self.rs_mode = os.environ.get("APPCORR_TP_RS", "pull")
+        if self.rs_mode not in ("pull", "push"):
+            raise ValueError("APPCORR_TP_RS must be 'pull' or 'push'")
 
     @classmethod
     def from_full(cls, full: EngineWeights, comm: TPComm, precision="bf16") -> "ViTEngineTP":
@@ -92,14 +107,15 @@ class ViTEngineTP(ViTEngine):
         M, D, L = B * sess.N, c.embed_dim, c.depth
         d, hd = self.local_dim, c.ffn_hidden // self.world
         dev = self.device
-        # replicated state that peers write into
-        x = comm.empty((M, D), BF16)
-        bos = comm.empty((L, M, D), BF16)
-        x_att = comm.empty((B * (c.n_prefix + sess.P), D), BF16)
-        part = comm.empty((M, D), BF16)
-        ps_local = comm.empty((B, sess.N), torch.float32)
-        sess.extra.update({"sym_x": x, "sym_bos": bos, "sym_x_att": x_att, "sym_part": part, "sym_ps": ps_local})
-        sess.x, sess.bos, sess.x_att = x.local, bos.local, x_att.local
+        R = (M + self.world - 1) // self.world
+        # symmetric buffers that peers store into
+        xg = comm.empty((M, D), BF16)                       # gathered LN rows (bf16, or e4m3 in its first M*D bytes)
+        xg8 = SymTensor(xg.local.view(torch.uint8).view(-1)[: M * D].view(M, D).view(torch.float8_e4m3fn), xg.ptrs)
+        sess.extra.update({
+            "R": R, "sym_xg": xg, "sym_xg8": xg8, "sym_xg_scale": comm.empty((M,), torch.float32),
+            "sym_part": (comm.empty((self.world, M, D), BF16) if self.rs_mode == "push" else comm.empty((M, D), BF16)),
+            "sym_ps": comm.empty((B, sess.N), torch.float32),
+            "sym_feat": comm.empty((B * sess.P, D), BF16)})
         # head-split buffers
         sess.q = torch.empty(M, d, device=dev, dtype=BF16)
         sess.o = torch.empty(M, d, device=dev, dtype=BF16)
@@ -110,46 +126,98 @@ class ViTEngineTP(ViTEngine):
         return sess
 
     # -------------------------------------------------------------- helpers
-    def _reduce(self, sess: Session, M: int, **kw) -> None:
-        comm = self.comm
-        comm.barrier()
-        comm.allreduce_epilogue(sess.extra["sym_part"], M=M, N=self.cfg.embed_dim, **kw)
-        comm.barrier()
+    def _gathered(self, sess: Session, n: int):
+        """The all-gathered GEMM operand rows [:n] (and their e4m3 scales)."""
+        e = sess.extra
+        if self._fp8:
+            return e["sym_xg8"].local[:n], e["sym_xg_scale"].local[:n]
+        return e["sym_xg"].local[:n], None
+
+    def _ag(self, sess: Session) -> Dict:
+        e = sess.extra
+        if self._fp8:
+            return {"ag": e["sym_xg8"], "ag_scale": e["sym_xg_scale"]}
+        return {"ag": e["sym_xg"]}
+
+    def _row_gemm(self, sess: Session, a, w, rows_out, a_scale, b_scale, n: int) -> None:
+        """Row-parallel GEMM producing this rank's partial product of n (packed) rows."""
+        e = sess.extra
+        if self.rs_mode == "push":  # partial rows stored into their owners' slots by the epilogue
+            K.gemm(a, w, None, out_rows=rows_out, a_scale=a_scale, b_scale=b_scale,
+                   rs=(e["sym_part"].ptrs, e["R"], self.rank, n, self.cfg.embed_dim))
+        else:
+            K.gemm(a, w, e["sym_part"].local[:n], a_scale=a_scale, b_scale=b_scale)
+
+    def _src(self, sess: Session, n: int) -> tuple:
+        """Where the owner finds row i of every rank's partial product (pointers, row offsets)."""
+        part = sess.extra["sym_part"]
+        if self.rs_mode == "push":
+            return [part.ptrs[self.rank]] * self.world, [s * n for s in range(self.world)]
+        return part.ptrs, [0] * self.world
 
     # -------------------------------------------------------------- approximate pass
     def approx_layer(self, sess: Session, l: int, x: torch.Tensor, x_out: torch.Tensor, server_pscore: str) -> None:
-        c, lw = self.cfg, self.w.layers[l]
-        B, N, Dh = sess.B, sess.N, c.head_dim
+        c, lw, comm = self.cfg, self.w.layers[l], self.comm
+        B, N, Dh, D = sess.B, sess.N, c.head_dim, c.embed_dim
         M = B * N
-        sym = sess.extra
-        part = sym["sym_part"].local
-        a, sa = self._norm(sess, x, lw.norm1_w, lw.norm1_b, sess.xn)
+        e = sess.extra
+        R = e["R"]
+        tm = self.timer
+        a, sa = self._gathered(sess, M)
         w, ws = self._w(lw, "qkv")
-        K.qkv_gemm(a, w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
-                   rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
+        with tm("a.qkv"):
+            K.qkv_gemm(a, w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
+                       rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         score = server_pscore not in ("none", "disabled")
-        self._attention_with_score(sess, l, self.local_heads, score, sym["sym_ps"].local)
-        a, sa = self._act(sess, sess.o)
+        with tm("a.attn"):
+            self._attention_with_score(sess, l, self.local_heads, score, e["sym_ps"].local)
+        with tm("a.quant"):
+            a, sa = self._act(sess, sess.o)
         w, ws = self._w(lw, "proj")
-        K.gemm(a, w, part, a_scale=sa, b_scale=ws)
-        bos = sym["sym_bos"]
-        off = l * M * c.embed_dim
-        self._reduce(sess, M, out=sym["sym_x"], aux=bos, aux_offset=off, aux_mode=K.AUX_SET, bias=lw.proj_b,
-                     gamma=lw.ls1, resid=x)
+        with tm("a.proj"):
+            self._row_gemm(sess, a, w, None, sa, ws, M)
+        with tm("a.barrier"):
+            comm.barrier()
         if score:  # every rank's local-head mean is ready (barrier above): average them
-            self.comm.mean_f32(sym["sym_ps"], sess.pscore[l])
-        a, sa = self._norm(sess, x, lw.norm2_w, lw.norm2_b, sess.xn)
-        self._mlp(lw, a, sess.h, sa)
-        a, sa = self._act(sess, sess.h)
+            comm.mean_f32(e["sym_ps"], sess.pscore[l])
+        with tm("a.row_ln_ag"):
+            comm.sp_row(M, D, R, src=self._src(sess, M), bias=lw.proj_b, gamma=lw.ls1, resid=x, out=x,
+                        aux=sess.bos[l], aux_mode=K.AUX_SET, ln_w=lw.norm2_w, ln_b=lw.norm2_b, eps=c.norm_eps,
+                        **self._ag(sess))
+        with tm("a.barrier"):
+            comm.barrier()
+        a, sa = self._gathered(sess, M)
+        with tm("a.w12"):
+            self._mlp(lw, a, sess.h, sa)
+        with tm("a.quant"):
+            a, sa = self._act(sess, sess.h)
         w, ws = self._w(lw, "fc2")
-        K.gemm(a, w, part, a_scale=sa, b_scale=ws)
-        self._reduce(sess, M, out=sym["sym_x"], aux=bos, aux_offset=off, aux_mode=K.AUX_ADD, bias=lw.fc2_b,
-                     gamma=lw.ls2, resid=x)
+        with tm("a.fc2"):
+            self._row_gemm(sess, a, w, None, sa, ws, M)
+        with tm("a.barrier"):
+            comm.barrier()
+        nxt = self.w.layers[l + 1] if l + 1 < sess.extra.get("approx_end", c.depth) else None
+        with tm("a.row_ln_ag"):
+            comm.sp_row(M, D, R, src=self._src(sess, M), bias=lw.fc2_b, gamma=lw.ls2, resid=x, out=x,
+                        aux=sess.bos[l], aux_mode=K.AUX_ADD,
+                        ln_w=nxt.norm1_w if nxt is not None else None, ln_b=nxt.norm1_b if nxt is not None else None,
+                        eps=c.norm_eps, **self._ag(sess))
+        if nxt is not None:
+            with tm("a.barrier"):
+                comm.barrier()
 
     def approx(self, sess: Session, start: int, end: int, server_pscore: str = "cls_attn_prob") -> torch.Tensor:
+        c = self.cfg
         if start == 0:
             sess.x.copy_(sess.x_in)
         self._set_pass(sess, "approx")
+        M = sess.B * sess.N
+        sess.extra["approx_end"] = end
+        if start < end:
+            lw = self.w.layers[start]
+            self.comm.sp_row(M, c.embed_dim, sess.extra["R"], x=sess.x, ln_w=lw.norm1_w, ln_b=lw.norm1_b,
+                             eps=c.norm_eps, **self._ag(sess))
+            self.comm.barrier()
         for l in range(start, end):
             self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
         sess.approx_done = max(sess.approx_done, end)
@@ -157,29 +225,63 @@ class ViTEngineTP(ViTEngine):
 
     # -------------------------------------------------------------- correction pass
     def correct_layer(self, sess: Session, l: int, x: torch.Tensor, upd: torch.Tensor, rows: torch.Tensor) -> None:
-        c, lw = self.cfg, self.w.layers[l]
-        B, N, Dh = sess.B, sess.N, c.head_dim
+        c, lw, comm = self.cfg, self.w.layers[l], self.comm
+        B, N, Dh, D = sess.B, sess.N, c.head_dim, c.embed_dim
         T = upd.shape[1]
         MT = B * T
-        sym = sess.extra
-        part = sym["sym_part"].local[:MT]
+        e = sess.extra
+        R = e["R"]
         x_act, x_att = sess.x_act[:MT], sess.x_att[:MT]
-        xn, q, o, h = sess.xn[:MT], sess.q[:MT], sess.o[:MT], sess.h[:MT]
-        a, sa = self._norm(sess, x, lw.norm1_w, lw.norm1_b, xn, rows=rows, copy_out=x_act)
-        K.add_(x, sess.bos[l])
+        q, o, h = sess.q[:MT], sess.o[:MT], sess.h[:MT]
+        # LN1 of the kept rows on their owners (raw rows kept as x_act), gathered everywhere
+        comm.sp_row(MT, D, R, tok=rows, x=x, copy_out=x_act, ln_w=lw.norm1_w, ln_b=lw.norm1_b, eps=c.norm_eps,
+                    **self._ag(sess))
+        lo, hi = self.rank * R, min((self.rank + 1) * R, B * N)
+        K.add_(x[lo:hi], sess.bos[l][lo:hi])
+        comm.barrier()
+        a, sa = self._gathered(sess, MT)
         w, ws = self._w(lw, "qkv")
         K.qkv_gemm(a, w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
                    kv_rows=rows, rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=self.local_heads, Dh=Dh)
         a, sa = self._act(sess, o)
         w, ws = self._w(lw, "proj")
-        K.gemm(a, w, part, a_scale=sa, b_scale=ws)
-        self._reduce(sess, MT, out=sym["sym_x_att"], bias=lw.proj_b, gamma=lw.ls1, resid=x_act)
-        a, sa = self._norm(sess, x_att, lw.norm2_w, lw.norm2_b, xn)
+        self._row_gemm(sess, a, w, rows, sa, ws, MT)
+        comm.barrier()
+        comm.sp_row(MT, D, R, tok=rows, src=self._src(sess, MT), bias=lw.proj_b, gamma=lw.ls1, resid=x_act,
+                    resid_tok=False, out=x_att, out_tok=False, ln_w=lw.norm2_w, ln_b=lw.norm2_b, eps=c.norm_eps,
+                    **self._ag(sess))
+        comm.barrier()
+        a, sa = self._gathered(sess, MT)
         self._mlp(lw, a, h, sa)
         a, sa = self._act(sess, h)
         w, ws = self._w(lw, "fc2")
-        K.gemm(a, w, part, a_scale=sa, b_scale=ws)
-        self._reduce(sess, MT, out=sym["sym_x"], out_rows=rows, aux=sym["sym_bos"],
-                     aux_offset=l * B * N * c.embed_dim, aux_mode=K.AUX_OUT_MINUS, bias=lw.fc2_b, gamma=lw.ls2,
-                     resid=x_att, resid2=x_act)
+        self._row_gemm(sess, a, w, rows, sa, ws, MT)
+        comm.barrier()
+        # x[row] = x_att + ls2 * mlp; increment[row] = (x_att - x_act) + ls2 * mlp  (owners)
+        comm.sp_row(MT, D, R, tok=rows, src=self._src(sess, MT), bias=lw.fc2_b, gamma=lw.ls2, resid=x_att,
+                    resid_tok=False, out=x, out_tok=True, aux=sess.bos[l], aux_mode=K.AUX_OUT_MINUS, resid2=x_act)
+
+    # -------------------------------------------------------------- outputs
+    def normed_tokens(self, sess: Session) -> torch.Tensor:
+        """Final LayerNorm of every token on its owner, gathered to every rank [B*N, D]."""
+        c = self.cfg
+        buf = sess.extra.get("sym_normed")
+        if buf is None:
+            buf = sess.extra["sym_normed"] = self.comm.empty((sess.B * sess.N, c.embed_dim), BF16)
+        self.comm.sp_row(sess.B * sess.N, c.embed_dim, sess.extra["R"], x=sess.x, ln_w=self.w.norm_w,
+                         ln_b=self.w.norm_b, eps=c.norm_eps, ag=buf)
+        self.comm.barrier()
+        return buf.local
+
+    def patch_features(self, sess: Session, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Final LayerNorm of the patch tokens on their owners, gathered to every rank [B*P, D]."""
+        c = self.cfg
+        feat = sess.extra["sym_feat"]
+        self.comm.sp_row(sess.B * sess.P, c.embed_dim, sess.extra["R"], tok=sess.patch_rows, x=sess.x,
+                         ln_w=self.w.norm_w, ln_b=self.w.norm_b, eps=c.norm_eps, ag=feat)
+        self.comm.barrier()
+        if out is not None:
+            out.copy_(feat.local)
+            return out
+        return feat.local

@@ -64,12 +64,8 @@ class DINOv3ClassifierExecutor(DINOv3BackboneMixin, ModelExecutor):
     def logits(self, context) -> torch.Tensor:
         if self.engine is not None:
             sess = context["session"]
-            c = self.cfg
-            buf = sess.extra.get("normed")
-            if buf is None:
-                buf = sess.extra["normed"] = torch.empty_like(sess.x)
-            K.layernorm(sess.x, self.engine.w.norm_w, self.engine.w.norm_b, c.norm_eps, buf)
-            return self.head_gpu.logits(buf, sess.B, sess.N, c.n_prefix)
+            buf = self.engine.normed_tokens(sess)
+            return self.head_gpu.logits(buf, sess.B, sess.N, self.cfg.n_prefix)
         with torch.no_grad():
             xn = self.backbone.final_norm(context["x"])
             npre = self.cfg.n_prefix

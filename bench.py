@@ -228,6 +228,9 @@ def run_mine(args, rank, world):
     torch.cuda.synchronize()
 
     clocks = ClockSampler() if rank == 0 else None
+    timer = getattr(ex.engine, "timer", None)
+    if timer is not None and timer.enabled:
+        timer.summary(reset=True)
     barrier(world)
     torch.cuda.synchronize()
     if clocks:
@@ -248,6 +251,9 @@ def run_mine(args, rank, world):
     ms = t0.elapsed_time(t1) / args.steps
     per_step = sorted(step_ev[i].elapsed_time(step_ev[i + 1]) for i in range(args.steps))
     ms_max = max_over_ranks(ms, world)
+    if timer is not None and timer.enabled:  # APPCORR_PHASE_TIMING=1: per-phase device ms per step
+        phases = {k: round(v / args.steps, 3) for k, v in sorted(timer.summary().items())}
+        print(json.dumps({"rank": rank, "phase_ms_per_step": phases}), file=sys.stderr)
 
     # ---- end-to-end through the public API: pinned host inputs in, labels out, every step
     e2e = None

@@ -37,7 +37,8 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
              optional<Tensor> k_out, optional<Tensor> v_out, optional<Tensor> kv_rows,
              optional<Tensor> tok_idx, int64_t seq_len, optional<Tensor> rope_sin, optional<Tensor> rope_cos,
              int64_t n_prefix, int64_t head_dim, int64_t max_ctas, optional<Tensor> a_scale,
-             optional<Tensor> b_scale, int64_t kv_dim) {
+             optional<Tensor> b_scale, int64_t kv_dim, std::vector<int64_t> rs_out, int64_t rs_rows_per_rank,
+             int64_t rs_rank, int64_t rs_slot_rows, int64_t rs_ld) {
   check_cuda(A, "A");
   check_cuda(B, "B");
   const bool fp8 = A.scalar_type() == at::kFloat8_e4m3fn;
@@ -89,6 +90,15 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
   ep.head_dim = static_cast<int>(head_dim);
   ep.a_scale = fp8 ? a_scale->data_ptr<float>() : nullptr;
   ep.b_scale = fp8 ? b_scale->data_ptr<float>() : nullptr;
+  if (!rs_out.empty()) {
+    TORCH_CHECK(epi == EPI_BF16 && rs_out.size() <= 8 && rs_rows_per_rank > 0 && rs_ld % 8 == 0,
+                "gemm: the reduce-scatter epilogue is EPI_BF16 with 1..8 slot buffers");
+    for (size_t r = 0; r < rs_out.size(); ++r) ep.rs_out[r] = reinterpret_cast<__nv_bfloat16*>(rs_out[r]);
+    ep.rs_rows_per_rank = static_cast<int>(rs_rows_per_rank);
+    ep.rs_rank = static_cast<int>(rs_rank);
+    ep.rs_slot_rows = rs_slot_rows;
+    ep.ldo = rs_ld;
+  }
   if (epi == EPI_QKV) {
     TORCH_CHECK(q_out && k_out && v_out, "qkv epilogue needs q_out, k_out, v_out");
     if (kv_dim > 0) {  // grouped-query: rows are [q (dim) | k (kv_dim) | v (kv_dim)]
@@ -107,7 +117,7 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
     TORCH_CHECK(head_dim == 64 || head_dim == 128, "qkv: head_dim must be 64 or 128");
     TORCH_CHECK(tile_n % head_dim == 0, "qkv: tile width must be a multiple of head_dim");
     TORCH_CHECK(tok_idx.has_value() || seq_len > 0, "qkv: need tok_idx or seq_len");
-  } else {
+  } else if (rs_out.empty()) {
     TORCH_CHECK(out.has_value(), "gemm: out is required");
     check_cuda(*out, "out");
     TORCH_CHECK(out->stride(1) == 1, "out must have unit inner stride");
@@ -137,7 +147,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_out") = py::none(), py::arg("kv_rows") = py::none(), py::arg("tok_idx") = py::none(),
         py::arg("seq_len") = 0, py::arg("rope_sin") = py::none(), py::arg("rope_cos") = py::none(),
         py::arg("n_prefix") = 0, py::arg("head_dim") = 128, py::arg("max_ctas") = 0,
-        py::arg("a_scale") = py::none(), py::arg("b_scale") = py::none(), py::arg("kv_dim") = 0);
+        py::arg("a_scale") = py::none(), py::arg("b_scale") = py::none(), py::arg("kv_dim") = 0,
+        py::arg("rs_out") = std::vector<int64_t>{}, py::arg("rs_rows_per_rank") = 0, py::arg("rs_rank") = 0,
+        py::arg("rs_slot_rows") = 0, py::arg("rs_ld") = 0);
   m.attr("EPI_BF16") = static_cast<int>(EPI_BF16);
   m.attr("EPI_F32") = static_cast<int>(EPI_F32);
   m.attr("EPI_GELU") = static_cast<int>(EPI_GELU);
@@ -151,5 +163,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_elementwise_ops(m);
   register_attention_ops(m);
   register_comm_ops(m);
+  register_sp_ops(m);
   register_attention_sm100_ops(m);
 }

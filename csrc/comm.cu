@@ -9,14 +9,9 @@
 //   tp_barrier          every rank stores `epoch` into slot [my_rank] of every peer's flag array,
 //                       then waits (bounded, ~1 s) until its own slots reach `epoch`; release /
 //                       acquire at system scope make the preceding writes visible
-//   tp_allreduce_epi    one-shot all-reduce fused with the block epilogue: rank r owns rows
-//                       [r*M/T, (r+1)*M/T); it sums the T peers' bf16 partial products of those
-//                       rows (peer loads), applies  delta = gamma * (sum + bias),
-//                       out = resid + delta, and the increment bookkeeping (aux := delta,
-//                       aux += delta, or aux := (resid - resid2) + delta), and stores out / aux
-//                       rows into every rank's replica (peer stores). Equivalent bytes to a
-//                       reduce-scatter + all-gather, in one kernel, with the epilogue fused.
-//   tp_allreduce_f32    small fp32 all-reduce (mean) of per-rank vectors (patch scores)
+//   tp_mean_f32         small fp32 all-reduce (mean) of per-rank vectors (patch scores)
+// The reduce-scatter and all-gather of the layer activations are fused into the GEMM epilogue
+// (csrc/gemm_sm100.cu, rs_out) and into the owner-side row kernel (csrc/tp_sp.cu).
 //
 // Every wait is bounded: on expiry the kernel records kErrTimeoutPeer in the caller's error word
 // and returns, so a missing peer surfaces as a host-side error instead of a hung GPU.
@@ -104,153 +99,11 @@ void tp_barrier_op(std::vector<int64_t> flag_ptrs, int64_t rank, int64_t epoch, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// ------------------------------------------------------------------------------ fused all-reduce
-struct ArEpi {
-  PeerPtrs part;        // bf16 [M, N] partial products, one per rank
-  long ldp;
-  PeerPtrs out;         // bf16 output replicas (row stride ldo), rows via out_rows
-  long ldo;
-  const int* out_rows;
-  PeerPtrs aux;         // bf16 increment replicas (row stride ldaux), rows via aux_rows
-  long ldaux;
-  const int* aux_rows;
-  int aux_mode;
-  const bf16* bias;
-  const bf16* gamma;    // nullptr: plain sum (+bias)
-  const bf16* resid;    // local, row m (or resid_rows[m])
-  long ldr;
-  const int* resid_rows;
-  const bf16* resid2;   // local, row m (AUX_OUT_MINUS)
-  long ldr2;
-  int M, N, world, rank;
-};
-
-__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
-  const uint32_t* w = &u.x;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 f = unpack_bf16x2(w[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
-  return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-}
-
-__global__ void tp_allreduce_epi_kernel(ArEpi e) {
-  const int rows_per = (e.M + e.world - 1) / e.world;
-  const int lo = e.rank * rows_per, hi = min(e.M, lo + rows_per);
-  const int n8 = e.N >> 3;
-  const long total = (long)max(hi - lo, 0) * n8;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const int m = lo + static_cast<int>(i / n8);
-    const int c = static_cast<int>(i - (long)(m - lo) * n8);
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int r = 0; r < e.world; ++r) {
-      const uint4 u = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(e.part.p[r]) + (long)m * e.ldp)[c];
-      float v[8];
-      unpack8(u, v);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] += v[j];
-    }
-    if (e.bias) {
-      float b[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(e.bias) + c), b);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] += b[j];
-    }
-    float o[8], d[8];
-    if (e.gamma) {
-      float g[8], rs[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(e.gamma) + c), g);
-      const long rr = e.resid_rows ? e.resid_rows[m] : m;
-      unpack8(reinterpret_cast<const uint4*>(e.resid + rr * e.ldr)[c], rs);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        d[j] = bf16_round(bf16_round(acc[j]) * g[j]);
-        o[j] = rs[j] + d[j];
-      }
-      if (e.aux_mode != AUX_NONE) {
-        const long ar = e.aux_rows ? e.aux_rows[m] : (e.out_rows ? e.out_rows[m] : m);
-        float a[8];
-        if (e.aux_mode == AUX_SET) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) a[j] = d[j];
-        } else if (e.aux_mode == AUX_ADD) {
-          unpack8(reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(e.aux.p[e.rank]) + ar * e.ldaux)[c], a);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) a[j] += d[j];
-        } else {
-          float r2[8];
-          unpack8(reinterpret_cast<const uint4*>(e.resid2 + (long)m * e.ldr2)[c], r2);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) a[j] = bf16_round(rs[j] - r2[j]) + d[j];
-        }
-        const uint4 pa = pack8(a);
-        for (int r = 0; r < e.world; ++r)
-          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(e.aux.p[r]) + ar * e.ldaux)[c] = pa;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = acc[j];
-    }
-    const long orow = e.out_rows ? e.out_rows[m] : m;
-    const uint4 po = pack8(o);
-    for (int r = 0; r < e.world; ++r)
-      reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(e.out.p[r]) + orow * e.ldo)[c] = po;
-  }
-}
-
 static PeerPtrs to_peers(const std::vector<int64_t>& v) {
   TORCH_CHECK(v.size() <= kMaxRanks, "at most 8 ranks");
   PeerPtrs p{};
   for (size_t i = 0; i < v.size(); ++i) p.p[i] = reinterpret_cast<void*>(v[i]);
   return p;
-}
-
-template <typename T = void>
-static const T* optp(const c10::optional<at::Tensor>& t) {
-  return (t.has_value() && t->defined()) ? reinterpret_cast<const T*>(t->data_ptr()) : nullptr;
-}
-
-void tp_allreduce_epi_op(std::vector<int64_t> part, int64_t ldp, std::vector<int64_t> out, int64_t ldo,
-                         c10::optional<at::Tensor> out_rows, std::vector<int64_t> aux, int64_t ldaux,
-                         c10::optional<at::Tensor> aux_rows, int64_t aux_mode, c10::optional<at::Tensor> bias,
-                         c10::optional<at::Tensor> gamma, c10::optional<at::Tensor> resid,
-                         c10::optional<at::Tensor> resid_rows, c10::optional<at::Tensor> resid2, int64_t M, int64_t N,
-                         int64_t rank) {
-  const int world = static_cast<int>(part.size());
-  TORCH_CHECK(out.size() == part.size() && (aux.empty() || aux.size() == part.size()), "peer lists must match");
-  TORCH_CHECK(N % 8 == 0 && ldp % 8 == 0 && ldo % 8 == 0, "allreduce_epi: N and strides multiples of 8");
-  if (gamma.has_value()) TORCH_CHECK(resid.has_value(), "allreduce_epi: gamma needs resid");
-  if (aux_mode == AUX_OUT_MINUS) TORCH_CHECK(resid2.has_value(), "allreduce_epi: AUX_OUT_MINUS needs resid2");
-  ArEpi e{};
-  e.part = to_peers(part);
-  e.ldp = ldp;
-  e.out = to_peers(out);
-  e.ldo = ldo;
-  e.out_rows = optp<int>(out_rows);
-  if (!aux.empty()) e.aux = to_peers(aux);
-  e.ldaux = ldaux;
-  e.aux_rows = optp<int>(aux_rows);
-  e.aux_mode = aux.empty() ? AUX_NONE : static_cast<int>(aux_mode);
-  e.bias = optp<bf16>(bias);
-  e.gamma = optp<bf16>(gamma);
-  e.resid = optp<bf16>(resid);
-  e.ldr = resid.has_value() ? resid->stride(0) : 0;
-  e.resid_rows = optp<int>(resid_rows);
-  e.resid2 = optp<bf16>(resid2);
-  e.ldr2 = resid2.has_value() ? resid2->stride(0) : 0;
-  e.M = static_cast<int>(M);
-  e.N = static_cast<int>(N);
-  e.world = world;
-  e.rank = static_cast<int>(rank);
-  if (M == 0) return;
-  const long work = ((M + world - 1) / world) * (N / 8);
-  const int grid = static_cast<int>(std::min<long>((work + 255) / 256, num_sms() * 4L));
-  tp_allreduce_epi_kernel<<<std::max(grid, 1), 256, 0, at::cuda::getCurrentCUDAStream()>>>(e);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // ------------------------------------------------------------------------------ small fp32 mean
@@ -280,10 +133,6 @@ void register_comm_ops(pybind11::module_& m) {
   m.def("ipc_free", &ipc_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("tp_barrier", &tp_barrier_op);
-  m.def("tp_allreduce_epi", &tp_allreduce_epi_op, py::arg("part"), py::arg("ldp"), py::arg("out"), py::arg("ldo"),
-        py::arg("out_rows"), py::arg("aux"), py::arg("ldaux"), py::arg("aux_rows"), py::arg("aux_mode"),
-        py::arg("bias"), py::arg("gamma"), py::arg("resid"), py::arg("resid_rows"), py::arg("resid2"), py::arg("M"),
-        py::arg("N"), py::arg("rank"));
   m.def("tp_mean_f32", &tp_mean_f32_op);
 }
 

@@ -256,7 +256,12 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
       if constexpr (EPI == EPI_F32) {
         store_f32x32(reinterpret_cast<float*>(ep.out) + (long)orow * ep.ldo + n, v);
       } else if constexpr (EPI == EPI_BF16) {
-        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + n, v);
+        if (ep.rs_out[0] != nullptr) {  // fused reduce-scatter: partial row to its owner's slot
+          const int owner = orow / ep.rs_rows_per_rank;
+          store_bf16x32(ep.rs_out[owner] + ((long)ep.rs_rank * ep.rs_slot_rows + m) * ep.ldo + n, v);
+        } else {
+          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + n, v);
+        }
       } else if constexpr (EPI == EPI_GELU) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = gelu_erf(bf16_round(v[j]));

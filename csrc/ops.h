@@ -42,6 +42,13 @@ struct GemmEpilogue {
   // FP8 operands: acc * a_scale[m] * b_scale[n] before the epilogue (nullptr: no scaling)
   const float* a_scale;
   const float* b_scale;
+  // reduce-scatter epilogue (EPI_BF16): row m is stored to rank owner = (out_rows ? out_rows[m] : m)
+  // / rs_rows_per_rank, into its slot buffer rs_out[owner] at row rs_rank * rs_slot_rows + m
+  // (a peer store over NVLink unless owner == rs_rank). rs_out[0] == nullptr: off.
+  __nv_bfloat16* rs_out[8];
+  int rs_rows_per_rank;
+  int rs_rank;
+  long rs_slot_rows;
 };
 
 struct GemmShape {
@@ -59,6 +66,7 @@ int num_sms();
 void register_elementwise_ops(pybind11::module_& m);
 void register_attention_ops(pybind11::module_& m);
 void register_comm_ops(pybind11::module_& m);
+void register_sp_ops(pybind11::module_& m);
 void register_attention_sm100_ops(pybind11::module_& m);
 
 }  // namespace appcorr

@@ -1,0 +1,351 @@
+// Sequence-parallel tensor-parallel row kernel: the owner-side half of the fused
+// GEMM -> reduce-scatter and the producer side of the all-gather -> GEMM, over NVLink peer memory.
+//
+// Layout (appcorr_b200/parallel/tp.py): the residual stream is split by rows; rank r owns token
+// rows [r*R, (r+1)*R). The row-parallel GEMMs (attention proj, MLP fc2) produce bf16 partial
+// products; the reduce-scatter is finished here by the owner of each row, either
+//   pull: every rank's GEMM writes its partial locally; the owner loads row i of every peer's
+//         partial over NVLink (16-byte coalesced peer loads), or
+//   push: the GEMM epilogue (csrc/gemm_sm100.cu, GemmEpilogue::rs_out) stores each partial row
+//         into the owner's slot buffer over NVLink while the GEMM runs; the owner loads locally.
+// After a barrier the owner runs this kernel, one CTA per (packed) row i:
+//
+//   reduce   acc = sum_src partial[src][i] + bias;  d = gamma * acc;  o = resid + d
+//            out := o; increment bookkeeping on the owner's rows (aux := d | aux += d |
+//            aux := (resid - resid2) + d)
+//   or load  o = x[tok(i)]  (copy_out[i] := o)
+//   then     optional LayerNorm / RMSNorm of o, quantised to e4m3 with one scale per row (or
+//            kept bf16), stored into row i of EVERY rank's gather buffer (peer stores): the
+//            all-gather that feeds the next column-parallel GEMM, fused into its producer.
+//
+// Rows whose token is owned by another rank return immediately, so the same launch serves the
+// contiguous approximate pass (tok(i) = i) and the packed correction rows (tok(i) = rows[i]).
+// Reference: none (the reference is single-GPU); the per-row math is that of the block epilogue
+// (block.py:1146-1191) and LayerNorm.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cfloat>
+#include <cuda_fp8.h>
+
+#include "sm100_common.cuh"
+#include "ops.h"
+
+namespace appcorr {
+
+using bf16 = __nv_bfloat16;
+constexpr int kSpThreads = 128;
+constexpr int kSpMaxVec = 8;  // D <= 128 * 8 * 8 = 8192
+constexpr int kSpMaxRanks = 8;
+
+struct SpArgs {
+  // rows
+  int M;                    // packed rows
+  const int* tok;           // packed row -> token row (nullptr: identity)
+  int rows_per_rank, rank, world;
+  int D;
+  // reduce
+  int reduce;               // 1: sum the partial rows; 0: load x[tok]
+  const bf16* src[kSpMaxRanks];  // partial row i of source s at src[s] + (src_off[s] + i) * D:
+  long src_off[kSpMaxRanks];     // local slots (push) or the peers' own partial buffers (pull)
+  const bf16* bias;
+  const bf16* gamma;        // nullptr: d = acc
+  const bf16* resid;        // resid row = tok (resid_tok) or i
+  long ldr;
+  int resid_tok;
+  const bf16* resid2;       // packed i (AUX_OUT_MINUS)
+  long ldr2;
+  bf16* out;                // out row = tok (out_tok) or i
+  long ldo;
+  int out_tok;
+  bf16* aux;                // row tok
+  long ldaux;
+  int aux_mode;
+  // load mode
+  const bf16* x;            // row tok
+  long ldx;
+  bf16* copy_out;           // row i
+  long ldc;
+  // norm + all-gather
+  const bf16* ln_w;         // nullptr: no norm / gather
+  const bf16* ln_b;
+  float eps;
+  int rms;
+  int fp8;
+  void* ag[kSpMaxRanks];    // gather buffers (row i), bf16 or e4m3
+  long ld_ag;               // elements
+  float* ag_scale[kSpMaxRanks];
+};
+
+__device__ __forceinline__ void sp_unpack8(const uint4& u, float (&v)[8]) {
+  const uint32_t* w = &u.x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16x2(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ uint4 sp_pack8(const float (&v)[8]) {
+  return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+}
+__device__ __forceinline__ uint32_t sp_e4m3x4(float a, float b, float c, float d) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+
+template <bool MAX>
+__device__ __forceinline__ float sp_block_reduce(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = MAX ? fmaxf(v, w) : v + w;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < kSpThreads / 32 ? red[lane] : (MAX ? 0.f : 0.f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, t, o);
+    t = MAX ? fmaxf(t, w) : t + w;
+  }
+  return t;
+}
+
+// NV: 16-byte vectors per thread (D <= 1024 * NV). Rows [row0, row0 + gridDim.x) are visited.
+template <int NV>
+__global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0) {
+  __shared__ float red[kSpThreads / 32];
+  const int i = row0 + blockIdx.x;
+  if (i >= a.M) return;
+  const int tok = a.tok ? a.tok[i] : i;
+  if (tok < 0 || tok / a.rows_per_rank != a.rank) return;  // another rank owns this row
+  const int nvec = a.D >> 3;
+  float v[NV][8];
+  if (a.reduce) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int c = threadIdx.x + k * kSpThreads;
+      if (c >= nvec) continue;
+      // issue the partial-row loads of every source before summing (peer loads in flight together)
+      uint4 u[kSpMaxRanks];
+#pragma unroll
+      for (int s = 0; s < kSpMaxRanks; ++s)
+        if (s < a.world) u[s] = reinterpret_cast<const uint4*>(a.src[s] + (a.src_off[s] + i) * a.D)[c];
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int s = 0; s < kSpMaxRanks; ++s) {
+        if (s >= a.world) break;
+        float p[8];
+        sp_unpack8(u[s], p);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += p[j];
+      }
+      if (a.bias) {
+        float b[8];
+        sp_unpack8(__ldg(reinterpret_cast<const uint4*>(a.bias) + c), b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += b[j];
+      }
+      float d[8], o[8];
+      const long rr = a.resid_tok ? tok : i;
+      float rs[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (a.resid) sp_unpack8(reinterpret_cast<const uint4*>(a.resid + rr * a.ldr)[c], rs);
+      if (a.gamma) {
+        float g[8];
+        sp_unpack8(__ldg(reinterpret_cast<const uint4*>(a.gamma) + c), g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d[j] = bf16_round(bf16_round(acc[j]) * g[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d[j] = bf16_round(acc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = bf16_round(rs[j] + d[j]);
+      if (a.aux_mode != AUX_NONE) {
+        uint4* ap = reinterpret_cast<uint4*>(a.aux + (long)tok * a.ldaux) + c;
+        float x[8];
+        if (a.aux_mode == AUX_SET) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] = d[j];
+        } else if (a.aux_mode == AUX_ADD) {
+          sp_unpack8(*ap, x);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] += d[j];
+        } else {
+          float r2[8];
+          sp_unpack8(reinterpret_cast<const uint4*>(a.resid2 + (long)i * a.ldr2)[c], r2);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] = bf16_round(rs[j] - r2[j]) + d[j];
+        }
+        *ap = sp_pack8(x);
+      }
+      const long orow = a.out_tok ? tok : i;
+      reinterpret_cast<uint4*>(a.out + orow * a.ldo)[c] = sp_pack8(o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[k][j] = o[j];
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int c = threadIdx.x + k * kSpThreads;
+      if (c >= nvec) continue;
+      const uint4 u = reinterpret_cast<const uint4*>(a.x + (long)tok * a.ldx)[c];
+      if (a.copy_out) reinterpret_cast<uint4*>(a.copy_out + (long)i * a.ldc)[c] = u;
+      sp_unpack8(u, v[k]);
+    }
+  }
+  if (a.ln_w == nullptr) return;
+  // ---- LayerNorm / RMSNorm of the finished row, then the all-gather stores
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+    if (threadIdx.x + k * kSpThreads < nvec)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[k][j];
+  const float mean = a.rms ? 0.f : sp_block_reduce<false>(s, red) / a.D;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+    if (threadIdx.x + k * kSpThreads < nvec)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float dd = v[k][j] - mean;
+        q += dd * dd;
+      }
+  const float rstd = rsqrtf(sp_block_reduce<false>(q, red) / a.D + a.eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int c = threadIdx.x + k * kSpThreads;
+    if (c >= nvec) continue;
+    float w[8], b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    sp_unpack8(__ldg(reinterpret_cast<const uint4*>(a.ln_w) + c), w);
+    if (a.ln_b) sp_unpack8(__ldg(reinterpret_cast<const uint4*>(a.ln_b) + c), b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[k][j] = bf16_round((v[k][j] - mean) * rstd * w[j] + b[j]);
+      amax = fmaxf(amax, fabsf(v[k][j]));
+    }
+  }
+  if (a.fp8) {
+    amax = sp_block_reduce<true>(amax, red);
+    const float sc = fmaxf(amax, 1e-12f) / 448.f;
+    const float inv = 1.f / sc;
+    if (threadIdx.x < a.world) a.ag_scale[threadIdx.x][i] = sc;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int c = threadIdx.x + k * kSpThreads;
+      if (c >= nvec) continue;
+      const uint2 pk = make_uint2(sp_e4m3x4(v[k][0] * inv, v[k][1] * inv, v[k][2] * inv, v[k][3] * inv),
+                                  sp_e4m3x4(v[k][4] * inv, v[k][5] * inv, v[k][6] * inv, v[k][7] * inv));
+      for (int r = 0; r < a.world; ++r)
+        reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(a.ag[r]) + (long)i * a.ld_ag)[c] = pk;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int c = threadIdx.x + k * kSpThreads;
+      if (c >= nvec) continue;
+      const uint4 pk = sp_pack8(v[k]);
+      for (int r = 0; r < a.world; ++r)
+        reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.ag[r]) + (long)i * a.ld_ag)[c] = pk;
+    }
+  }
+}
+
+template <typename T = void>
+static T* sp_opt(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, int64_t rank, int64_t world, int64_t D,
+               std::vector<int64_t> src, std::vector<int64_t> src_off, c10::optional<at::Tensor> bias,
+               c10::optional<at::Tensor> gamma, c10::optional<at::Tensor> resid, bool resid_tok,
+               c10::optional<at::Tensor> resid2, c10::optional<at::Tensor> out, bool out_tok,
+               c10::optional<at::Tensor> aux, int64_t aux_mode, c10::optional<at::Tensor> x,
+               c10::optional<at::Tensor> copy_out, c10::optional<at::Tensor> ln_w, c10::optional<at::Tensor> ln_b,
+               double eps, bool rms, bool fp8, std::vector<int64_t> ag, int64_t ld_ag, std::vector<int64_t> ag_scale) {
+  TORCH_CHECK(D % 8 == 0 && D <= kSpThreads * kSpMaxVec * 8, "sp_row: D % 8 == 0 and D <= 8192");
+  TORCH_CHECK(world >= 1 && world <= kSpMaxRanks, "sp_row: 1..8 ranks");
+  SpArgs a{};
+  a.M = static_cast<int>(M);
+  a.tok = sp_opt<const int>(tok);
+  a.rows_per_rank = static_cast<int>(rows_per_rank);
+  a.rank = static_cast<int>(rank);
+  a.world = static_cast<int>(world);
+  a.D = static_cast<int>(D);
+  a.reduce = src.empty() ? 0 : 1;
+  if (a.reduce) {
+    TORCH_CHECK(out.has_value(), "sp_row: reduce needs out");
+    TORCH_CHECK(static_cast<int64_t>(src.size()) == world && src_off.size() == src.size(),
+                "sp_row: one partial source (and row offset) per rank");
+    for (int r = 0; r < world; ++r) {
+      a.src[r] = reinterpret_cast<const bf16*>(src[r]);
+      a.src_off[r] = src_off[r];
+    }
+    a.bias = sp_opt<const bf16>(bias);
+    a.gamma = sp_opt<const bf16>(gamma);
+    a.resid = sp_opt<const bf16>(resid);
+    a.ldr = resid.has_value() ? resid->stride(0) : 0;
+    a.resid_tok = resid_tok ? 1 : 0;
+    a.resid2 = sp_opt<const bf16>(resid2);
+    a.ldr2 = resid2.has_value() ? resid2->stride(0) : 0;
+    a.out = sp_opt<bf16>(out);
+    a.ldo = out->stride(0);
+    a.out_tok = out_tok ? 1 : 0;
+    a.aux = sp_opt<bf16>(aux);
+    a.ldaux = aux.has_value() ? aux->stride(0) : 0;
+    a.aux_mode = aux.has_value() ? static_cast<int>(aux_mode) : AUX_NONE;
+    if (a.aux_mode == AUX_OUT_MINUS) TORCH_CHECK(a.resid2 && a.resid, "sp_row: AUX_OUT_MINUS needs resid, resid2");
+  } else {
+    TORCH_CHECK(x.has_value(), "sp_row: load mode needs x");
+    a.x = sp_opt<const bf16>(x);
+    a.ldx = x->stride(0);
+    a.copy_out = sp_opt<bf16>(copy_out);
+    a.ldc = copy_out.has_value() ? copy_out->stride(0) : 0;
+  }
+  a.ln_w = sp_opt<const bf16>(ln_w);
+  a.ln_b = sp_opt<const bf16>(ln_b);
+  a.eps = static_cast<float>(eps);
+  a.rms = rms ? 1 : 0;
+  a.fp8 = fp8 ? 1 : 0;
+  if (a.ln_w) {
+    TORCH_CHECK(static_cast<int64_t>(ag.size()) == world, "sp_row: one gather buffer per rank");
+    for (int r = 0; r < world; ++r) a.ag[r] = reinterpret_cast<void*>(ag[r]);
+    a.ld_ag = ld_ag;
+    if (fp8) {
+      TORCH_CHECK(static_cast<int64_t>(ag_scale.size()) == world, "sp_row: one scale buffer per rank");
+      for (int r = 0; r < world; ++r) a.ag_scale[r] = reinterpret_cast<float*>(ag_scale[r]);
+    }
+  }
+  if (M == 0) return;
+  // contiguous rows (no token map): only this rank's block [rank*R, (rank+1)*R) is visited
+  int row0 = 0, nrows = static_cast<int>(M);
+  if (a.tok == nullptr) {
+    row0 = static_cast<int>(std::min<int64_t>(M, rank * rows_per_rank));
+    nrows = static_cast<int>(std::min<int64_t>(M, (rank + 1) * rows_per_rank)) - row0;
+    if (nrows <= 0) return;
+  }
+  const int nv = (static_cast<int>(D) / 8 + kSpThreads - 1) / kSpThreads;
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (nv <= 1) sp_row_kernel<1><<<nrows, kSpThreads, 0, st>>>(a, row0);
+  else if (nv <= 2) sp_row_kernel<2><<<nrows, kSpThreads, 0, st>>>(a, row0);
+  else if (nv <= 4) sp_row_kernel<4><<<nrows, kSpThreads, 0, st>>>(a, row0);
+  else sp_row_kernel<8><<<nrows, kSpThreads, 0, st>>>(a, row0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void register_sp_ops(pybind11::module_& m) {
+  namespace py = pybind11;
+  m.def("sp_row", &sp_row_op, py::arg("M"), py::arg("tok"), py::arg("rows_per_rank"), py::arg("rank"),
+        py::arg("world"), py::arg("D"), py::arg("src"), py::arg("src_off"), py::arg("bias"), py::arg("gamma"),
+        py::arg("resid"), py::arg("resid_tok"), py::arg("resid2"), py::arg("out"), py::arg("out_tok"),
+        py::arg("aux"), py::arg("aux_mode"), py::arg("x"), py::arg("copy_out"), py::arg("ln_w"), py::arg("ln_b"),
+        py::arg("eps"), py::arg("rms"), py::arg("fp8"), py::arg("ag"), py::arg("ld_ag"), py::arg("ag_scale"));
+}
+
+}  // namespace appcorr

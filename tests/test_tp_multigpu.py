@@ -15,7 +15,8 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, precision="bf16", rs_mode="pull"):
+    os.environ["APPCORR_TP_RS"] = rs_mode
     import torch.distributed as dist
 
     from appcorr_b200.models.dinov3.vit import ViTConfig
@@ -30,8 +31,11 @@ def _worker(rank, world, port, q):
                     layerscale_init=0.3)
     full = random_weights(cfg, dev, seed=3, std=0.05)
     comm = TPComm(device=dev)
-    tp = ViTEngineTP.from_full(full, comm)
-    ref = ViTEngine(full, dev)
+    tp = ViTEngineTP.from_full(full, comm, precision)
+    # fp8: per-channel scales of a split weight differ from the full weight's, so the reference
+    # is the bf16 single-GPU engine and every token is corrected (a fixed plan)
+    ref = ViTEngine(random_weights(cfg, dev, seed=3, std=0.05), dev, "bf16")
+    keep = 0.5 if precision == "bf16" else 1.0
     B, H, W = 2, 64, 96
     g = torch.Generator(device=dev).manual_seed(0)
     img0 = torch.randint(0, 256, (B, H, W, 3), dtype=torch.uint8, device=dev, generator=g)
@@ -41,35 +45,43 @@ def _worker(rank, world, port, q):
         s = eng.new_session(B, H, W)
         eng.prepare_tokens(s, img0)
         eng.approx(s, 0, cfg.depth)
-        xa = s.x.clone()
+        # the tensor-parallel residual stream is split by rows: compare the final-normed tokens,
+        # which both engines produce for every row
+        xa = eng.normed_tokens(s).clone()
         eng.prepare_tokens(s, img1)
         pre = torch.arange(cfg.n_prefix, dtype=torch.int32, device=dev).repeat(B, 1).contiguous()
         cand = torch.arange(cfg.n_prefix, s.N, dtype=torch.int32, device=dev).repeat(B, 1).contiguous()
-        xc = eng.correct(s, 0, cfg.depth, pre, cand, {"token_keep_ratio": 0.5, "server_pscore": "cls_attn_prob_layermean"})
+        eng.correct(s, 0, cfg.depth, pre, cand, {"token_keep_ratio": keep, "server_pscore": "cls_attn_prob_layermean"})
+        xc = eng.normed_tokens(s).clone()
         torch.cuda.synchronize()
-        outs.append((xa, xc.clone(), s.pscore.clone()))
+        outs.append((xa, xc, s.pscore.clone()))
     comm.check()
     (ra, rc, rp), (ta, tc, tpp) = outs
     rel = lambda a, b: ((a.float() - b.float()).norm() / b.float().norm()).item()  # noqa: E731
     q.put((rank, rel(ta, ra), rel(tc, rc), rel(tpp, rp)))
+    print("tp-vs-single", precision, rank, rel(ta, ra), rel(tc, rc), rel(tpp, rp), flush=True)
     dist.barrier()
     comm.close()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_single_gpu():
+@pytest.mark.parametrize("precision,rs_mode", [("bf16", "pull"), ("bf16", "push"), ("fp8", "pull")])
+def test_tp2_matches_single_gpu(precision, rs_mode):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, precision, rs_mode)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
+    # fp8: per-channel weight scales differ between a full and a split weight, so the two runs
+    # quantise differently; compare at the fp8 noise level
+    tol = (2e-2, 3e-2, 1e-2) if precision == "bf16" else (1.2e-1, 1.2e-1, 1e-1)
     for rank, a, c, ps in res:
-        assert a < 2e-2 and c < 3e-2 and ps < 1e-2, (rank, a, c, ps)
+        assert a < tol[0] and c < tol[1] and ps < tol[2], (rank, a, c, ps)
