@@ -3,6 +3,8 @@
     python -m appcorr_b200.ops.bench_kernels gemm --M 8232 --N 12288 --K 4096 [--bn 256] [--epi bf16]
     python -m appcorr_b200.ops.bench_kernels attention --B 8 --H 32 --Dh 128 --Tq 1029 --Tk 1029
     python -m appcorr_b200.ops.bench_kernels layernorm --M 8232 --D 4096
+    python -m appcorr_b200.ops.bench_kernels sp_row --M 8232 --D 4096 --world 2   (tensor-parallel
+        owner row kernel, every "peer" emulated by a local buffer on this GPU)
     ... --once    launch the kernel exactly once (for `ncu -k ... -c 1`)
 
 Prints one JSON line: time per launch (ms), achieved TFLOP/s or GB/s, and the library
@@ -33,7 +35,8 @@ def _time(fn, iters: int, warmup: int = 3) -> float:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "attention", "layernorm"])
+    ap.add_argument("op", choices=["gemm", "attention", "layernorm", "sp_row"])
+    ap.add_argument("--world", type=int, default=2)
     ap.add_argument("--M", type=int, default=8232)
     ap.add_argument("--N", type=int, default=12288)
     ap.add_argument("--K", type=int, default=4096)
@@ -87,6 +90,25 @@ def main(argv=None) -> None:
         else:
             ref = None
         res.update(B=a.B, H=a.H, Dh=a.Dh, Tq=a.Tq, Tk=a.Tk, impl=a.impl)
+    elif a.op == "sp_row":
+        from .native import lib
+
+        W, M, D = a.world, a.M, a.D
+        R = (M + W - 1) // W
+        parts = [torch.randn(M, D, device=dev).to(torch.bfloat16) for _ in range(W)]
+        x = torch.randn(M, D, device=dev).to(torch.bfloat16)
+        aux = torch.zeros(M, D, device=dev, dtype=torch.bfloat16)
+        vec = torch.ones(D, device=dev, dtype=torch.bfloat16)
+        ag = [torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn) for _ in range(W)]
+        ags = [torch.empty(M, device=dev) for _ in range(W)]
+        fn = lambda: lib().sp_row(M, None, R, 0, W, D, [p.data_ptr() for p in parts], [0] * W, vec, vec, x, True,  # noqa: E731
+                                  None, x, True, aux, K.AUX_ADD, None, None, vec, vec, 1e-6, False, True,
+                                  [t.data_ptr() for t in ag], D, [t.data_ptr() for t in ags])
+        flops = 0.0
+        rows = R
+        res.update(M=M, D=D, world=W, rows=rows,
+                   bytes=rows * D * (2 * W + 2 + 4 + 2) + rows * D * W)  # partials, resid, aux rw, out, e4m3 gather
+        ref = None
     else:
         x = torch.randn(a.M, a.D, device=dev).to(torch.bfloat16)
         wt = torch.ones(a.D, device=dev, dtype=torch.bfloat16)

@@ -84,9 +84,11 @@ class ViTEngineTP(ViTEngine):
         self.timer = PhaseTimer.from_env()
         # reduce-scatter of the row-parallel GEMMs: "pull" (owner loads peers' partials in the row
         # kernel) or "push" (GEMM epilogue stores partial rows into the owner's slots)
+        # "ce": contiguous row blocks (approximate pass) travel by copy-engine peer copies into the
+        # owners' slots, packed correction rows are pulled
         self.rs_mode = os.environ.get("APPCORR_TP_RS", "pull")
-        if self.rs_mode not in ("pull", "push"):
-            raise ValueError("APPCORR_TP_RS must be 'pull' or 'push'")
+        if self.rs_mode not in ("pull", "push", "ce"):
+            raise ValueError("APPCORR_TP_RS must be 'pull', 'push' or 'ce'")
 
     @classmethod
     def from_full(cls, full: EngineWeights, comm: TPComm, precision="bf16") -> "ViTEngineTP":
@@ -114,6 +116,7 @@ class ViTEngineTP(ViTEngine):
         sess.extra.update({
             "R": R, "sym_xg": xg, "sym_xg8": xg8, "sym_xg_scale": comm.empty((M,), torch.float32),
             "sym_part": (comm.empty((self.world, M, D), BF16) if self.rs_mode == "push" else comm.empty((M, D), BF16)),
+            "sym_slot": comm.empty((self.world, M, D), BF16) if self.rs_mode == "ce" else None,
             "sym_ps": comm.empty((B, sess.N), torch.float32),
             "sym_feat": comm.empty((B * sess.P, D), BF16)})
         # head-split buffers
@@ -148,11 +151,35 @@ class ViTEngineTP(ViTEngine):
         else:
             K.gemm(a, w, e["sym_part"].local[:n], a_scale=a_scale, b_scale=b_scale)
 
-    def _src(self, sess: Session, n: int) -> tuple:
+    def _ce_scatter(self, sess: Session, n: int) -> None:
+        """Copy-engine reduce-scatter of a contiguous partial product: row block p (owned by rank
+        p) goes to slot [my rank] of rank p with one peer cudaMemcpyAsync per peer."""
+        e = sess.extra
+        views = e.get("slot_views")
+        if views is None:
+            from ..ops.native import lib
+
+            slot = e["sym_slot"]
+            views = e["slot_views"] = [lib().tensor_from_ptr(p, [self.world * n, self.cfg.embed_dim], BF16,
+                                                             self.device.index) for p in slot.ptrs]
+        R, part = e["R"], e["sym_part"].local
+        for p in range(self.world):
+            if p == self.rank:
+                continue
+            lo, hi = p * R, min((p + 1) * R, n)
+            if hi > lo:
+                views[p][self.rank * n + lo:self.rank * n + hi].copy_(part[lo:hi], non_blocking=True)
+
+    def _src(self, sess: Session, n: int, contiguous: bool = False) -> tuple:
         """Where the owner finds row i of every rank's partial product (pointers, row offsets)."""
-        part = sess.extra["sym_part"]
+        e = sess.extra
+        part = e["sym_part"]
         if self.rs_mode == "push":
             return [part.ptrs[self.rank]] * self.world, [s * n for s in range(self.world)]
+        if self.rs_mode == "ce" and contiguous:
+            ptrs = [e["sym_slot"].ptrs[self.rank]] * self.world
+            ptrs[self.rank] = part.ptrs[self.rank]
+            return ptrs, [s * n if s != self.rank else 0 for s in range(self.world)]
         return part.ptrs, [0] * self.world
 
     # -------------------------------------------------------------- approximate pass
@@ -176,12 +203,15 @@ class ViTEngineTP(ViTEngine):
         w, ws = self._w(lw, "proj")
         with tm("a.proj"):
             self._row_gemm(sess, a, w, None, sa, ws, M)
+        if self.rs_mode == "ce":
+            with tm("a.rs_copy"):
+                self._ce_scatter(sess, M)
         with tm("a.barrier"):
             comm.barrier()
         if score:  # every rank's local-head mean is ready (barrier above): average them
             comm.mean_f32(e["sym_ps"], sess.pscore[l])
         with tm("a.row_ln_ag"):
-            comm.sp_row(M, D, R, src=self._src(sess, M), bias=lw.proj_b, gamma=lw.ls1, resid=x, out=x,
+            comm.sp_row(M, D, R, src=self._src(sess, M, contiguous=True), bias=lw.proj_b, gamma=lw.ls1, resid=x, out=x,
                         aux=sess.bos[l], aux_mode=K.AUX_SET, ln_w=lw.norm2_w, ln_b=lw.norm2_b, eps=c.norm_eps,
                         **self._ag(sess))
         with tm("a.barrier"):
@@ -194,11 +224,14 @@ class ViTEngineTP(ViTEngine):
         w, ws = self._w(lw, "fc2")
         with tm("a.fc2"):
             self._row_gemm(sess, a, w, None, sa, ws, M)
+        if self.rs_mode == "ce":
+            with tm("a.rs_copy"):
+                self._ce_scatter(sess, M)
         with tm("a.barrier"):
             comm.barrier()
         nxt = self.w.layers[l + 1] if l + 1 < sess.extra.get("approx_end", c.depth) else None
         with tm("a.row_ln_ag"):
-            comm.sp_row(M, D, R, src=self._src(sess, M), bias=lw.fc2_b, gamma=lw.ls2, resid=x, out=x,
+            comm.sp_row(M, D, R, src=self._src(sess, M, contiguous=True), bias=lw.fc2_b, gamma=lw.ls2, resid=x, out=x,
                         aux=sess.bos[l], aux_mode=K.AUX_ADD,
                         ln_w=nxt.norm1_w if nxt is not None else None, ln_b=nxt.norm1_b if nxt is not None else None,
                         eps=c.norm_eps, **self._ag(sess))

@@ -115,8 +115,10 @@ __device__ __forceinline__ float sp_block_reduce(float v, float* red) {
   return t;
 }
 
-// NV: 16-byte vectors per thread (D <= 1024 * NV). Rows [row0, row0 + gridDim.x) are visited.
-template <int NV>
+// NV: 16-byte vectors per thread (D <= 1024 * NV); W: ranks (partial sources). The finished row is
+// held as packed bf16 (it is bf16-rounded anyway) to keep registers low. Rows
+// [row0, row0 + gridDim.x) are visited.
+template <int NV, int W>
 __global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0) {
   __shared__ float red[kSpThreads / 32];
   const int i = row0 + blockIdx.x;
@@ -124,21 +126,19 @@ __global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0) 
   const int tok = a.tok ? a.tok[i] : i;
   if (tok < 0 || tok / a.rows_per_rank != a.rank) return;  // another rank owns this row
   const int nvec = a.D >> 3;
-  float v[NV][8];
+  uint4 vb[NV];
   if (a.reduce) {
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int c = threadIdx.x + k * kSpThreads;
       if (c >= nvec) continue;
       // issue the partial-row loads of every source before summing (peer loads in flight together)
-      uint4 u[kSpMaxRanks];
+      uint4 u[W];
 #pragma unroll
-      for (int s = 0; s < kSpMaxRanks; ++s)
-        if (s < a.world) u[s] = reinterpret_cast<const uint4*>(a.src[s] + (a.src_off[s] + i) * a.D)[c];
+      for (int s = 0; s < W; ++s) u[s] = reinterpret_cast<const uint4*>(a.src[s] + (a.src_off[s] + i) * a.D)[c];
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-      for (int s = 0; s < kSpMaxRanks; ++s) {
-        if (s >= a.world) break;
+      for (int s = 0; s < W; ++s) {
         float p[8];
         sp_unpack8(u[s], p);
 #pragma unroll
@@ -184,18 +184,16 @@ __global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0) 
         *ap = sp_pack8(x);
       }
       const long orow = a.out_tok ? tok : i;
-      reinterpret_cast<uint4*>(a.out + orow * a.ldo)[c] = sp_pack8(o);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[k][j] = o[j];
+      vb[k] = sp_pack8(o);
+      reinterpret_cast<uint4*>(a.out + orow * a.ldo)[c] = vb[k];
     }
   } else {
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int c = threadIdx.x + k * kSpThreads;
       if (c >= nvec) continue;
-      const uint4 u = reinterpret_cast<const uint4*>(a.x + (long)tok * a.ldx)[c];
-      if (a.copy_out) reinterpret_cast<uint4*>(a.copy_out + (long)i * a.ldc)[c] = u;
-      sp_unpack8(u, v[k]);
+      vb[k] = reinterpret_cast<const uint4*>(a.x + (long)tok * a.ldx)[c];
+      if (a.copy_out) reinterpret_cast<uint4*>(a.copy_out + (long)i * a.ldc)[c] = vb[k];
     }
   }
   if (a.ln_w == nullptr) return;
@@ -203,46 +201,57 @@ __global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0) 
   float s = 0.f;
 #pragma unroll
   for (int k = 0; k < NV; ++k)
-    if (threadIdx.x + k * kSpThreads < nvec)
+    if (threadIdx.x + k * kSpThreads < nvec) {
+      float v[8];
+      sp_unpack8(vb[k], v);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s += v[k][j];
+      for (int j = 0; j < 8; ++j) s += v[j];
+    }
   const float mean = a.rms ? 0.f : sp_block_reduce<false>(s, red) / a.D;
   float q = 0.f;
 #pragma unroll
   for (int k = 0; k < NV; ++k)
-    if (threadIdx.x + k * kSpThreads < nvec)
+    if (threadIdx.x + k * kSpThreads < nvec) {
+      float v[8];
+      sp_unpack8(vb[k], v);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float dd = v[k][j] - mean;
+        const float dd = v[j] - mean;
         q += dd * dd;
       }
+    }
   const float rstd = rsqrtf(sp_block_reduce<false>(q, red) / a.D + a.eps);
   float amax = 0.f;
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int c = threadIdx.x + k * kSpThreads;
     if (c >= nvec) continue;
-    float w[8], b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float v[8], w[8], b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    sp_unpack8(vb[k], v);
     sp_unpack8(__ldg(reinterpret_cast<const uint4*>(a.ln_w) + c), w);
     if (a.ln_b) sp_unpack8(__ldg(reinterpret_cast<const uint4*>(a.ln_b) + c), b);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      v[k][j] = bf16_round((v[k][j] - mean) * rstd * w[j] + b[j]);
-      amax = fmaxf(amax, fabsf(v[k][j]));
+      v[j] = (v[j] - mean) * rstd * w[j] + b[j];
+      amax = fmaxf(amax, fabsf(bf16_round(v[j])));
     }
+    vb[k] = sp_pack8(v);  // the normalised row, bf16-rounded (the bf16 path's GEMM operand)
   }
   if (a.fp8) {
     amax = sp_block_reduce<true>(amax, red);
     const float sc = fmaxf(amax, 1e-12f) / 448.f;
     const float inv = 1.f / sc;
-    if (threadIdx.x < a.world) a.ag_scale[threadIdx.x][i] = sc;
+    if (threadIdx.x < W) a.ag_scale[threadIdx.x][i] = sc;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int c = threadIdx.x + k * kSpThreads;
       if (c >= nvec) continue;
-      const uint2 pk = make_uint2(sp_e4m3x4(v[k][0] * inv, v[k][1] * inv, v[k][2] * inv, v[k][3] * inv),
-                                  sp_e4m3x4(v[k][4] * inv, v[k][5] * inv, v[k][6] * inv, v[k][7] * inv));
-      for (int r = 0; r < a.world; ++r)
+      float v[8];
+      sp_unpack8(vb[k], v);
+      const uint2 pk = make_uint2(sp_e4m3x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv),
+                                  sp_e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv));
+#pragma unroll
+      for (int r = 0; r < W; ++r)
         reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(a.ag[r]) + (long)i * a.ld_ag)[c] = pk;
     }
   } else {
@@ -250,9 +259,9 @@ __global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0) 
     for (int k = 0; k < NV; ++k) {
       const int c = threadIdx.x + k * kSpThreads;
       if (c >= nvec) continue;
-      const uint4 pk = sp_pack8(v[k]);
-      for (int r = 0; r < a.world; ++r)
-        reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.ag[r]) + (long)i * a.ld_ag)[c] = pk;
+#pragma unroll
+      for (int r = 0; r < W; ++r)
+        reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.ag[r]) + (long)i * a.ld_ag)[c] = vb[k];
     }
   }
 }
@@ -332,10 +341,19 @@ void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, 
   }
   const int nv = (static_cast<int>(D) / 8 + kSpThreads - 1) / kSpThreads;
   auto st = at::cuda::getCurrentCUDAStream();
-  if (nv <= 1) sp_row_kernel<1><<<nrows, kSpThreads, 0, st>>>(a, row0);
-  else if (nv <= 2) sp_row_kernel<2><<<nrows, kSpThreads, 0, st>>>(a, row0);
-  else if (nv <= 4) sp_row_kernel<4><<<nrows, kSpThreads, 0, st>>>(a, row0);
-  else sp_row_kernel<8><<<nrows, kSpThreads, 0, st>>>(a, row0);
+#define APPCORR_SP_LAUNCH_W(NV)                                                             \
+  switch (world) {                                                                          \
+    case 1: sp_row_kernel<NV, 1><<<nrows, kSpThreads, 0, st>>>(a, row0); break;             \
+    case 2: sp_row_kernel<NV, 2><<<nrows, kSpThreads, 0, st>>>(a, row0); break;             \
+    case 4: sp_row_kernel<NV, 4><<<nrows, kSpThreads, 0, st>>>(a, row0); break;             \
+    case 8: sp_row_kernel<NV, 8><<<nrows, kSpThreads, 0, st>>>(a, row0); break;             \
+    default: TORCH_CHECK(false, "sp_row: world must be 1, 2, 4 or 8");                      \
+  }
+  if (nv <= 1) { APPCORR_SP_LAUNCH_W(1) }
+  else if (nv <= 2) { APPCORR_SP_LAUNCH_W(2) }
+  else if (nv <= 4) { APPCORR_SP_LAUNCH_W(4) }
+  else { APPCORR_SP_LAUNCH_W(8) }
+#undef APPCORR_SP_LAUNCH_W
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
