@@ -363,6 +363,7 @@ class ViTEngine:
         """Approximate pass over layers [start, end) on the running features."""
         if start == 0:
             sess.x.copy_(sess.x_in)
+            sess.extra.pop("layermean", None)  # a new request's approximate pass
         self._set_pass(sess, "approx")
         for l in range(start, end):
             self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
@@ -416,28 +417,33 @@ class ViTEngine:
         pre: int32 [B, n_prefix] prefix token indices; cand: int32 [B, P_g] candidate patch tokens
         (the residual group that just arrived). Keeps k = int(P_g * token_keep_ratio) per image.
         """
+        st = self._correct_begin(sess, start, cand, opts)
+        for l in range(start, end):
+            self._correct_step(sess, l, st, pre, cand, opts, mobile, valid)
+        return sess.x
+
+    def _correct_begin(self, sess: Session, start: int, cand: torch.Tensor, opts: Dict) -> Dict:
         P_g = cand.shape[1]
         ratio = float(opts.get("token_keep_ratio", 0.2))
-        k = min(int(P_g * ratio), P_g)
         if opts.get("token_keep_thres") is not None:
             raise NotImplementedError("threshold selection on the sm_100a engine uses token_keep_cap (sync-free)")
         kind = str(opts.get("server_pscore", "cls_attn_prob"))
         if start == 0:
             sess.x.copy_(sess.x_in)
         self._set_pass(sess, "correct")
-        x = sess.x
         shared = None
         if kind in LAYERMEAN_SERVER_PSCORES:
             shared = sess.extra.get("layermean")
-            if shared is None:
+            if shared is None:  # mean over the approximate pass's layers, computed once per request
                 shared = sess.pscore[: max(sess.approx_done, 1)].mean(0)
                 sess.extra["layermean"] = shared
-        upd = rows = None
-        for l in range(start, end):
-            if upd is None or shared is None:
-                upd, rows = self.plan(sess, l, pre, cand, k, opts, mobile=mobile, valid=valid, server=shared)
-            self.correct_layer(sess, l, x, upd, rows)
-        return x
+        return {"k": min(int(P_g * ratio), P_g), "shared": shared, "upd": None, "rows": None}
+
+    def _correct_step(self, sess: Session, l: int, st: Dict, pre, cand, opts, mobile, valid) -> None:
+        if st["upd"] is None or st["shared"] is None:
+            st["upd"], st["rows"] = self.plan(sess, l, pre, cand, st["k"], opts, mobile=mobile, valid=valid,
+                                              server=st["shared"])
+        self.correct_layer(sess, l, sess.x, st["upd"], st["rows"])
 
     # -------------------------------------------------------------- outputs
     def normed_tokens(self, sess: Session) -> torch.Tensor:

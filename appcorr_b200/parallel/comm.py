@@ -31,6 +31,12 @@ class SymTensor:
         return [p + offset_elems * es for p in self.ptrs]
 
 
+@dataclass
+class BarrierChannel:
+    flags: SymTensor
+    epoch: int = 0
+
+
 class TPComm:
     def __init__(self, group: Optional["dist.ProcessGroup"] = None, device: Optional[torch.device] = None):
         self.group = group
@@ -41,9 +47,12 @@ class TPComm:
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self._owned: List[int] = []
         self._opened: List[int] = []
-        self.epoch = 0
-        self.flags = self.empty((MAX_RANKS,), torch.int32)
         self.err = err_word(self.device)
+        self._default = self.channel()
+
+    def channel(self) -> "BarrierChannel":
+        """An independent barrier (own flags and epoch), for work issued on its own stream."""
+        return BarrierChannel(self.empty((MAX_RANKS,), torch.int32))
 
     # ------------------------------------------------------------------ buffers
     def empty(self, shape: Sequence[int], dtype: torch.dtype) -> SymTensor:
@@ -82,13 +91,15 @@ class TPComm:
         self._opened, self._owned = [], []
 
     # ------------------------------------------------------------------ collectives
-    def barrier(self) -> None:
-        """Device-side barrier across the group on the current stream (bounded wait)."""
+    def barrier(self, ch: Optional["BarrierChannel"] = None) -> None:
+        """Device-side barrier across the group on the current stream (bounded wait). Barriers
+        of one channel must be issued in the same order on every rank."""
         if self.world == 1:
             return
-        self.epoch = (self.epoch + 1) & 0x7FFFFFFF
+        ch = ch or self._default
+        ch.epoch = (ch.epoch + 1) & 0x7FFFFFFF
         _count()
-        lib().tp_barrier(self.flags.ptrs, self.rank, self.epoch, self.err)
+        lib().tp_barrier(ch.flags.ptrs, self.rank, ch.epoch, self.err)
 
     def sp_row(self, M: int, D: int, rows_per_rank: int, *, tok=None, src: Optional[Tuple[List[int], List[int]]] = None,
                bias=None, gamma=None, resid=None, resid_tok: bool = True, resid2=None,

@@ -82,6 +82,10 @@ class ViTEngineTP(ViTEngine):
         self.local_heads = self.cfg.num_heads // self.world
         self.local_dim = self.cfg.embed_dim // self.world
         self.timer = PhaseTimer.from_env()
+        # micro-batches per session: each runs on its own stream with its own barriers, so one
+        # micro-batch's collectives overlap the other's GEMMs
+        self.microbatch = max(1, int(os.environ.get("APPCORR_TP_MICROBATCH", "2")))
+        self._streams = []
         # reduce-scatter of the row-parallel GEMMs: "pull" (owner loads peers' partials in the row
         # kernel) or "push" (GEMM epilogue stores partial rows into the owner's slots)
         # "ce": contiguous row blocks (approximate pass) travel by copy-engine peer copies into the
@@ -104,6 +108,44 @@ class ViTEngineTP(ViTEngine):
 
     # -------------------------------------------------------------- sessions
     def new_session(self, B: int, H: int, W: int) -> Session:
+        k = self.microbatch
+        if k > 1 and B % k == 0 and self.world > 1:
+            return self._new_split_session(B, H, W, k)
+        return self._new_sub_session(B, H, W)
+
+    def _new_split_session(self, B: int, H: int, W: int, k: int) -> Session:
+        """A session of B images served as k micro-batches of B/k images (sub-sessions)."""
+        c, comm = self.cfg, self.comm
+        Bh = B // k
+        D = c.embed_dim
+        subs = []
+        feat = comm.empty((B * ((H // c.patch_size) * (W // c.patch_size)), D), BF16)
+        for i in range(k):
+            subs.append(self._new_sub_session(Bh, H, W))
+        s0 = subs[0]
+        N, P = s0.N, s0.P
+        M = B * N
+        dev = self.device
+        parent = Session(
+            B=B, img_hw=(H, W), grid_hw=s0.grid_hw, N=N, P=P,
+            x_in=torch.empty(M, D, device=dev, dtype=BF16), x=s0.x, x_tmp=s0.x_tmp, xn=s0.xn, q=s0.q, o=s0.o,
+            h=s0.h, kc=s0.kc, vc=s0.vc, bos=s0.bos, pscore=torch.zeros(c.depth, B, N, device=dev),
+            ps_scratch=s0.ps_scratch, cols=torch.empty(B * P, 3 * c.patch_size ** 2, device=dev, dtype=BF16),
+            patch_rows=(torch.arange(B, device=dev)[:, None] * N + c.n_prefix
+                        + torch.arange(P, device=dev)[None, :]).reshape(-1).to(torch.int32).contiguous(),
+            rope=s0.rope, upd=s0.upd, rows=s0.rows, x_act=s0.x_act, x_att=s0.x_att, plan_stats=s0.plan_stats,
+            stat_acc=s0.stat_acc)
+        Mh = Bh * N
+        for i, sub in enumerate(subs):
+            sub.x_in = parent.x_in[i * Mh:(i + 1) * Mh]
+            sub.pscore = parent.pscore[:, i * Bh:(i + 1) * Bh]
+            off = i * Bh * P
+            sub.extra["sym_feat"] = SymTensor(feat.local[off:off + Bh * P], feat.view_ptrs(off * D))
+        parent.extra["subs"] = subs
+        parent.extra["feat"] = feat
+        return parent
+
+    def _new_sub_session(self, B: int, H: int, W: int) -> Session:
         c, comm = self.cfg, self.comm
         sess = super().new_session(B, H, W)
         M, D, L = B * sess.N, c.embed_dim, c.depth
@@ -114,7 +156,7 @@ class ViTEngineTP(ViTEngine):
         xg = comm.empty((M, D), BF16)                       # gathered LN rows (bf16, or e4m3 in its first M*D bytes)
         xg8 = SymTensor(xg.local.view(torch.uint8).view(-1)[: M * D].view(M, D).view(torch.float8_e4m3fn), xg.ptrs)
         sess.extra.update({
-            "R": R, "sym_xg": xg, "sym_xg8": xg8, "sym_xg_scale": comm.empty((M,), torch.float32),
+            "R": R, "chan": comm.channel(), "sym_xg": xg, "sym_xg8": xg8, "sym_xg_scale": comm.empty((M,), torch.float32),
             "sym_part": (comm.empty((self.world, M, D), BF16) if self.rs_mode == "push" else comm.empty((M, D), BF16)),
             "sym_slot": comm.empty((self.world, M, D), BF16) if self.rs_mode == "ce" else None,
             "sym_ps": comm.empty((B, sess.N), torch.float32),
@@ -207,7 +249,7 @@ class ViTEngineTP(ViTEngine):
             with tm("a.rs_copy"):
                 self._ce_scatter(sess, M)
         with tm("a.barrier"):
-            comm.barrier()
+            comm.barrier(e["chan"])
         if score:  # every rank's local-head mean is ready (barrier above): average them
             comm.mean_f32(e["sym_ps"], sess.pscore[l])
         with tm("a.row_ln_ag"):
@@ -215,7 +257,7 @@ class ViTEngineTP(ViTEngine):
                         aux=sess.bos[l], aux_mode=K.AUX_SET, ln_w=lw.norm2_w, ln_b=lw.norm2_b, eps=c.norm_eps,
                         **self._ag(sess))
         with tm("a.barrier"):
-            comm.barrier()
+            comm.barrier(e["chan"])
         a, sa = self._gathered(sess, M)
         with tm("a.w12"):
             self._mlp(lw, a, sess.h, sa)
@@ -228,7 +270,7 @@ class ViTEngineTP(ViTEngine):
             with tm("a.rs_copy"):
                 self._ce_scatter(sess, M)
         with tm("a.barrier"):
-            comm.barrier()
+            comm.barrier(e["chan"])
         nxt = self.w.layers[l + 1] if l + 1 < sess.extra.get("approx_end", c.depth) else None
         with tm("a.row_ln_ag"):
             comm.sp_row(M, D, R, src=self._src(sess, M, contiguous=True), bias=lw.fc2_b, gamma=lw.ls2, resid=x, out=x,
@@ -237,23 +279,78 @@ class ViTEngineTP(ViTEngine):
                         eps=c.norm_eps, **self._ag(sess))
         if nxt is not None:
             with tm("a.barrier"):
-                comm.barrier()
+                comm.barrier(e["chan"])
 
-    def approx(self, sess: Session, start: int, end: int, server_pscore: str = "cls_attn_prob") -> torch.Tensor:
+    def _fork(self, k: int):
+        cur = torch.cuda.current_stream(self.device)
+        while len(self._streams) < k:
+            self._streams.append(torch.cuda.Stream(self.device))
+        for st in self._streams[:k]:
+            st.wait_stream(cur)
+        return self._streams[:k]
+
+    def _join(self, streams) -> None:
+        cur = torch.cuda.current_stream(self.device)
+        for st in streams:
+            cur.wait_stream(st)
+
+    def _approx_begin(self, sess: Session, start: int, end: int) -> None:
         c = self.cfg
         if start == 0:
             sess.x.copy_(sess.x_in)
+            sess.extra.pop("layermean", None)
         self._set_pass(sess, "approx")
-        M = sess.B * sess.N
         sess.extra["approx_end"] = end
         if start < end:
             lw = self.w.layers[start]
-            self.comm.sp_row(M, c.embed_dim, sess.extra["R"], x=sess.x, ln_w=lw.norm1_w, ln_b=lw.norm1_b,
-                             eps=c.norm_eps, **self._ag(sess))
-            self.comm.barrier()
-        for l in range(start, end):
-            self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
+            self.comm.sp_row(sess.B * sess.N, c.embed_dim, sess.extra["R"], x=sess.x, ln_w=lw.norm1_w,
+                             ln_b=lw.norm1_b, eps=c.norm_eps, **self._ag(sess))
+            self.comm.barrier(sess.extra["chan"])
+
+    def approx(self, sess: Session, start: int, end: int, server_pscore: str = "cls_attn_prob") -> torch.Tensor:
+        subs = sess.extra.get("subs")
+        if subs is None:
+            self._approx_begin(sess, start, end)
+            for l in range(start, end):
+                self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
+        else:  # micro-batches interleaved layer by layer on their own streams
+            if start == 0:
+                sess.extra.pop("layermean", None)
+            streams = self._fork(len(subs))
+            for sub, st in zip(subs, streams):
+                with torch.cuda.stream(st):
+                    self._approx_begin(sub, start, end)
+            for l in range(start, end):
+                for sub, st in zip(subs, streams):
+                    with torch.cuda.stream(st):
+                        self.approx_layer(sub, l, sub.x, sub.x, server_pscore)
+            self._join(streams)
+            for sub in subs:
+                sub.approx_done = max(sub.approx_done, end)
         sess.approx_done = max(sess.approx_done, end)
+        return sess.x
+
+    def correct(self, sess: Session, start: int, end: int, pre: torch.Tensor, cand: torch.Tensor, opts: Dict,
+                mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None) -> torch.Tensor:
+        subs = sess.extra.get("subs")
+        if subs is None:
+            return super().correct(sess, start, end, pre, cand, opts, mobile=mobile, valid=valid)
+        Bh = sess.B // len(subs)
+
+        def part(t, i):
+            return None if t is None else t[i * Bh:(i + 1) * Bh]
+
+        streams = self._fork(len(subs))
+        states = []
+        for i, (sub, st) in enumerate(zip(subs, streams)):
+            with torch.cuda.stream(st):
+                states.append(self._correct_begin(sub, start, part(cand, i), opts))
+        for l in range(start, end):
+            for i, (sub, st) in enumerate(zip(subs, streams)):
+                with torch.cuda.stream(st):
+                    self._correct_step(sub, l, states[i], part(pre, i), part(cand, i), opts, part(mobile, i),
+                                       part(valid, i))
+        self._join(streams)
         return sess.x
 
     # -------------------------------------------------------------- correction pass
@@ -271,7 +368,7 @@ class ViTEngineTP(ViTEngine):
                     **self._ag(sess))
         lo, hi = self.rank * R, min((self.rank + 1) * R, B * N)
         K.add_(x[lo:hi], sess.bos[l][lo:hi])
-        comm.barrier()
+        comm.barrier(e["chan"])
         a, sa = self._gathered(sess, MT)
         w, ws = self._w(lw, "qkv")
         K.qkv_gemm(a, w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
@@ -280,17 +377,17 @@ class ViTEngineTP(ViTEngine):
         a, sa = self._act(sess, o)
         w, ws = self._w(lw, "proj")
         self._row_gemm(sess, a, w, rows, sa, ws, MT)
-        comm.barrier()
+        comm.barrier(e["chan"])
         comm.sp_row(MT, D, R, tok=rows, src=self._src(sess, MT), bias=lw.proj_b, gamma=lw.ls1, resid=x_act,
                     resid_tok=False, out=x_att, out_tok=False, ln_w=lw.norm2_w, ln_b=lw.norm2_b, eps=c.norm_eps,
                     **self._ag(sess))
-        comm.barrier()
+        comm.barrier(e["chan"])
         a, sa = self._gathered(sess, MT)
         self._mlp(lw, a, h, sa)
         a, sa = self._act(sess, h)
         w, ws = self._w(lw, "fc2")
         self._row_gemm(sess, a, w, rows, sa, ws, MT)
-        comm.barrier()
+        comm.barrier(e["chan"])
         # x[row] = x_att + ls2 * mlp; increment[row] = (x_att - x_act) + ls2 * mlp  (owners)
         comm.sp_row(MT, D, R, tok=rows, src=self._src(sess, MT), bias=lw.fc2_b, gamma=lw.ls2, resid=x_att,
                     resid_tok=False, out=x, out_tok=True, aux=sess.bos[l], aux_mode=K.AUX_OUT_MINUS, resid2=x_act)
@@ -299,21 +396,42 @@ class ViTEngineTP(ViTEngine):
     def normed_tokens(self, sess: Session) -> torch.Tensor:
         """Final LayerNorm of every token on its owner, gathered to every rank [B*N, D]."""
         c = self.cfg
+        subs = sess.extra.get("subs")
+        if subs is not None:
+            buf = sess.extra.get("sym_normed")
+            if buf is None:
+                buf = sess.extra["sym_normed"] = self.comm.empty((sess.B * sess.N, c.embed_dim), BF16)
+                Mh = sess.B // len(subs) * sess.N
+                for i, sub in enumerate(subs):
+                    sub.extra["sym_normed"] = SymTensor(buf.local[i * Mh:(i + 1) * Mh],
+                                                        buf.view_ptrs(i * Mh * c.embed_dim))
+            for sub in subs:
+                self.normed_tokens(sub)
+            return buf.local
         buf = sess.extra.get("sym_normed")
         if buf is None:
             buf = sess.extra["sym_normed"] = self.comm.empty((sess.B * sess.N, c.embed_dim), BF16)
         self.comm.sp_row(sess.B * sess.N, c.embed_dim, sess.extra["R"], x=sess.x, ln_w=self.w.norm_w,
                          ln_b=self.w.norm_b, eps=c.norm_eps, ag=buf)
-        self.comm.barrier()
+        self.comm.barrier(sess.extra["chan"])
         return buf.local
 
     def patch_features(self, sess: Session, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Final LayerNorm of the patch tokens on their owners, gathered to every rank [B*P, D]."""
         c = self.cfg
+        subs = sess.extra.get("subs")
+        if subs is not None:
+            for sub in subs:
+                self.patch_features(sub)
+            feat = sess.extra["feat"].local
+            if out is not None:
+                out.copy_(feat)
+                return out
+            return feat
         feat = sess.extra["sym_feat"]
         self.comm.sp_row(sess.B * sess.P, c.embed_dim, sess.extra["R"], tok=sess.patch_rows, x=sess.x,
                          ln_w=self.w.norm_w, ln_b=self.w.norm_b, eps=c.norm_eps, ag=feat)
-        self.comm.barrier()
+        self.comm.barrier(sess.extra["chan"])
         if out is not None:
             out.copy_(feat.local)
             return out

@@ -15,8 +15,9 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q, precision="bf16", rs_mode="pull"):
+def _worker(rank, world, port, q, precision="bf16", rs_mode="pull", microbatch=2):
     os.environ["APPCORR_TP_RS"] = rs_mode
+    os.environ["APPCORR_TP_MICROBATCH"] = str(microbatch)
     import torch.distributed as dist
 
     from appcorr_b200.models.dinov3.vit import ViTConfig
@@ -66,14 +67,15 @@ def _worker(rank, world, port, q, precision="bf16", rs_mode="pull"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("precision,rs_mode", [("bf16", "pull"), ("bf16", "push"), ("fp8", "pull")])
-def test_tp2_matches_single_gpu(precision, rs_mode):
+@pytest.mark.parametrize("precision,rs_mode,microbatch", [("bf16", "pull", 2), ("bf16", "pull", 1), ("bf16", "push", 2),
+                                                          ("bf16", "ce", 1), ("fp8", "pull", 2)])
+def test_tp2_matches_single_gpu(precision, rs_mode, microbatch):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, precision, rs_mode)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, precision, rs_mode, microbatch)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
