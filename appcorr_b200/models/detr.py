@@ -75,7 +75,7 @@ class DetrDecoder(nn.Module):
             h = lin(h)
             if i < 2:
                 h = F.relu(h)
-        return {"pred_logits": logits, "pred_boxes": h.sigmoid()}
+        return {"pred_logits": logits, "pred_boxes": h.sigmoid(), "hidden": tgt}
 
 
 def postprocess(out: Dict[str, torch.Tensor], top_k: int = 100):
@@ -173,4 +173,5 @@ class DetrDecoderGPU:
         boxes = self._e(B * Q, self.box_w3.shape[0], dtype=torch.float32)
         K.gemm(hb, self.box_w3, boxes, epi=K.EPI_F32, bias=self.box_b3)
         C = self.m.num_classes + 1
-        return {"pred_logits": logits[:, :C].view(B, Q, C), "pred_boxes": boxes[:, :4].sigmoid().view(B, Q, 4)}
+        return {"pred_logits": logits[:, :C].view(B, Q, C), "pred_boxes": boxes[:, :4].sigmoid().view(B, Q, 4),
+                "hidden": tgt}

@@ -68,6 +68,13 @@ class EngineWeights:
     norm_b: torch.Tensor
     cls_norm_w: Optional[torch.Tensor] = None
     cls_norm_b: Optional[torch.Tensor] = None
+    # learned absolute position embedding [n_prefix + P, D] (periods is then None: no RoPE) and
+    # a LayerNorm applied to the tokens before the first block (CLIP-style towers)
+    pos_embed: Optional[torch.Tensor] = None
+    pre_norm_w: Optional[torch.Tensor] = None
+    pre_norm_b: Optional[torch.Tensor] = None
+    pixel_mean: Tuple[float, float, float] = K.IMAGENET_MEAN
+    pixel_std: Tuple[float, float, float] = K.IMAGENET_STD
 
 
 def _bf(t: Optional[torch.Tensor], device) -> Optional[torch.Tensor]:
@@ -235,6 +242,7 @@ class ViTEngine:
                 if lw.q8 is None:
                     quantize_layer_e4m3(lw)
         self._fp8 = False  # precision of the pass being run
+        self.taps: Tuple[int, ...] = ()  # layers whose output is kept for dense heads
 
     @classmethod
     def from_module(cls, model: DinoVisionTransformer, device, precision="bf16") -> "ViTEngine":
@@ -303,7 +311,7 @@ class ViTEngine:
             kc=e(L, M, D), vc=e(L, M, D), bos=e(L, M, D), pscore=torch.zeros(L, B, N, device=dev),
             ps_scratch=e(B, c.num_heads, N, dtype=torch.float32), cols=e(B * P, 3 * p * p),
             patch_rows=patch_rows.reshape(-1).to(torch.int32).contiguous(),
-            rope=rope_tables(c, self.w.periods, gh, gw),
+            rope=rope_tables(c, self.w.periods, gh, gw) if self.w.periods is not None else None,
             upd=torch.zeros(B, T, device=dev, dtype=torch.int32), rows=torch.zeros(B * T, device=dev, dtype=torch.int32),
             x_act=e(B * T, D), x_att=e(B * T, D), plan_stats=torch.zeros(B, 2, device=dev),
             stat_acc=torch.zeros(5, device=dev))
@@ -314,9 +322,19 @@ class ViTEngine:
         """uint8 [B, H, W, 3] image -> tokens [B*N, D] (CLS + storage + patch embeddings)."""
         c = self.cfg
         out = sess.x_in if out is None else out
-        K.patch_im2col(img, c.patch_size, sess.cols)
+        K.patch_im2col(img, c.patch_size, sess.cols, mean=self.w.pixel_mean, std=self.w.pixel_std)
         K.gemm(sess.cols, self.w.patch_w, out, bias=self.w.patch_b, out_rows=sess.patch_rows)
         K.set_prefix(out, self.w.prefix, sess.B, sess.N)
+        if self.w.pos_embed is not None:
+            rep = sess.extra.get("pos_rep")
+            if rep is None:
+                if self.w.pos_embed.shape[0] != sess.N:
+                    raise ValueError(f"learned position embedding has {self.w.pos_embed.shape[0]} rows, "
+                                     f"the image has {sess.N} tokens")
+                rep = sess.extra["pos_rep"] = self.w.pos_embed.repeat(sess.B, 1).contiguous()
+            K.add_(out, rep)
+        if self.w.pre_norm_w is not None:  # row-wise in place: each row is read before it is written
+            K.layernorm(out, self.w.pre_norm_w, self.w.pre_norm_b, c.norm_eps, out)
         return out
 
     # -------------------------------------------------------------- approximate pass
@@ -367,8 +385,25 @@ class ViTEngine:
         self._set_pass(sess, "approx")
         for l in range(start, end):
             self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
+            self._tap(sess, l)
         sess.approx_done = max(sess.approx_done, end)
         return sess.x
+
+    def _tap(self, sess: Session, l: int) -> None:
+        """Keep the running features after layer l when l is a tap layer (dense heads read them)."""
+        if l in self.taps:
+            t = sess.extra.get(f"tap{l}")
+            if t is None:
+                t = sess.extra[f"tap{l}"] = torch.empty_like(sess.x)
+            t.copy_(sess.x)
+
+    def tap_features(self, sess: Session, l: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Final-norm patch tokens of tap layer l -> [B*P, D] (DINOv3 intermediate layers, norm=True)."""
+        c = self.cfg
+        if out is None:
+            out = torch.empty(sess.B * sess.P, c.embed_dim, device=self.device, dtype=BF16)
+        K.layernorm(sess.extra[f"tap{l}"], self.w.norm_w, self.w.norm_b, c.norm_eps, out, rows=sess.patch_rows)
+        return out
 
     # -------------------------------------------------------------- correction pass
     def plan(self, sess: Session, l: int, pre: torch.Tensor, cand: torch.Tensor, k: int, opts: Dict,
@@ -444,6 +479,7 @@ class ViTEngine:
             st["upd"], st["rows"] = self.plan(sess, l, pre, cand, st["k"], opts, mobile=mobile, valid=valid,
                                               server=st["shared"])
         self.correct_layer(sess, l, sess.x, st["upd"], st["rows"])
+        self._tap(sess, l)
 
     # -------------------------------------------------------------- outputs
     def normed_tokens(self, sess: Session) -> torch.Tensor:

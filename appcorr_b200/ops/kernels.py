@@ -167,6 +167,30 @@ def set_prefix(x: torch.Tensor, prefix: torch.Tensor, B: int, N: int) -> None:
     lib().set_prefix(x, prefix, B, N)
 
 
+def msda(value: torch.Tensor, ref: torch.Tensor, offs: torch.Tensor, logits: torch.Tensor, out: torch.Tensor,
+         shapes, M: int, L: int, P: int) -> torch.Tensor:
+    """Multi-scale deformable attention: value [N, S, M, Dh] bf16, ref [N, Q, L, 2] fp32,
+    offs / logits bf16 rows per query (offsets [M, L, P, 2], logits [M, L*P]) -> out [N, Q, M*Dh]."""
+    _count()
+    lib().msda(value, ref, offs, logits, out, [int(v) for v in shapes], int(M), int(L), int(P))
+    return out
+
+
+def im2col_nhwc(x: torch.Tensor, kh: int, kw: int, stride: int, pad: int, out: torch.Tensor) -> torch.Tensor:
+    """NHWC patches for a kh x kw convolution: out [B*Ho*Wo, >= kh*kw*C], column (ky*kw+kx)*C + c."""
+    _count()
+    lib().im2col_nhwc(x, kh, kw, stride, pad, out)
+    return out
+
+
+def resize_nhwc(x: torch.Tensor, out: torch.Tensor, align_corners: bool = False,
+                add: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Bilinear resize of [B, H, W, C] bf16 into out [B, Ho, Wo, C] (+ add)."""
+    _count()
+    lib().resize_nhwc(x, out, bool(align_corners), add)
+    return out
+
+
 def row_sqdist(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """out[r] = ||a[r] - b[r]||^2 (fp32)."""
     _count()

@@ -30,6 +30,10 @@ def get_model_executor(name: str, device) -> ModelExecutor:
         from .qwen25vl_executor import Qwen25VLExecutor
 
         return Qwen25VLExecutor(device)
+    if "openclip" in name or "clip" in name:
+        from .openclip_executor import OpenCLIPExecutor
+
+        return OpenCLIPExecutor(device)
     if "dinov3" in name:
         from .dinov3_classifier import DINOv3ClassifierExecutor
 

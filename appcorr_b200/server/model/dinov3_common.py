@@ -65,6 +65,11 @@ class DINOv3BackboneMixin:
         self._group_cache.clear()
         tp = int(getattr(config, "tp_size", 1) or 1)
         prec = self.engine_precision(config)
+        self.sr_engine = None
+        if self.device.type == "cuda" and hasattr(config, "lowres_sr_enabled") and config.lowres_sr_enabled():
+            from ..sr import create_lowres_sr_engine
+
+            self.sr_engine = create_lowres_sr_engine(config.get_lowres_sr_config(), self.device)
         if self.device.type == "cuda" and tp > 1:
             import torch.distributed as dist
 
@@ -109,6 +114,15 @@ class DINOv3BackboneMixin:
         if isinstance(batch_data, PyramidBatch):
             cur = to_device_uint8_images(batch_data.base, dev)
             steps = batch_data.residual_steps()
+            sr = getattr(self, "sr_engine", None)
+            if sr is not None and all(r is None for r in steps):
+                # approximate pass with super-resolution: the base is upscaled by the network
+                # instead of the pyramid's pyrUp chain (reference worker.py:586-614)
+                B, h, w, _ = cur.shape
+                f = 2 ** len(steps)
+                context["canvas"] = sr.upscale(cur, (h * f, w * f))
+                context["target_shapes"] = batch_data.target_shapes
+                return context["canvas"]
             for i, r in enumerate(steps):
                 B, h, w, _ = cur.shape
                 if r is not None:

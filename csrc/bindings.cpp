@@ -164,5 +164,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_attention_ops(m);
   register_comm_ops(m);
   register_sp_ops(m);
+  register_msda_ops(m);
+  register_conv_ops(m);
   register_attention_sm100_ops(m);
 }

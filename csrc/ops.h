@@ -67,6 +67,8 @@ void register_elementwise_ops(pybind11::module_& m);
 void register_attention_ops(pybind11::module_& m);
 void register_comm_ops(pybind11::module_& m);
 void register_sp_ops(pybind11::module_& m);
+void register_msda_ops(pybind11::module_& m);
+void register_conv_ops(pybind11::module_& m);
 void register_attention_sm100_ops(pybind11::module_& m);
 
 }  // namespace appcorr

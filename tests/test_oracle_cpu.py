@@ -137,3 +137,46 @@ def test_qwen_oracle_window_order_and_full_correction():
         for i, ly in enumerate(m.layers):
             x2 = ly.correct(x2, torch.arange(x0.shape[0]), s, c, cache, f"l{i}")
     assert torch.allclose(x, x2, atol=1e-5)
+
+
+def test_msda_reference_matches_direct_bilinear():
+    """The deformable-sampling oracle equals a direct per-point bilinear sum (zeros outside)."""
+    from appcorr_b200.models.m2f import msda_reference
+
+    torch.manual_seed(0)
+    N, M, Dh, L, P, Q = 1, 2, 4, 2, 3, 5
+    shapes = [(5, 6), (3, 4)]
+    S = sum(h * w for h, w in shapes)
+    value = torch.randn(N, S, M, Dh, dtype=torch.float64)
+    loc = torch.rand(N, Q, M, L, P, 2, dtype=torch.float64) * 1.4 - 0.2
+    w = torch.rand(N, Q, M, L, P, dtype=torch.float64)
+    got = msda_reference(value, shapes, loc, w).view(N, Q, M, Dh)
+    starts = [0, shapes[0][0] * shapes[0][1]]
+    exp = torch.zeros(N, Q, M, Dh, dtype=torch.float64)
+    for q in range(Q):
+        for m in range(M):
+            for l, (h, wd) in enumerate(shapes):
+                for p in range(P):
+                    x = loc[0, q, m, l, p, 0].item() * wd - 0.5
+                    y = loc[0, q, m, l, p, 1].item() * h - 0.5
+                    x0, y0 = int(torch.floor(torch.tensor(x))), int(torch.floor(torch.tensor(y)))
+                    for cx, cy, cw in ((x0, y0, (1 - (x - x0)) * (1 - (y - y0))), (x0 + 1, y0, (x - x0) * (1 - (y - y0))),
+                                       (x0, y0 + 1, (1 - (x - x0)) * (y - y0)), (x0 + 1, y0 + 1, (x - x0) * (y - y0))):
+                        if 0 <= cx < wd and 0 <= cy < h:
+                            exp[0, q, m] += w[0, q, m, l, p] * cw * value[0, starts[l] + cy * wd + cx, m]
+    assert torch.allclose(got.double(), exp, atol=1e-5)
+
+
+def test_realesrgan_key_conversion_loads_strictly():
+    from appcorr_b200.models.conv import RRDBNet
+    from appcorr_b200.server.sr import convert_realesrgan_state
+
+    net = RRDBNet(nf=8, nb=2, gc=4)
+    ref = {}
+    for k, v in net.state_dict().items():  # rebuild the Real-ESRGAN layout from our names
+        k = k.replace("conv_up.0.", "conv_up1.").replace("conv_up.1.", "conv_up2.")
+        parts = k.split(".")
+        if parts[0] == "body":
+            k = f"body.{parts[1]}.rdb{int(parts[3]) + 1}.conv{int(parts[5]) + 1}.{parts[6]}"
+        ref[k] = v
+    net.load_state_dict(convert_realesrgan_state({"params_ema": ref}), strict=True)
