@@ -35,7 +35,7 @@ def _time(fn, iters: int, warmup: int = 3) -> float:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "attention", "layernorm", "sp_row"])
+    ap.add_argument("op", choices=["gemm", "attention", "layernorm", "sp_row", "msda"])
     ap.add_argument("--world", type=int, default=2)
     ap.add_argument("--M", type=int, default=8232)
     ap.add_argument("--N", type=int, default=12288)
@@ -90,6 +90,21 @@ def main(argv=None) -> None:
         else:
             ref = None
         res.update(B=a.B, H=a.H, Dh=a.Dh, Tq=a.Tq, Tk=a.Tk, impl=a.impl)
+    elif a.op == "msda":  # Mask2Former pixel decoder shape: 3 levels of a 64x64 grid, 8 heads x 32, 4 points
+        N, M, Dh, L, P = a.B, 8, 32, 3, 4
+        shapes = [(64, 64), (32, 32), (16, 16)]
+        S = sum(h * w for h, w in shapes)
+        value = torch.randn(N, S, M, Dh, device=dev).to(torch.bfloat16)
+        refp = torch.rand(N, S, L, 2, device=dev)
+        offs = torch.randn(N * S, M * L * P * 3, device=dev).to(torch.bfloat16)
+        out = torch.empty(N, S, M * Dh, device=dev, dtype=torch.bfloat16)
+        sh = [v for hw in shapes for v in hw]
+        fn = lambda: K.msda(value, refp, offs, offs[:, M * L * P * 2:], out, sh, M, L, P)  # noqa: E731
+        flops = 0.0
+        # bytes: the value rows each sample touches (4 corners x Dh bf16, mostly L2 hits) are not
+        # counted; count the per-query inputs and outputs (offsets, logits, reference, output)
+        res.update(N=N, S=S, bytes=N * S * (M * L * P * 3 * 2 + L * 2 * 4 + M * Dh * 2) + value.numel() * 2)
+        ref = None
     elif a.op == "sp_row":
         from .native import lib
 

@@ -7,6 +7,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "ops.h"
+#include "registry.h"
 
 namespace py = pybind11;
 using at::Tensor;

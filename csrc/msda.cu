@@ -6,10 +6,11 @@
 // ops/src/cuda/ms_deform_im2col_cuda.cuh (zero padding outside the map, sample at
 // (x * W_l - 0.5, y * H_l - 0.5), i.e. grid_sample with align_corners=False).
 //
-// One warp per (image, query, head): the L*P attention logits are softmaxed across the warp's
-// lanes, each lane owns Dh/32 channels of the head, and every bilinear corner is one contiguous
-// 64-byte (Dh = 32) row segment of the value map, so a sample costs four coalesced loads. The
-// softmax, the location arithmetic and the weighted sum are fused; nothing is materialised.
+// Dh/8 lanes per (image, query, head), 8 channels per lane: every bilinear corner is one 16-byte
+// load per lane (the head's Dh channels of one value row), so a warp serves 32/(Dh/8) heads at
+// once. The softmax, the location arithmetic and the weighted sum are fused; nothing is
+// materialised. (A first version with one warp per head and one channel per lane was
+// instruction-issue bound: 0.68 ms for 8 x 5376 queries x 8 heads, 83 % SM throughput.)
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -35,75 +36,61 @@ struct MsdaArgs {
   int H[kMsdaMaxLevels], W[kMsdaMaxLevels], start[kMsdaMaxLevels];
 };
 
+// Lane groups: G = DH / 8 lanes serve one (image, query, head); each lane owns 8 channels and reads
+// them with one 16-byte load per bilinear corner, so a warp works on 32 / G heads at once.
 template <int DH>
 __global__ void __launch_bounds__(256) msda_fwd_kernel(MsdaArgs a) {
-  constexpr int CPL = DH / 32;  // channels per lane
-  const int warp = (blockIdx.x * (blockDim.x >> 5)) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+  constexpr int G = DH / 8;
+  const long gid = (blockIdx.x * (long)blockDim.x + threadIdx.x) / G;  // (n, q, m) index
+  const int sub = threadIdx.x % G;                                     // channel block of this lane
   const long total = (long)a.N * a.Q * a.M;
-  if (warp >= total) return;
-  const int m = warp % a.M;
-  const long nq = warp / a.M;
+  if (gid >= total) return;
+  const int m = static_cast<int>(gid % a.M);
+  const long nq = gid / a.M;
   const int n = static_cast<int>(nq / a.Q);
   const int LP = a.L * a.P;
-  // softmax of the L*P logits (LP <= 32 handled one per lane)
+  // softmax of the L*P logits (every lane of the group computes it; the loads are broadcasts)
   const bf16* lg = a.logits + nq * a.ld_logits + (long)m * LP;
-  float z = lane < LP ? __bfloat162float(lg[lane]) : -FLT_MAX;
-  float mx = z;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float e = lane < LP ? __expf(z - mx) : 0.f;
-  float sum = e;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float wgt = e / sum;
-  // sampling location of sample `lane` (lane < LP)
-  float sx = 0.f, sy = 0.f;
-  if (lane < LP) {
-    const int l = lane / a.P;
-    const bf16* of = a.offs + nq * a.ld_offs + ((long)m * LP + lane) * 2;
-    const float* rp = a.ref + (nq * a.L + l) * 2;
-    // location in [0,1] -> pixel coordinate of the sample (align_corners = False)
-    sx = (rp[0] + __bfloat162float(of[0]) / a.W[l]) * a.W[l] - 0.5f;
-    sy = (rp[1] + __bfloat162float(of[1]) / a.H[l]) * a.H[l] - 0.5f;
-  }
-  float acc[CPL];
-#pragma unroll
-  for (int c = 0; c < CPL; ++c) acc[c] = 0.f;
-  const long vstride = (long)a.M * DH;  // between value rows
-  const bf16* vbase = a.value + (long)n * a.S * vstride + (long)m * DH + lane * CPL;
+  float mx = -FLT_MAX;
+  for (int s = 0; s < LP; ++s) mx = fmaxf(mx, __bfloat162float(lg[s]));
+  float sum = 0.f;
+  for (int s = 0; s < LP; ++s) sum += __expf(__bfloat162float(lg[s]) - mx);
+  const float inv = 1.f / sum;
+  const bf16* of = a.offs + nq * a.ld_offs + (long)m * LP * 2;
+  const float* rp = a.ref + nq * a.L * 2;
+  const long vstride = (long)a.M * DH;
+  const bf16* vbase = a.value + (long)n * a.S * vstride + (long)m * DH + sub * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int s = 0; s < LP; ++s) {
     const int l = s / a.P;
-    const float x = __shfl_sync(0xffffffffu, sx, s);
-    const float y = __shfl_sync(0xffffffffu, sy, s);
-    const float w = __shfl_sync(0xffffffffu, wgt, s);
     const int Hl = a.H[l], Wl = a.W[l];
+    const float2 o = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(of + 2 * s));
+    // location in [0,1] -> pixel coordinate of the sample (align_corners = False)
+    const float x = (rp[2 * l] + o.x / Wl) * Wl - 0.5f;
+    const float y = (rp[2 * l + 1] + o.y / Hl) * Hl - 0.5f;
     if (!(x > -1.f && y > -1.f && x < Wl && y < Hl)) continue;  // entirely outside: zero padding
+    const float w = __expf(__bfloat162float(lg[s]) - mx) * inv;
     const int x0 = static_cast<int>(floorf(x)), y0 = static_cast<int>(floorf(y));
     const float fx = x - x0, fy = y - y0;
-    const float cw[4] = {(1.f - fx) * (1.f - fy), fx * (1.f - fy), (1.f - fx) * fy, fx * fy};
-    const int cx[4] = {x0, x0 + 1, x0, x0 + 1};
-    const int cy[4] = {y0, y0, y0 + 1, y0 + 1};
+    const bf16* lvl = vbase + (long)a.start[l] * vstride;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      if (cx[k] < 0 || cy[k] < 0 || cx[k] >= Wl || cy[k] >= Hl) continue;
-      const bf16* vp = vbase + (long)(a.start[l] + cy[k] * Wl + cx[k]) * vstride;
-      const float ww = w * cw[k];
-      if constexpr (CPL == 1) {
-        acc[0] += ww * __bfloat162float(vp[0]);
-      } else {
+      const int cx = x0 + (k & 1), cy = y0 + (k >> 1);
+      if (cx < 0 || cy < 0 || cx >= Wl || cy >= Hl) continue;
+      const float ww = w * ((k & 1) ? fx : 1.f - fx) * ((k >> 1) ? fy : 1.f - fy);
+      const uint4 u = *reinterpret_cast<const uint4*>(lvl + (long)(cy * Wl + cx) * vstride);
+      const uint32_t* wd = &u.x;
 #pragma unroll
-        for (int c = 0; c < CPL; c += 2) {
-          const float2 f = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(vp + c));
-          acc[c] += ww * f.x;
-          acc[c + 1] += ww * f.y;
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(wd[j]);
+        acc[2 * j] = fmaf(ww, f.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(ww, f.y, acc[2 * j + 1]);
       }
     }
   }
-  bf16* op = a.out + nq * ((long)a.M * DH) + (long)m * DH + lane * CPL;
-#pragma unroll
-  for (int c = 0; c < CPL; ++c) op[c] = __float2bfloat16_rn(acc[c]);
+  bf16* op = a.out + nq * vstride + (long)m * DH + sub * 8;
+  *reinterpret_cast<uint4*>(op) = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                             pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
 }
 
 void msda_op(const at::Tensor& value, const at::Tensor& ref, const at::Tensor& offs, const at::Tensor& logits,
@@ -146,10 +133,13 @@ void msda_op(const at::Tensor& value, const at::Tensor& ref, const at::Tensor& o
     acc += a.H[l] * a.W[l];
   }
   TORCH_CHECK(acc == S, "msda: level shapes must cover the value rows");
-  const long warps = (long)N * Q * M;
-  if (warps == 0) return;
+  const long groups = (long)N * Q * M;
+  if (groups == 0) return;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(offs.data_ptr()) & 3) == 0 && a.ld_offs % 2 == 0,
+              "msda: offsets need 4-byte aligned (x, y) pairs");
   c10::cuda::CUDAGuard g(value.device());
-  const int grid = static_cast<int>((warps + 7) / 8);
+  const long threads = groups * (Dh / 8);
+  const int grid = static_cast<int>((threads + 255) / 256);
   auto st = at::cuda::getCurrentCUDAStream();
   if (Dh == 32) msda_fwd_kernel<32><<<grid, 256, 0, st>>>(a);
   else msda_fwd_kernel<64><<<grid, 256, 0, st>>>(a);

@@ -63,12 +63,5 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, int64_t rows, int64_t cols, int64
                               int box_cols);
 CUtensorMap make_tmap_u8_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols);
 int num_sms();
-void register_elementwise_ops(pybind11::module_& m);
-void register_attention_ops(pybind11::module_& m);
-void register_comm_ops(pybind11::module_& m);
-void register_sp_ops(pybind11::module_& m);
-void register_msda_ops(pybind11::module_& m);
-void register_conv_ops(pybind11::module_& m);
-void register_attention_sm100_ops(pybind11::module_& m);
 
 }  // namespace appcorr
