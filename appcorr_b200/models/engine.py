@@ -369,7 +369,7 @@ class ViTEngine:
         """Full attention of layer l; with `score`, the CLS softmax row (server patch score)
         comes out of the same attention pass and is averaged over the heads into score_out."""
         B, N, Dh = sess.B, sess.N, self.cfg.head_dim
-        fused = score and K.ATTENTION_IMPL[0] == "tcgen05"
+        fused = score and K.ATTENTION_IMPL[0].startswith("tcgen05")
         if score and not fused:
             K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out)
         K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh,

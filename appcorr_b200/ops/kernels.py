@@ -121,7 +121,9 @@ def add_(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     return x
 
 
-ATTENTION_IMPL = ["tcgen05"]  # "tcgen05" (sm_100a tensor cores + TMEM) or "mma" (mma.sync kernel)
+# "tcgen05": one 128-row query tile per CTA, P in shared memory (default: measured faster);
+# "tcgen05_2q": two query tiles per CTA sharing K/V, P kept in TMEM; "mma": the mma.sync kernel
+ATTENTION_IMPL = ["tcgen05"]
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, *, B: int, Tq: int,
@@ -141,12 +143,12 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor
     if scale is None:
         scale = Dh ** -0.5
     impl = impl or ATTENTION_IMPL[0]
-    if Hkv or causal or q_pos is not None or block_table is not None:
+    if impl == "mma" and (Hkv or causal or q_pos is not None or block_table is not None):
         impl = "tcgen05"
     _count()
-    if impl == "tcgen05":
+    if impl in ("tcgen05", "tcgen05_2q"):
         lib().attention_sm100(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse, err_word(q.device), cls_probs,
-                              Hkv, causal, q_pos, block_table)
+                              Hkv, causal, q_pos, block_table, 0 if impl == "tcgen05_2q" else 1)
     else:
         lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
     return o

@@ -359,10 +359,295 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------------ two-tile variant
+// One CTA = two 128-row query tiles of one (batch, head) sharing every K / V tile; 10 warps:
+//   warp 0      TMA: both Q tiles once; K and V tiles of 128 keys into a 2-stage ring
+//   warp 1      MMA (one thread), issue order per key block j:
+//                 PV0_j, S0_{j+1}, PV1_j, [release K/V stage j], S1_{j+1}
+//               so each tile's softmax of block j+1 overlaps the other tile's PV_j and S_{j+1}.
+//               P is written by the softmax warps into the tile's S columns of TMEM (bf16, two per
+//               32-bit column) and read from there as the A operand of PV (no shared-memory P);
+//               tcgen05 MMAs of one thread complete in issue order, so S_{j+1} overwriting P_j
+//               after PV_j was issued is safe, and the completion of S_{j+1} (its commit) also
+//               means PV_j has completed, which is when a softmax warp may rescale O in TMEM.
+//   warps 2..5  softmax of tile 0, warps 6..9 softmax of tile 1 (one query row per thread).
+// TMEM (512 columns): S0 / P0 at 0, S1 / P1 at 128, O0 at 256, O1 at 256 + DH.
+constexpr int kFa2Threads = 320;
+
+__device__ __forceinline__ void umma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int DH>
+__global__ void __launch_bounds__(kFa2Threads, 1)
+    fa2_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, FaParams p) {
+  constexpr int NCH = DH / 64;
+  constexpr uint32_t CHUNK_BYTES = 128 * 128;
+  constexpr uint32_t QT_BYTES = NCH * CHUNK_BYTES;   // one 128-row Q tile
+  constexpr uint32_t KV_BYTES = NCH * CHUNK_BYTES;   // one K (or V) stage
+  constexpr uint32_t IDESC_S = idesc_bf16_f32(kFaBM, kFaBN);
+  constexpr uint32_t IDESC_O = idesc_bf16_f32_b(kFaBM, DH, true);
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t O_COL = 2 * kFaBN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                   // 2 tiles
+  uint8_t* sK = sQ + 2 * QT_BYTES;      // 2 stages
+  uint8_t* sV = sK + 2 * KV_BYTES;      // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * KV_BYTES);
+  uint64_t* q_full = bars;              // 1
+  uint64_t* kv_full = bars + 1;         // 2
+  uint64_t* kv_empty = bars + 3;        // 2
+  uint64_t* s_full = bars + 5;          // 2 (per tile)
+  uint64_t* p_full = bars + 7;          // 2 (per tile)
+  uint64_t* o_full = bars + 9;          // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  __shared__ int s_nkb;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qt * 2 * kFaBM;
+  const bool has1 = q0 + kFaBM < p.Tq;  // the second tile holds at least one query row
+  const int kvh = h / (p.H / p.Hkv);
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(smem_addr(q_full), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&kv_full[i]), 1);
+      mbar_init(smem_addr(&kv_empty[i]), 1);
+      mbar_init(smem_addr(&s_full[i]), 1);
+      mbar_init(smem_addr(&p_full[i]), 128);
+    }
+    mbar_init(smem_addr(o_full), 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 2) {  // key blocks this CTA needs (causal: up to its last query's position)
+    int nk = (p.Tk + kFaBN - 1) / kFaBN;
+    if (p.causal) {
+      int mq = 0;
+      for (int r = lane; r < 2 * kFaBM; r += 32) {
+        const int qi = min(q0 + r, p.Tq - 1);
+        mq = max(mq, p.q_pos ? p.q_pos[(long)b * p.Tq + qi] : qi + p.Tk - p.Tq);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mq = max(mq, __shfl_xor_sync(0xffffffffu, mq, o));
+      nk = max(1, min(nk, mq / kFaBN + 1));
+    }
+    if (lane == 0) s_nkb = nk;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nkb = s_nkb;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t qb = smem_addr(q_full);
+      mbar_arrive_expect_tx(qb, 2 * QT_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < NCH; ++c)
+          tma_load_2d(smem_addr(sQ + t * QT_BYTES + c * CHUNK_BYTES), &tmQ, qb, h * DH + c * 64,
+                      b * p.Tq + q0 + t * kFaBM);
+      for (int j = 0; j < nkb; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(smem_addr(&kv_empty[s]), ((j >> 1) & 1) ^ 1, p.err, kErrTimeoutProducer)) break;
+        const uint32_t fb = smem_addr(&kv_full[s]);
+        mbar_arrive_expect_tx(fb, 2 * KV_BYTES);
+        const int row = p.block_table ? p.block_table[(long)b * p.max_blocks + j] * kFaBN : b * p.Tk + j * kFaBN;
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_2d(smem_addr(sK + s * KV_BYTES + c * CHUNK_BYTES), &tmK, fb, kvh * DH + c * 64, row);
+          tma_load_2d(smem_addr(sV + s * KV_BYTES + c * CHUNK_BYTES), &tmV, fb, kvh * DH + c * 64, row);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(smem_addr(q_full), 0, p.err, kErrTimeoutMma);
+      auto issue_s = [&](int t, int j) -> bool {
+        const int s = j & 1;
+        if (t == 0 && !mbar_wait(smem_addr(&kv_full[s]), (j >> 1) & 1, p.err, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t qa = smem_addr(sQ + t * QT_BYTES), ka = smem_addr(sK + s * KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < DH / 16; ++k) {
+          const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
+          umma_f16(tmem + t * kFaBN, sw128_kmajor_desc(qa + off), sw128_kmajor_desc(ka + off), IDESC_S, k > 0);
+        }
+        umma_commit(smem_addr(&s_full[t]));
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!mbar_wait(smem_addr(&p_full[t]), j & 1, p.err, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t va = smem_addr(sV + (j & 1) * KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < kFaBN / 16; ++k)
+          umma_f16_tmem_a(tmem + O_COL + t * DH, tmem + t * kFaBN + k * 8,
+                          sw128_mnmajor_desc(va + k * 2048, CHUNK_BYTES, 1024), IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0);
+      if (ok && has1) ok = issue_s(1, 0);
+      for (int j = 0; ok && j < nkb; ++j) {
+        if (!issue_pv(0, j)) { ok = false; break; }
+        if (j + 1 < nkb && !issue_s(0, j + 1)) { ok = false; break; }
+        if (has1 && !issue_pv(1, j)) { ok = false; break; }
+        umma_commit(smem_addr(&kv_empty[j & 1]));
+        if (has1 && j + 1 < nkb && !issue_s(1, j + 1)) { ok = false; break; }
+      }
+      if (ok) umma_commit(smem_addr(o_full));
+    }
+  } else {
+    const int t = (warp - 2) >> 2;                // query tile of this softmax warpgroup
+    const int qd = warp & 3;                      // TMEM lane quadrant
+    const int row = qd * 32 + lane;               // query row inside the tile
+    const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    const uint32_t s_col = t * kFaBN;
+    const int qrow = q0 + t * kFaBM + row;
+    float m_run = -FLT_MAX, l_run = 0.f;
+    bool ok = t == 0 || has1;
+    const bool cls_row = p.cls != nullptr && qt == 0 && t == 0 && row == 0;
+    const float sl2 = p.scale_log2;
+    int qpos = 0x7FFFFFFF;
+    if (p.causal) {
+      const int qi = min(qrow, p.Tq - 1);
+      qpos = p.q_pos ? p.q_pos[(long)b * p.Tq + qi] : qi + p.Tk - p.Tq;
+    }
+    for (int j = 0; ok && j < nkb; ++j) {
+      if (!mbar_wait(smem_addr(&s_full[t]), j & 1, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      const int kbase = j * kFaBN;
+      const int klim = min(p.Tk - 1, qpos);
+      const bool ragged = kbase + kFaBN - 1 > klim;
+      // pass 1: row max (S is read again in pass 2, so only 32 scores are live at a time)
+      float mx8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mx8[u] = -FLT_MAX;
+#pragma unroll
+      for (int c = 0; c < kFaBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + s_col + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+          float x = __uint_as_float(r[u]);
+          if (ragged && kbase + c * 32 + u > klim) x = -FLT_MAX;
+          mx8[u & 7] = fmaxf(mx8[u & 7], x);
+          if (cls_row && kbase + c * 32 + u < p.Tk) p.cls[((long)b * p.H + h) * p.Tk + kbase + c * 32 + u] = x * sl2;
+        }
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const bool grow = (mx - m_run) * sl2 > kRescaleThreshold;
+      const bool any_grow = __any_sync(0xffffffffu, grow) && j > 0;
+      float corr = 1.f;
+      if (grow || j == 0) {
+        const float mnew = fmaxf(m_run, mx);
+        corr = (j == 0) ? 0.f : ex2_approx((m_run - mnew) * sl2);
+        m_run = mnew;
+      }
+      if (any_grow) {  // PV_{j-1} of this tile completed before S_j did: O may be rescaled now
+#pragma unroll 1
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + O_COL + t * DH + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < 32; ++u) r[u] = __float_as_uint(__uint_as_float(r[u]) * corr);
+          tmem_st32(tmem + lane_base + O_COL + t * DH + c * 32, r);
+        }
+      }
+      l_run *= (j == 0) ? 0.f : corr;
+      const float moff = m_run * sl2;
+      float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // pass 2: P = exp2(S * scale - m) for 64 keys at a time, packed two per 32-bit TMEM column
+      // into the tile's S columns [32c, 32c + 32): those scores were consumed by an earlier chunk
+#pragma unroll
+      for (int c = 0; c < kFaBN / 64; ++c) {
+        uint32_t r0[32], r1[32], pk[32];
+        tmem_ld32(tmem + lane_base + s_col + c * 64, r0);
+        tmem_ld32(tmem + lane_base + s_col + c * 64 + 32, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+          const int k0 = kbase + c * 64 + 2 * u;
+          const uint32_t a0 = u < 16 ? r0[2 * u] : r1[2 * u - 32];
+          const uint32_t a1 = u < 16 ? r0[2 * u + 1] : r1[2 * u - 31];
+          float e0 = ex2_approx(fmaf(__uint_as_float(a0), sl2, -moff));
+          float e1 = ex2_approx(fmaf(__uint_as_float(a1), sl2, -moff));
+          if (ragged) {
+            if (k0 > klim) e0 = 0.f;
+            if (k0 + 1 > klim) e1 = 0.f;
+          }
+          ls8[(2 * u) & 7] += e0;
+          ls8[(2 * u + 1) & 7] += e1;
+          pk[u] = pack_bf16x2(e0, e1);
+        }
+        tmem_st32(tmem + lane_base + s_col + c * 32, pk);
+      }
+      tmem_wait_st();
+      l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
+      tc_fence_before();
+      mbar_arrive(smem_addr(&p_full[t]));
+    }
+    if (ok && (t == 0 || has1) && mbar_wait(smem_addr(o_full), 0, p.err, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+      const float inv = 1.f / l_run;
+      bf16* orow = p.o + ((long)b * p.Tq + qrow) * p.ldo + (long)h * DH;
+#pragma unroll 1
+      for (int c = 0; c < DH / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + O_COL + t * DH + c * 32, r);
+        tmem_wait_ld();
+        if (qrow < p.Tq) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            dst[v] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * v]) * inv, __uint_as_float(r[8 * v + 1]) * inv),
+                                pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv),
+                                pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv),
+                                pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv));
+        }
+      }
+      if (p.lse != nullptr && qrow < p.Tq)
+        p.lse[((long)b * p.H + h) * p.Tq + qrow] = (m_run * sl2 + log2f(l_run)) * 0.69314718055994531f;
+    }
+    if (p.cls != nullptr && qt == 0 && t == 0 && qd == 0) {  // the warp holding row 0 normalises the CLS row
+      __syncwarp();
+      const float m0 = __shfl_sync(0xffffffffu, m_run, 0) * sl2;
+      const float inv0 = 1.f / __shfl_sync(0xffffffffu, l_run, 0);
+      float* src = p.cls + ((long)b * p.H + h) * p.Tk;
+      for (int u = lane; u < p.Tk; u += 32) src[u] = exp2f(src[u] - m0) * inv0;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, int64_t B,
                         int64_t Tq, int64_t Tk, int64_t H, int64_t Dh, double scale, c10::optional<at::Tensor> lse,
                         const at::Tensor& err, c10::optional<at::Tensor> cls, int64_t Hkv, bool causal,
-                        c10::optional<at::Tensor> q_pos, c10::optional<at::Tensor> block_table) {
+                        c10::optional<at::Tensor> q_pos, c10::optional<at::Tensor> block_table, int64_t variant) {
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &o}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->stride(-1) == 1, "attention: bf16 CUDA tensors");
     TORCH_CHECK(t->stride(-2) % 8 == 0 && (reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) == 0, "attention: 16B-aligned rows");
@@ -405,8 +690,22 @@ void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tens
     TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->numel() >= B * H * Tq, "attention: lse fp32 [B,H,Tq]");
     p.lse = lse->data_ptr<float>();
   }
-  dim3 grid((Tq + kFaBM - 1) / kFaBM, H, B);
   auto st = at::cuda::getCurrentCUDAStream();
+  if (variant == 0) {  // two query tiles per CTA
+    dim3 grid2((Tq + 2 * kFaBM - 1) / (2 * kFaBM), H, B);
+    const int nch2 = static_cast<int>(Dh / 64);
+    const int smem2 = nch2 * 16384 * 6 + 1024 + 256;
+    if (Dh == 128) {
+      cudaFuncSetAttribute(fa2_fwd_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
+      fa2_fwd_sm100_kernel<128><<<grid2, kFa2Threads, smem2, st>>>(tq, tk, tv, p);
+    } else {
+      cudaFuncSetAttribute(fa2_fwd_sm100_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
+      fa2_fwd_sm100_kernel<64><<<grid2, kFa2Threads, smem2, st>>>(tq, tk, tv, p);
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  dim3 grid((Tq + kFaBM - 1) / kFaBM, H, B);
   const int nch = static_cast<int>(Dh / 64);
   const int smem = nch * 16384 * 5 + 4 * 16384 + 1024 + 256;
   if (Dh == 128) {
@@ -424,7 +723,7 @@ void register_attention_sm100_ops(pybind11::module_& m) {
   m.def("attention_sm100", &attention_sm100_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("B"),
         py::arg("Tq"), py::arg("Tk"), py::arg("H"), py::arg("Dh"), py::arg("scale"), py::arg("lse"), py::arg("err"),
         py::arg("cls") = py::none(), py::arg("Hkv") = 0, py::arg("causal") = false, py::arg("q_pos") = py::none(),
-        py::arg("block_table") = py::none());
+        py::arg("block_table") = py::none(), py::arg("variant") = 0);
 }
 
 }  // namespace appcorr
