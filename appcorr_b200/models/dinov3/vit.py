@@ -57,6 +57,12 @@ class ViTConfig:
     mask_k_bias: bool = True
     untie_cls_and_patch_norms: bool = False
     untie_global_and_local_cls_norm: bool = False
+    # windowed attention (SAM-style towers; engine only): square windows of `window_size` patches,
+    # global attention at `global_layers`; window-local RoPE coordinates on windowed layers
+    window_size: int = 0
+    global_layers: Tuple[int, ...] = ()
+    window_rope_everywhere: bool = False  # global layers also use window-local RoPE (multi-frame towers)
+    cls_token: bool = True                # False: patch tokens only (SAM- / VGGT-style towers)
 
     @property
     def head_dim(self) -> int:
@@ -64,7 +70,7 @@ class ViTConfig:
 
     @property
     def n_prefix(self) -> int:
-        return 1 + self.n_storage_tokens
+        return int(self.cls_token) + self.n_storage_tokens
 
     @property
     def norm_eps(self) -> float:

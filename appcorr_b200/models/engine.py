@@ -231,6 +231,9 @@ class ViTEngine:
         self.device = torch.device(device) if device is not None else weights.patch_w.device
         if self.cfg.head_dim not in (64, 128):
             raise ValueError("the sm_100a engine supports head_dim 64 or 128")
+        kp = (3 * self.cfg.patch_size ** 2 + 15) // 16 * 16  # patch rows padded to 16 elements
+        if self.w.patch_w.shape[1] != kp:
+            self.w.patch_w = torch.nn.functional.pad(self.w.patch_w, (0, kp - self.w.patch_w.shape[1])).contiguous()
         if isinstance(precision, str):
             precision = {"approx": precision, "correct": precision}
         for v in precision.values():
@@ -305,24 +308,57 @@ class ViTEngine:
 
         patch_rows = (torch.arange(B, device=dev)[:, None] * N + c.n_prefix + torch.arange(P, device=dev)[None, :])
         T = c.n_prefix + P
+        order = None
+        if c.window_size > 0:
+            if c.n_prefix or gh % c.window_size or gw % c.window_size:
+                raise ValueError("windowed towers need no prefix tokens and a grid that tiles into windows")
+            from .qwen25vl import window_order
+
+            order = window_order(gh, gw, c.window_size, 1).to(device=dev, dtype=torch.int32)
         sess = Session(
             B=B, img_hw=(H, W), grid_hw=(gh, gw), N=N, P=P,
             x_in=e(M, D), x=e(M, D), x_tmp=e(M, D), xn=e(M, D), q=e(M, D), o=e(M, D), h=e(M, Hd),
             kc=e(L, M, D), vc=e(L, M, D), bos=e(L, M, D), pscore=torch.zeros(L, B, N, device=dev),
-            ps_scratch=e(B, c.num_heads, N, dtype=torch.float32), cols=e(B * P, 3 * p * p),
+            ps_scratch=e(B, c.num_heads, N, dtype=torch.float32),
+            cols=torch.zeros(B * P, self.w.patch_w.shape[1], device=dev, dtype=BF16),
             patch_rows=patch_rows.reshape(-1).to(torch.int32).contiguous(),
-            rope=rope_tables(c, self.w.periods, gh, gw) if self.w.periods is not None else None,
+            rope=self._rope_global(gh, gw, order),
             upd=torch.zeros(B, T, device=dev, dtype=torch.int32), rows=torch.zeros(B * T, device=dev, dtype=torch.int32),
             x_act=e(B * T, D), x_att=e(B * T, D), plan_stats=torch.zeros(B, 2, device=dev),
             stat_acc=torch.zeros(5, device=dev))
+        if order is not None:
+            ws = c.window_size
+            sess.extra["order"] = order.contiguous()
+            sess.extra["n_windows"] = (gh // ws) * (gw // ws)
+            if self.w.periods is not None:
+                sw, cw = rope_tables(c, self.w.periods, ws, ws)
+                reps = (gh // ws) * (gw // ws)
+                sess.extra["rope_win"] = (sw.repeat(reps, 1).contiguous(), cw.repeat(reps, 1).contiguous())
         return sess
+
+    def _rope_global(self, gh: int, gw: int, order: Optional[torch.Tensor]):
+        if self.w.periods is None:
+            return None
+        s, c = rope_tables(self.cfg, self.w.periods, gh, gw)
+        if order is not None:  # tables follow the token order
+            s, c = s[order.long()].contiguous(), c[order.long()].contiguous()
+        return s, c
+
+    def _windowed(self, l: int) -> bool:
+        return self.cfg.window_size > 0 and l not in self.cfg.global_layers
+
+    def _rope(self, sess: Session, l: int):
+        if self._windowed(l) or (self.cfg.window_size > 0 and self.cfg.window_rope_everywhere):
+            return sess.extra.get("rope_win", sess.rope)
+        return sess.rope
 
     # -------------------------------------------------------------- tokens
     def prepare_tokens(self, sess: Session, img: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """uint8 [B, H, W, 3] image -> tokens [B*N, D] (CLS + storage + patch embeddings)."""
         c = self.cfg
         out = sess.x_in if out is None else out
-        K.patch_im2col(img, c.patch_size, sess.cols, mean=self.w.pixel_mean, std=self.w.pixel_std)
+        K.patch_im2col(img, c.patch_size, sess.cols, mean=self.w.pixel_mean, std=self.w.pixel_std,
+                       perm=sess.extra.get("order"))
         K.gemm(sess.cols, self.w.patch_w, out, bias=self.w.patch_b, out_rows=sess.patch_rows)
         K.set_prefix(out, self.w.prefix, sess.B, sess.N)
         if self.w.pos_embed is not None:
@@ -350,8 +386,13 @@ class ViTEngine:
         a, sa = self._norm(sess, x, lw.norm1_w, lw.norm1_b, sess.xn)
         w, ws = self._w(lw, "qkv")
         K.qkv_gemm(a, w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
-                   rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
-        self._attention_with_score(sess, l, H, server_pscore not in ("none", "disabled"), sess.pscore[l])
+                   rope=self._rope(sess, l), n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
+        if self._windowed(l):  # windows are contiguous token runs: a batched attention over windows
+            nw = sess.extra["n_windows"]
+            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B * nw, Tq=N // nw, Tk=N // nw, H=H, Dh=Dh)
+        else:
+            self._attention_with_score(sess, l, H, server_pscore not in ("none", "disabled") and c.n_prefix > 0,
+                                       sess.pscore[l])
         # x_out = x + ls1 * proj(o); bos[l] = ls1 * proj(o)
         a, sa = self._act(sess, sess.o)
         w, ws = self._w(lw, "proj")
@@ -415,10 +456,21 @@ class ViTEngine:
         rows = sess.rows[: B * T]
         if server is None:
             server = sess.pscore[l]
+        sess.extra["plan_id"] = sess.extra.get("plan_id", 0) + 1
         K.correction_plan(server, pre, cand, k, upd, rows, mobile=mobile, ws=float(opts.get("server_pscore_weight", 1.0)),
                           wm=float(opts.get("mobile_pscore_weight", 0.0)), fusion=opts.get("pscore_fusion", "add"),
                           valid=valid, stats=sess.plan_stats)
         return upd, rows
+
+    def _window_bounds(self, sess: Session, upd: torch.Tensor):
+        """Per packed query: first and last key of its window (cached per plan)."""
+        key = upd.data_ptr(), upd.shape[1], sess.extra.get("plan_id", 0)
+        wb = sess.extra.get("win_bounds")
+        if wb is None or wb[0] != key:
+            tw = self.cfg.window_size ** 2
+            lo = (upd.view(-1) // tw * tw).to(torch.int32).contiguous()
+            wb = sess.extra["win_bounds"] = (key, lo, (lo + tw - 1).contiguous())
+        return wb[1], wb[2]
 
     def correct_layer(self, sess: Session, l: int, x: torch.Tensor, upd: torch.Tensor, rows: torch.Tensor) -> None:
         c, lw = self.cfg, self.w.layers[l]
@@ -432,8 +484,12 @@ class ViTEngine:
         K.add_(x, sess.bos[l])
         w, ws = self._w(lw, "qkv")
         K.qkv_gemm(a, w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
-                   kv_rows=rows, rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
-        K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh)
+                   kv_rows=rows, rope=self._rope(sess, l), n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
+        if self._windowed(l):  # each kept query attends its own window's keys
+            lo, hi = self._window_bounds(sess, upd)
+            K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh, causal=True, q_pos=hi, q_lo=lo)
+        else:
+            K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh)
         a, sa = self._act(sess, o)
         w, ws = self._w(lw, "proj")
         K.gemm(a, w, x_att, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x_act, a_scale=sa, b_scale=ws)
@@ -446,13 +502,16 @@ class ViTEngine:
                aux=sess.bos[l], aux_mode=K.AUX_OUT_MINUS, resid2=x_act, a_scale=sa, b_scale=ws)
 
     def correct(self, sess: Session, start: int, end: int, pre: torch.Tensor, cand: torch.Tensor, opts: Dict,
-                mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None) -> torch.Tensor:
+                mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None,
+                server: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Correction pass over layers [start, end) starting from the fresh tokens `sess.x_in`.
 
         pre: int32 [B, n_prefix] prefix token indices; cand: int32 [B, P_g] candidate patch tokens
         (the residual group that just arrived). Keeps k = int(P_g * token_keep_ratio) per image.
         """
         st = self._correct_begin(sess, start, cand, opts)
+        if server is not None:  # caller-provided per-token score [B, N], one plan for every layer
+            st["shared"] = server
         for l in range(start, end):
             self._correct_step(sess, l, st, pre, cand, opts, mobile, valid)
         return sess.x

@@ -130,7 +130,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor
               Tk: int, H: int, Dh: int, scale: Optional[float] = None,
               lse: Optional[torch.Tensor] = None, impl: Optional[str] = None,
               cls_probs: Optional[torch.Tensor] = None, Hkv: int = 0, causal: bool = False,
-              q_pos: Optional[torch.Tensor] = None, block_table: Optional[torch.Tensor] = None) -> torch.Tensor:
+              q_pos: Optional[torch.Tensor] = None, block_table: Optional[torch.Tensor] = None,
+              q_lo: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Attention on BTHD tensors: q/o [B*Tq, H*Dh], k/v [B*Tk, Hkv*Dh].
 
     cls_probs (tcgen05 path): fp32 [B, H, Tk] receives the softmax row of query 0 (the CLS
@@ -138,17 +139,21 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor
     Hkv: key/value heads (grouped-query attention; 0 = H). causal: query row i sees keys up to
     q_pos[i] (int32 [B*Tq]; default i + Tk - Tq), so a packed, non-contiguous query set attends
     with its own causal frontier. block_table: int32 [B, blocks] of 128-row pages in a paged
-    K/V pool (k/v are then the pools).
+    K/V pool (k/v are then the pools). q_lo: int32 [B*Tq] first key of each query row; with
+    causal=True and q_pos as the last key, each query attends the key range [q_lo, q_pos]
+    (windowed attention of packed queries).
     """
     if scale is None:
         scale = Dh ** -0.5
     impl = impl or ATTENTION_IMPL[0]
     if impl == "mma" and (Hkv or causal or q_pos is not None or block_table is not None):
         impl = "tcgen05"
+    if q_lo is not None:
+        impl = "tcgen05"
     _count()
     if impl in ("tcgen05", "tcgen05_2q"):
         lib().attention_sm100(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse, err_word(q.device), cls_probs,
-                              Hkv, causal, q_pos, block_table, 0 if impl == "tcgen05_2q" else 1)
+                              Hkv, causal, q_pos, block_table, 0 if impl == "tcgen05_2q" else 1, q_lo)
     else:
         lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
     return o

@@ -130,7 +130,7 @@ class ViTEngineTP(ViTEngine):
             B=B, img_hw=(H, W), grid_hw=s0.grid_hw, N=N, P=P,
             x_in=torch.empty(M, D, device=dev, dtype=BF16), x=s0.x, x_tmp=s0.x_tmp, xn=s0.xn, q=s0.q, o=s0.o,
             h=s0.h, kc=s0.kc, vc=s0.vc, bos=s0.bos, pscore=torch.zeros(c.depth, B, N, device=dev),
-            ps_scratch=s0.ps_scratch, cols=torch.empty(B * P, 3 * c.patch_size ** 2, device=dev, dtype=BF16),
+            ps_scratch=s0.ps_scratch, cols=torch.zeros(B * P, self.w.patch_w.shape[1], device=dev, dtype=BF16),
             patch_rows=(torch.arange(B, device=dev)[:, None] * N + c.n_prefix
                         + torch.arange(P, device=dev)[None, :]).reshape(-1).to(torch.int32).contiguous(),
             rope=s0.rope, upd=s0.upd, rows=s0.rows, x_act=s0.x_act, x_att=s0.x_att, plan_stats=s0.plan_stats,

@@ -30,6 +30,14 @@ def get_model_executor(name: str, device) -> ModelExecutor:
         from .qwen25vl_executor import Qwen25VLExecutor
 
         return Qwen25VLExecutor(device)
+    if "vggt" in name:
+        from .vggt_executor import VGGTExecutor
+
+        return VGGTExecutor(device)
+    if "sam3" in name:
+        from .sam3_executor import Sam3Executor
+
+        return Sam3Executor(device)
     if "openclip" in name or "clip" in name:
         from .openclip_executor import OpenCLIPExecutor
 

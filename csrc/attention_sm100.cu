@@ -72,6 +72,8 @@ struct FaParams {
   const int* q_pos;         // [B * Tq] key-axis position of each query row (causal; nullptr: i + Tk - Tq)
   const int* block_table;   // [B, max_blocks] physical 128-row page of each key block (nullptr: b * Tk + j * 128)
   int max_blocks;
+  const int* q_lo;          // [B * Tq] first key each query row may see (nullptr: 0); with causal / q_pos
+                            // as the last one this gives per-query key ranges (windowed attention)
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int q0 = qt * kFaBM;
   const int kvh = h / (p.H / p.Hkv);
-  __shared__ int s_nkb;
+  __shared__ int s_nkb, s_kb0;
 
   if (warp == 0 && lane == 0) {
     mbar_init(smem_addr(q_full), 1);
@@ -149,13 +151,25 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       for (int o = 16; o > 0; o >>= 1) mq = max(mq, __shfl_xor_sync(0xffffffffu, mq, o));
       nk = max(1, min(nk, mq / kFaBN + 1));
     }
-    if (lane == 0) s_nkb = nk;
+    int kb0 = 0;  // first key block (per-query lower bounds: the tile's smallest)
+    if (p.q_lo) {
+      int lo = 0x7FFFFFFF;
+      for (int r = lane; r < kFaBM; r += 32) lo = min(lo, p.q_lo[(long)b * p.Tq + min(q0 + r, p.Tq - 1)]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      kb0 = min(max(lo, 0) / kFaBN, nk - 1);
+    }
+    if (lane == 0) {
+      s_nkb = nk - kb0;
+      s_kb0 = kb0;
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int nkb = s_nkb;
+  const int nkb = s_nkb;   // key blocks visited: kb0 .. kb0 + nkb - 1
+  const int kb0 = s_kb0;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -169,7 +183,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (!mbar_wait(smem_addr(&kv_empty[s]), ph ^ 1, p.err, kErrTimeoutProducer)) break;
         const uint32_t fb = smem_addr(&kv_full[s]);
         mbar_arrive_expect_tx(fb, 2 * KV_BYTES);
-        const int row = p.block_table ? p.block_table[(long)b * p.max_blocks + j] * kFaBN : b * p.Tk + j * kFaBN;
+        const int jb = kb0 + j;
+        const int row = p.block_table ? p.block_table[(long)b * p.max_blocks + jb] * kFaBN : b * p.Tk + jb * kFaBN;
         for (int c = 0; c < NCH; ++c) {
           tma_load_2d(smem_addr(sK + s * KV_BYTES + c * CHUNK_BYTES), &tmK, fb, kvh * DH + c * 64, row);
           tma_load_2d(smem_addr(sV + s * KV_BYTES + c * CHUNK_BYTES), &tmV, fb, kvh * DH + c * 64, row);
@@ -226,6 +241,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       const int qi = min(q0 + row, p.Tq - 1);
       qpos = p.q_pos ? p.q_pos[(long)b * p.Tq + qi] : qi + p.Tk - p.Tq;
     }
+    const int qlo = p.q_lo ? p.q_lo[(long)b * p.Tq + min(q0 + row, p.Tq - 1)] : 0;  // first key it may see
     // m_run: running max of the raw scores; exponent = S * sl2 - m_run * sl2 (one FFMA)
     for (int j = 0; j < nkb; ++j) {
       const int s = j & 1;
@@ -242,12 +258,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(smem_addr(&s_free[s]));
-      const int kbase = j * kFaBN;
+      const int kbase = (kb0 + j) * kFaBN;
       const int klim = min(p.Tk - 1, qpos);  // keys past Tk do not exist; causal rows stop at qpos
-      if (kbase + kFaBN - 1 > klim) {
+      if (kbase + kFaBN - 1 > klim || kbase < qlo) {
 #pragma unroll
         for (int t = 0; t < kFaBN; ++t)
-          if (kbase + t > klim) sv[t] = -FLT_MAX;
+          if (kbase + t > klim || kbase + t < qlo) sv[t] = -FLT_MAX;
       }
       float mx8[8];
 #pragma unroll
@@ -647,7 +663,8 @@ __global__ void __launch_bounds__(kFa2Threads, 1)
 void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, int64_t B,
                         int64_t Tq, int64_t Tk, int64_t H, int64_t Dh, double scale, c10::optional<at::Tensor> lse,
                         const at::Tensor& err, c10::optional<at::Tensor> cls, int64_t Hkv, bool causal,
-                        c10::optional<at::Tensor> q_pos, c10::optional<at::Tensor> block_table, int64_t variant) {
+                        c10::optional<at::Tensor> q_pos, c10::optional<at::Tensor> block_table, int64_t variant,
+                        c10::optional<at::Tensor> q_lo) {
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &o}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->stride(-1) == 1, "attention: bf16 CUDA tensors");
     TORCH_CHECK(t->stride(-2) % 8 == 0 && (reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) == 0, "attention: 16B-aligned rows");
@@ -680,7 +697,13 @@ void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tens
              static_cast<float>(scale * 1.4426950408889634), reinterpret_cast<bf16*>(o.data_ptr()), o.stride(-2),
              nullptr, nullptr, err.data_ptr<int>(), static_cast<int>(Hkv), causal ? 1 : 0,
              q_pos.has_value() ? q_pos->data_ptr<int>() : nullptr,
-             block_table.has_value() ? block_table->data_ptr<int>() : nullptr, max_blocks};
+             block_table.has_value() ? block_table->data_ptr<int>() : nullptr, max_blocks, nullptr};
+  if (q_lo.has_value()) {
+    TORCH_CHECK(q_lo->scalar_type() == at::kInt && q_lo->numel() == B * Tq && q_lo->is_contiguous(),
+                "attention: q_lo int32 [B*Tq]");
+    TORCH_CHECK(variant != 0, "attention: per-query lower key bounds run on the one-tile kernel");
+    p.q_lo = q_lo->data_ptr<int>();
+  }
   if (cls.has_value()) {
     TORCH_CHECK(cls->scalar_type() == at::kFloat && cls->is_contiguous() && cls->numel() >= B * H * Tk,
                 "attention: cls fp32 [B,H,Tk]");
@@ -723,7 +746,7 @@ void register_attention_sm100_ops(pybind11::module_& m) {
   m.def("attention_sm100", &attention_sm100_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("B"),
         py::arg("Tq"), py::arg("Tk"), py::arg("H"), py::arg("Dh"), py::arg("scale"), py::arg("lse"), py::arg("err"),
         py::arg("cls") = py::none(), py::arg("Hkv") = 0, py::arg("causal") = false, py::arg("q_pos") = py::none(),
-        py::arg("block_table") = py::none(), py::arg("variant") = 0);
+        py::arg("block_table") = py::none(), py::arg("variant") = 0, py::arg("q_lo") = py::none());
 }
 
 }  // namespace appcorr
