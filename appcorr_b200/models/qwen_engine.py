@@ -103,7 +103,13 @@ class QwenSession:
 
 
 class QwenVLEngine:
-    def __init__(self, model: Qwen25VL, device):
+    """precision "fp8": the LLM's four GEMMs per layer run on e4m3 operands (per-row activation /
+    per-channel weight scales, RMSNorm emitting e4m3 rows directly); the vision tower stays bf16."""
+
+    def __init__(self, model: Qwen25VL, device, precision: str = "bf16"):
+        if precision not in ("bf16", "fp8"):
+            raise ValueError(f"precision must be bf16 or fp8, got {precision!r}")
+        self.fp8 = precision == "fp8"
         self.cfg = c = model.cfg
         self.device = dev = torch.device(device)
         bf = lambda t: t.detach().to(device=dev, dtype=BF16).contiguous()  # noqa: E731
@@ -147,6 +153,11 @@ class QwenVLEngine:
             w12, _ = pack_swiglu(ly.mlp.gate_proj.weight.detach(), ly.mlp.up_proj.weight.detach(), None, None)
             self.llm.append(LlmW(bf(ly.input_layernorm.weight), bf(qkv_w), bf(qkv_b), bf(ly.o_proj.weight),
                                  bf(ly.post_attention_layernorm.weight), bf(w12), bf(ly.mlp.down_proj.weight)))
+        self.q8 = None
+        if self.fp8:
+            self.q8 = [{n: K.quantize_weight_e4m3(getattr(w, n)) for n in ("qkv_w", "o_w", "w12", "w3")}
+                       for w in self.llm]
+        self.nh, self.nkv, self.nffn = c.heads, c.kv_heads, c.ffn  # heads / hidden held by this process
         self.norm = bf(model.norm.weight)
         lm = model.lm_head.weight.detach()
         self.lm_head = bf(torch.nn.functional.pad(lm, (0, 0, 0, _pad_to(c.vocab, 32) - c.vocab)))
@@ -182,10 +193,10 @@ class QwenVLEngine:
         pos = mrope_positions(n_before, gh // c.merge, gw // c.merge, n_after)
         s, co = mrope_tables(c, pos)
         t["sin"], t["cos"] = s.to(dev).contiguous(), co.to(dev).contiguous()
-        D, L, kvd = c.hidden, c.depth, c.kv_heads * c.head_dim
+        D, L, kvd = c.hidden, c.depth, self.nkv * c.head_dim
         t["x_in"], t["x"], t["xn"] = e(N, D), e(N, D), e(N, D)
-        t["q"], t["o"] = e(N, c.heads * c.head_dim), e(N, c.heads * c.head_dim)
-        t["h"] = e(N, c.ffn)
+        t["q"], t["o"] = e(N, self.nh * c.head_dim), e(N, self.nh * c.head_dim)
+        t["h"] = e(N, self.nffn)
         t["x_act"], t["x_att"] = e(N, D), e(N, D)
         t["bos"] = e(L, N, D)
         t["emb_prev"] = e(n_img, D)
@@ -205,7 +216,34 @@ class QwenVLEngine:
         t["rows"] = torch.zeros(N, device=dev, dtype=torch.int32)
         t["plan_stats"] = torch.zeros(1, 2, device=dev)
         t["logits"] = e(1, _pad_to(c.vocab, 32), dtype=torch.float32)
+        if self.fp8:
+            t["a8"] = torch.empty(N, max(D, self.nffn), device=dev, dtype=torch.float8_e4m3fn)
+            t["a8s"] = torch.empty(N, device=dev, dtype=torch.float32)
         return sess
+
+    # ------------------------------------------------------------------ LLM operand helpers
+    def _norm(self, t, x, w, out, **kw):
+        """RMSNorm feeding a GEMM -> (operand, row scales or None)."""
+        if not self.fp8:
+            K.rmsnorm(x, w, self.cfg.rms_eps, out, **kw)
+            return out, None
+        n = out.shape[0]
+        q8, sc = t["a8"][:n, :out.shape[1]], t["a8s"][:n]
+        K.layernorm(x, w, None, self.cfg.rms_eps, q8, scale8=sc, rms=True, **kw)
+        return q8, sc
+
+    def _act(self, t, a):
+        if not self.fp8:
+            return a, None
+        n, k = a.shape
+        q8, sc = t["a8"][:n, :k], t["a8s"][:n]
+        K.quant_rows_e4m3(a, q8, sc)
+        return q8, sc
+
+    def _wt(self, l: int, name: str):
+        if self.fp8:
+            return self.q8[l][name]
+        return getattr(self.llm[l], name), None
 
     # ------------------------------------------------------------------ vision tower
     def vision(self, sess: QwenSession, img: torch.Tensor) -> None:
@@ -247,18 +285,24 @@ class QwenVLEngine:
         x, xn = t["x"], t["xn"]
         x.copy_(t["x_in"])
         for l, w in enumerate(self.llm):
-            K.rmsnorm(x, w.norm1, c.rms_eps, xn)
-            K.qkv_gemm(xn, w.qkv_w, w.qkv_b, t["q"], t["kc"][l], t["vc"][l], head_dim=c.head_dim, seq_len=N,
+            a, sa = self._norm(t, x, w.norm1, xn)
+            wq, sw = self._wt(l, "qkv_w")
+            K.qkv_gemm(a, wq, w.qkv_b, t["q"], t["kc"][l], t["vc"][l], head_dim=c.head_dim, seq_len=N,
                        kv_rows=t["phys"], rope=(t["sin"], t["cos"]), n_prefix=0,
-                       kv_dim=c.kv_heads * c.head_dim)
+                       kv_dim=c.kv_heads * c.head_dim, a_scale=sa, b_scale=sw)
             K.attention(t["q"], t["kc"][l], t["vc"][l], t["o"], B=1, Tq=N, Tk=N, H=c.heads, Dh=c.head_dim,
                         Hkv=c.kv_heads, causal=True, block_table=t["block_table"])
-            K.gemm(t["o"], w.o_w, x, epi=K.EPI_RESID, gamma=self.ones, resid=x, aux=t["bos"][l],
-                   aux_mode=K.AUX_SET)
-            K.rmsnorm(x, w.norm2, c.rms_eps, xn)
-            K.gemm(xn, w.w12, t["h"], epi=K.EPI_SWIGLU)
-            K.gemm(t["h"], w.w3, x, epi=K.EPI_RESID, gamma=self.ones, resid=x, aux=t["bos"][l],
-                   aux_mode=K.AUX_ADD)
+            a, sa = self._act(t, t["o"])
+            wq, sw = self._wt(l, "o_w")
+            K.gemm(a, wq, x, epi=K.EPI_RESID, gamma=self.ones, resid=x, aux=t["bos"][l],
+                   aux_mode=K.AUX_SET, a_scale=sa, b_scale=sw)
+            a, sa = self._norm(t, x, w.norm2, xn)
+            wq, sw = self._wt(l, "w12")
+            K.gemm(a, wq, t["h"], epi=K.EPI_SWIGLU, a_scale=sa, b_scale=sw)
+            a, sa = self._act(t, t["h"])
+            wq, sw = self._wt(l, "w3")
+            K.gemm(a, wq, x, epi=K.EPI_RESID, gamma=self.ones, resid=x, aux=t["bos"][l],
+                   aux_mode=K.AUX_ADD, a_scale=sa, b_scale=sw)
         t["emb_prev"].copy_(t["x_in"][sess.n_before:sess.n_before + sess.n_img])
         sess.approx_done = True
         return x
@@ -287,16 +331,23 @@ class QwenVLEngine:
         xn, q, o, h = t["xn"][:T], t["q"][:T], t["o"][:T], t["h"][:T]
         x_act, x_att = t["x_act"][:T], t["x_att"][:T]
         for l, w in enumerate(self.llm):
-            K.rmsnorm(x, w.norm1, c.rms_eps, xn, rows=rows, copy_out=x_act)
+            a, sa = self._norm(t, x, w.norm1, xn, rows=rows, copy_out=x_act)
             K.add_(x, t["bos"][l])
-            K.qkv_gemm(xn, w.qkv_w, w.qkv_b, q, t["kc"][l], t["vc"][l], head_dim=c.head_dim, tok_idx=upd.view(-1),
-                       kv_rows=kv_sel, rope=(t["sin"], t["cos"]), n_prefix=0, kv_dim=c.kv_heads * c.head_dim)
+            wq, sw = self._wt(l, "qkv_w")
+            K.qkv_gemm(a, wq, w.qkv_b, q, t["kc"][l], t["vc"][l], head_dim=c.head_dim, tok_idx=upd.view(-1),
+                       kv_rows=kv_sel, rope=(t["sin"], t["cos"]), n_prefix=0, kv_dim=c.kv_heads * c.head_dim,
+                       a_scale=sa, b_scale=sw)
             K.attention(q, t["kc"][l], t["vc"][l], o, B=1, Tq=T, Tk=N, H=c.heads, Dh=c.head_dim, Hkv=c.kv_heads,
                         causal=True, q_pos=upd.view(-1), block_table=t["block_table"])
-            K.gemm(o, w.o_w, x_att, epi=K.EPI_RESID, gamma=self.ones, resid=x_act)
-            K.rmsnorm(x_att, w.norm2, c.rms_eps, xn)
-            K.gemm(xn, w.w12, h, epi=K.EPI_SWIGLU)
-            K.gemm(h, w.w3, x, epi=K.EPI_RESID, gamma=self.ones, resid=x_att, out_rows=rows)
+            a, sa = self._act(t, o)
+            wq, sw = self._wt(l, "o_w")
+            K.gemm(a, wq, x_att, epi=K.EPI_RESID, gamma=self.ones, resid=x_act, a_scale=sa, b_scale=sw)
+            a, sa = self._norm(t, x_att, w.norm2, xn)
+            wq, sw = self._wt(l, "w12")
+            K.gemm(a, wq, h, epi=K.EPI_SWIGLU, a_scale=sa, b_scale=sw)
+            a, sa = self._act(t, h)
+            wq, sw = self._wt(l, "w3")
+            K.gemm(a, wq, x, epi=K.EPI_RESID, gamma=self.ones, resid=x_att, out_rows=rows, a_scale=sa, b_scale=sw)
         t["emb_prev"].copy_(t["x_in"][sess.n_before:sess.n_before + sess.n_img])
         return x
 

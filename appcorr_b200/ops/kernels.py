@@ -75,8 +75,8 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
     [q (N - 2 kv_dim) | k (kv_dim) | v (kv_dim)].
     """
     dim = w.shape[0] - 2 * kv_dim if kv_dim else w.shape[0] // 3
-    if bn is None:
-        bn = 256 if dim % 256 == 0 and (kv_dim or dim) % 256 == 0 else 128
+    if bn is None:  # widest tile that divides the q and the k / v widths (tiles never straddle)
+        bn = next((t for t in (256, 128, 64) if dim % t == 0 and (kv_dim or dim) % t == 0), 128)
     sin, cos = rope if rope is not None else (None, None)
     _count()
     lib().gemm(a, w, EPI_QKV, bn, err_word(a.device), bias=bias, q_out=q_out, k_out=k_out, v_out=v_out,

@@ -40,7 +40,19 @@ class Qwen25VLExecutor(ModelExecutor):
         self.n_before = int(profile.get("n_text_before", 16))
         self.n_after = int(profile.get("n_text", 128)) - self.n_before
         model = Qwen25VL.random_on(self.cfg, self.device, seed)
-        self.engine = QwenVLEngine(model, self.device)
+        prec = DINOv3BackboneMixin.engine_precision(config)["approx"]
+        tp = int(getattr(config, "tp_size", 1) or 1)
+        if tp > 1:
+            import torch.distributed as dist
+
+            from ...parallel.comm import TPComm
+            from ...parallel.qwen_tp import QwenVLEngineTP
+
+            if not dist.is_initialized() or dist.get_world_size() != tp:
+                raise RuntimeError(f"tp_size={tp} needs a torch.distributed group of {tp} ranks, one per GPU")
+            self.engine = QwenVLEngineTP(model, TPComm(device=self.device), prec)
+        else:
+            self.engine = QwenVLEngine(model, self.device, prec)
         del model
         torch.cuda.empty_cache()
         g = torch.Generator().manual_seed(seed + 1)
@@ -74,7 +86,7 @@ class Qwen25VLExecutor(ModelExecutor):
 
     def approx_forward(self, params, context, config):
         self.engine.approx(context["session"])
-        return {"precision": "bf16"}
+        return {"precision": "fp8" if self.engine.fp8 else "bf16"}
 
     def correct_forward(self, params, context, config):
         opts = normalize_appcorr_kwargs(config.appcorr_kwargs, config.transmission_kwargs)

@@ -774,7 +774,8 @@ void gemm_dispatch(int epi, int bn, const at::Tensor& A, const at::Tensor& B, in
       if (bn == 512) launch_gemm_2sm<6, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
       else if (bn == 256) launch_gemm<256, 4, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
       else if (bn == 128) launch_gemm<128, 6, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
-      else TORCH_CHECK(false, "qkv epilogue uses BN=128 or 256");
+      else if (bn == 64) launch_gemm<64, 8, EPI_QKV>(A, B, M, N, K, ep, err, max_ctas, st);
+      else TORCH_CHECK(false, "qkv epilogue uses BN=64, 128 or 256");
       break;
     default:
       TORCH_CHECK(false, "unknown epilogue ", epi);

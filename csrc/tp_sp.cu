@@ -25,7 +25,9 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <algorithm>
 #include <cfloat>
+#include <cstdlib>
 #include <cuda_fp8.h>
 
 #include "sm100_common.cuh"
@@ -116,13 +118,9 @@ __device__ __forceinline__ float sp_block_reduce(float v, float* red) {
 }
 
 // NV: 16-byte vectors per thread (D <= 1024 * NV); W: ranks (partial sources). The finished row is
-// held as packed bf16 (it is bf16-rounded anyway) to keep registers low. Rows
-// [row0, row0 + gridDim.x) are visited.
+// held as packed bf16 (it is bf16-rounded anyway) to keep registers low.
 template <int NV, int W>
-__global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0) {
-  __shared__ float red[kSpThreads / 32];
-  const int i = row0 + blockIdx.x;
-  if (i >= a.M) return;
+__device__ __forceinline__ void sp_row_one(const SpArgs& a, int i, float* red) {
   const int tok = a.tok ? a.tok[i] : i;
   if (tok < 0 || tok / a.rows_per_rank != a.rank) return;  // another rank owns this row
   const int nvec = a.D >> 3;
@@ -266,6 +264,14 @@ __global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0) 
   }
 }
 
+// Persistent over rows: a bounded grid (about two CTAs per SM) walks the rows, so the kernel leaves
+// SM room for the GEMM of the other micro-batch instead of flooding every SM with row CTAs.
+template <int NV, int W>
+__global__ void __launch_bounds__(kSpThreads) sp_row_kernel(SpArgs a, int row0, int row_end) {
+  __shared__ float red[kSpThreads / 32];
+  for (int i = row0 + blockIdx.x; i < row_end; i += gridDim.x) sp_row_one<NV, W>(a, i, red);
+}
+
 template <typename T = void>
 static T* sp_opt(const c10::optional<at::Tensor>& t) {
   return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
@@ -341,12 +347,18 @@ void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, 
   }
   const int nv = (static_cast<int>(D) / 8 + kSpThreads - 1) / kSpThreads;
   auto st = at::cuda::getCurrentCUDAStream();
+  const int row_end = row0 + nrows;
+  static const int ctas_per_sm = [] {
+    const char* e = std::getenv("APPCORR_SP_CTAS_PER_SM");
+    return e ? std::max(1, std::atoi(e)) : 2;
+  }();
+  nrows = std::min(nrows, ctas_per_sm * num_sms());
 #define APPCORR_SP_LAUNCH_W(NV)                                                             \
   switch (world) {                                                                          \
-    case 1: sp_row_kernel<NV, 1><<<nrows, kSpThreads, 0, st>>>(a, row0); break;             \
-    case 2: sp_row_kernel<NV, 2><<<nrows, kSpThreads, 0, st>>>(a, row0); break;             \
-    case 4: sp_row_kernel<NV, 4><<<nrows, kSpThreads, 0, st>>>(a, row0); break;             \
-    case 8: sp_row_kernel<NV, 8><<<nrows, kSpThreads, 0, st>>>(a, row0); break;             \
+    case 1: sp_row_kernel<NV, 1><<<nrows, kSpThreads, 0, st>>>(a, row0, row_end); break;             \
+    case 2: sp_row_kernel<NV, 2><<<nrows, kSpThreads, 0, st>>>(a, row0, row_end); break;             \
+    case 4: sp_row_kernel<NV, 4><<<nrows, kSpThreads, 0, st>>>(a, row0, row_end); break;             \
+    case 8: sp_row_kernel<NV, 8><<<nrows, kSpThreads, 0, st>>>(a, row0, row_end); break;             \
     default: TORCH_CHECK(false, "sp_row: world must be 1, 2, 4 or 8");                      \
   }
   if (nv <= 1) { APPCORR_SP_LAUNCH_W(1) }

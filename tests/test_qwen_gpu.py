@@ -142,3 +142,28 @@ def test_attention_gqa_causal_paged():
     qq = q2.float().view(-1, H, Dh).transpose(0, 1)
     ref2 = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=True).transpose(0, 1).reshape(N, -1)
     assert (o2.float() - ref2).abs().max().item() < 2e-2 * ref2.abs().max().item() + 2e-2
+
+
+def test_llm_fp8_tracks_fp32():
+    """e4m3 LLM GEMMs: approximate and full-correction passes stay close to the fp32 model."""
+    from appcorr_b200.models.qwen25vl import PRESETS, Qwen25VL, mrope_positions, mrope_tables
+    from appcorr_b200.models.qwen_engine import QwenVLEngine
+
+    cfg = PRESETS["tiny"]
+    m = Qwen25VL(cfg).init_weights(4).to(DEV).eval()
+    eng = QwenVLEngine(m, DEV, "fp8")
+    nb, na = 8, 24
+    ids = torch.randint(0, cfg.vocab, (nb + na,), generator=torch.Generator().manual_seed(4)).to(DEV)
+    img = torch.randint(0, 256, (1, 224, 224, 3), dtype=torch.uint8, device=DEV)
+    sess = eng.new_session(224, 224, nb, na)
+    eng.vision(sess, img)
+    eng.embed_text(sess, ids)
+    x = eng.approx(sess).clone()
+    sin, cos = (v.to(DEV) for v in mrope_tables(cfg, mrope_positions(nb, 8, 8, na)))
+    with torch.no_grad():
+        xr = _oracle_x_in(m, img, ids, nb)
+        for i, ly in enumerate(m.layers):
+            xr = ly.approx(xr, sin, cos, {}, f"l{i}")
+    assert _rel(x, xr) < 8e-2
+    xc = eng.correct(sess, 1.0)
+    assert _rel(xc, xr) < 8e-2

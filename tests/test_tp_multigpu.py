@@ -87,3 +87,65 @@ def test_tp2_matches_single_gpu(precision, rs_mode, microbatch):
     tol = (2e-2, 3e-2, 1e-2) if precision == "bf16" else (1.2e-1, 1.2e-1, 1e-1)
     for rank, a, c, ps in res:
         assert a < tol[0] and c < tol[1] and ps < tol[2], (rank, a, c, ps)
+
+
+def _qwen_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from appcorr_b200.models.qwen25vl import PRESETS, Qwen25VL
+    from appcorr_b200.models.qwen_engine import QwenVLEngine
+    from appcorr_b200.parallel.comm import TPComm
+    from appcorr_b200.parallel.qwen_tp import QwenVLEngineTP
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    dev = torch.device("cuda", rank)
+    cfg = PRESETS["tiny"]
+    m = Qwen25VL(cfg).init_weights(5).to(dev).eval()
+    ref = QwenVLEngine(m, dev)
+    comm = TPComm(device=dev)
+    tp = QwenVLEngineTP(m, comm)
+    nb, na = 8, 24
+    ids = torch.randint(0, cfg.vocab, (nb + na,), generator=torch.Generator().manual_seed(5)).to(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    img0 = torch.randint(0, 256, (1, 224, 224, 3), dtype=torch.uint8, device=dev, generator=g)
+    img1 = img0.clone()
+    img1[:, :112] = torch.randint(0, 256, (1, 112, 224, 3), dtype=torch.uint8, device=dev, generator=g)
+    outs = []
+    for eng in (ref, tp):
+        s = eng.new_session(224, 224, nb, na)
+        eng.vision(s, img0)
+        eng.embed_text(s, ids)
+        eng.approx(s)
+        eng.first_token(s)
+        la = s.tensors["logits"][0, : cfg.vocab].clone()
+        eng.vision(s, img1)
+        eng.correct(s, 0.25)
+        eng.first_token(s)
+        lc = s.tensors["logits"][0, : cfg.vocab].clone()
+        torch.cuda.synchronize()
+        outs.append((la, lc))
+    comm.check()
+    rel = lambda a, b: ((a.float() - b.float()).norm() / b.float().norm()).item()  # noqa: E731
+    q.put((rank, rel(outs[1][0], outs[0][0]), rel(outs[1][1], outs[0][1])))
+    dist.barrier()
+    comm.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_qwen_tp2_matches_single_gpu():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_qwen_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, a, c in res:
+        assert a < 3e-2 and c < 3e-2, (rank, a, c)
