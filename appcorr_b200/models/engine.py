@@ -31,7 +31,7 @@ from ..common.protocol import LAYERMEAN_SERVER_PSCORES
 from ..ops import kernels as K
 from .dinov3.layers import linear_bias
 from .dinov3.vit import DinoVisionTransformer, ViTConfig
-from .weights import pack_swiglu
+from .weights import pack_swiglu, repack_swiglu
 
 BF16 = torch.bfloat16
 
@@ -54,6 +54,9 @@ class LayerW:
     ls2: torch.Tensor
     # e4m3 copies (w8 [N, K], per-output-channel fp32 scale [N]) for the fp8 GEMM path
     q8: Optional[Dict[str, Tuple[torch.Tensor, torch.Tensor]]] = None
+    # NVFP4 copies (w4 [N, K/2], (channel scale [N], block scales)) of qkv / fc1 / fc2, and the
+    # fc1 bias re-packed for 64-row SwiGLU blocks ("fc1_b")
+    q4: Optional[Dict[str, object]] = None
 
 
 @dataclass
@@ -210,13 +213,31 @@ class Session:
     extra: Dict[str, torch.Tensor] = field(default_factory=dict)
 
 
-PRECISIONS = ("bf16", "fp8")
+PRECISIONS = ("bf16", "fp8", "nvfp4")
 _Q8_NAMES = ("qkv", "proj", "fc1", "fc2")
+# nvfp4 precision: these GEMMs take NVFP4 operands; attn.proj stays e4m3 (the reference's
+# FastFP4 path keeps proj in FP8 by default, offload/server/model/fp4_fast_linear.py)
+_Q4_NAMES = ("qkv", "fc1", "fc2")
 
 
 def quantize_layer_e4m3(lw: LayerW) -> None:
     """Attach per-output-channel e4m3 copies of the four GEMM weights of a layer."""
     lw.q8 = {n: K.quantize_weight_e4m3(getattr(lw, n + "_w")) for n in _Q8_NAMES}
+
+
+def quantize_layer_nvfp4(lw: LayerW, swiglu: bool) -> None:
+    """Attach NVFP4 copies of qkv / fc1 / fc2 (fc1 re-packed to 64-row SwiGLU blocks)."""
+    q4: Dict[str, object] = {}
+    for n in _Q4_NAMES:
+        w = getattr(lw, n + "_w")
+        if w.shape[1] % 256:
+            raise ValueError(f"nvfp4 precision needs GEMM K % 256 == 0 ({n}: K = {w.shape[1]})")
+        if n == "fc1" and swiglu:
+            w, b = repack_swiglu(w, lw.fc1_b)
+            q4["fc1_b"] = b
+        q4[n] = K.quantize_weight_nvfp4(w)
+    q4.setdefault("fc1_b", lw.fc1_b)
+    lw.q4 = q4
 
 
 class ViTEngine:
@@ -240,11 +261,14 @@ class ViTEngine:
             if v not in PRECISIONS:
                 raise ValueError(f"engine precision must be one of {PRECISIONS}, got {v!r}")
         self.precision = dict(precision)
-        if "fp8" in self.precision.values():
-            for lw in self.w.layers:
-                if lw.q8 is None:
-                    quantize_layer_e4m3(lw)
-        self._fp8 = False  # precision of the pass being run
+        low = set(self.precision.values()) - {"bf16"}
+        for lw in self.w.layers:
+            if low and lw.q8 is None:
+                quantize_layer_e4m3(lw)
+            if "nvfp4" in low and lw.q4 is None:
+                quantize_layer_nvfp4(lw, self.cfg.is_swiglu)
+        self._fp8 = False  # precision of the pass being run: e4m3 or NVFP4 operands
+        self._fp4 = False  # NVFP4 for the _Q4_NAMES GEMMs
         self.taps: Tuple[int, ...] = ()  # layers whose output is kept for dense heads
 
     @classmethod
@@ -262,34 +286,55 @@ class ViTEngine:
         if not self._fp8:
             K.layernorm(x, w, b, self.cfg.norm_eps, out, rows=rows, copy_out=copy_out)
             return out, None
-        n = out.shape[0]
-        q8, s = sess.extra["a8"][:n, : out.shape[1]], sess.extra["a8_scale"][:n]
+        n, k = out.shape
+        e = sess.extra
+        if self._fp4:  # every LayerNorm feeds an NVFP4 GEMM (qkv or fc1)
+            q4, s, sf = e["a4"][:n, : k // 2], e["a4_scale"][:n], e["a4_sf"]
+            K.layernorm(x, w, b, self.cfg.norm_eps, q4, rows=rows, copy_out=copy_out, scale8=s, sf=sf)
+            return q4, (s, sf)
+        q8, s = e["a8"][:n, :k], e["a8_scale"][:n]
         K.layernorm(x, w, b, self.cfg.norm_eps, q8, rows=rows, copy_out=copy_out, scale8=s)
         return q8, s
 
-    def _act(self, sess: Session, t: torch.Tensor):
-        """bf16 activation feeding a GEMM: returns (operand, row scale or None)."""
+    def _act(self, sess: Session, t: torch.Tensor, name: str = "fc2"):
+        """bf16 activation feeding GEMM `name`: returns (operand, row scale(s) or None)."""
         if not self._fp8:
             return t, None
         n, k = t.shape
-        q8, s = sess.extra["a8"][:n, :k], sess.extra["a8_scale"][:n]
+        e = sess.extra
+        if self._fp4 and name in _Q4_NAMES:
+            q4, s, sf = e["a4"][:n, : k // 2], e["a4_scale"][:n], e["a4_sf"]
+            K.quant_rows_nvfp4(t, q4, sf, s)
+            return q4, (s, sf)
+        q8, s = e["a8"][:n, :k], e["a8_scale"][:n]
         K.quant_rows_e4m3(t, q8, s)
         return q8, s
 
     def _w(self, lw: LayerW, name: str):
+        if self._fp4 and name in _Q4_NAMES:
+            return lw.q4[name]
         if self._fp8:
             return lw.q8[name]
         return getattr(lw, name + "_w"), None
 
+    def _fc1_bias(self, lw: LayerW):
+        return lw.q4["fc1_b"] if self._fp4 else lw.fc1_b
+
     def _ensure_fp8_scratch(self, sess: Session) -> None:
-        if "a8" not in sess.extra:
-            M = sess.x.shape[0]
-            width = max(self.cfg.embed_dim, sess.h.shape[1])
-            sess.extra["a8"] = torch.empty(M, width, device=self.device, dtype=torch.float8_e4m3fn)
-            sess.extra["a8_scale"] = torch.empty(M, device=self.device, dtype=torch.float32)
+        e = sess.extra
+        M = sess.x.shape[0]
+        width = max(self.cfg.embed_dim, sess.h.shape[1])
+        if "a8" not in e:
+            e["a8"] = torch.empty(M, width, device=self.device, dtype=torch.float8_e4m3fn)
+            e["a8_scale"] = torch.empty(M, device=self.device, dtype=torch.float32)
+        if self._fp4 and "a4" not in e:
+            e["a4"] = torch.empty(M, width // 2, device=self.device, dtype=torch.uint8)
+            e["a4_scale"] = torch.empty(M, device=self.device, dtype=torch.float32)
+            e["a4_sf"] = torch.zeros(K.nvfp4_sf_bytes(M, width), device=self.device, dtype=torch.uint8)
 
     def _set_pass(self, sess: Session, which: str) -> None:
-        self._fp8 = self.precision[which] == "fp8"
+        self._fp4 = self.precision[which] == "nvfp4"
+        self._fp8 = self.precision[which] in ("fp8", "nvfp4")
         if self._fp8:
             self._ensure_fp8_scratch(sess)
 
@@ -377,7 +422,7 @@ class ViTEngine:
     def _mlp(self, lw: LayerW, xin: torch.Tensor, hbuf: torch.Tensor, a_scale=None) -> torch.Tensor:
         w, ws = self._w(lw, "fc1")
         epi = K.EPI_SWIGLU if self.cfg.is_swiglu else K.EPI_GELU
-        K.gemm(xin, w, hbuf, epi=epi, bias=lw.fc1_b, a_scale=a_scale, b_scale=ws)
+        K.gemm(xin, w, hbuf, epi=epi, bias=self._fc1_bias(lw), a_scale=a_scale, b_scale=ws)
         return hbuf
 
     def approx_layer(self, sess: Session, l: int, x: torch.Tensor, x_out: torch.Tensor, server_pscore: str) -> None:
@@ -394,7 +439,7 @@ class ViTEngine:
             self._attention_with_score(sess, l, H, server_pscore not in ("none", "disabled") and c.n_prefix > 0,
                                        sess.pscore[l])
         # x_out = x + ls1 * proj(o); bos[l] = ls1 * proj(o)
-        a, sa = self._act(sess, sess.o)
+        a, sa = self._act(sess, sess.o, "proj")
         w, ws = self._w(lw, "proj")
         K.gemm(a, w, x_out, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x,
                aux=sess.bos[l], aux_mode=K.AUX_SET, a_scale=sa, b_scale=ws)
@@ -490,7 +535,7 @@ class ViTEngine:
             K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh, causal=True, q_pos=hi, q_lo=lo)
         else:
             K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh)
-        a, sa = self._act(sess, o)
+        a, sa = self._act(sess, o, "proj")
         w, ws = self._w(lw, "proj")
         K.gemm(a, w, x_att, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x_act, a_scale=sa, b_scale=ws)
         a, sa = self._norm(sess, x_att, lw.norm2_w, lw.norm2_b, xn)

@@ -16,23 +16,35 @@ import torch
 SWIGLU_BLOCK = 128
 
 
-def pack_swiglu(w1: torch.Tensor, w2: torch.Tensor, b1: Optional[torch.Tensor], b2: Optional[torch.Tensor]
-                ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+def pack_swiglu(w1: torch.Tensor, w2: torch.Tensor, b1: Optional[torch.Tensor], b2: Optional[torch.Tensor],
+                block: int = SWIGLU_BLOCK) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Interleave w1 / w2 rows in `block`-row blocks: a GEMM tile of 2 * block columns then holds
+    matching gate and up columns (128 for the 256-wide bf16 / e4m3 tiles, 64 for NVFP4's 128)."""
     hd, k = w1.shape
-    assert w2.shape == (hd, k) and hd % SWIGLU_BLOCK == 0, "SwiGLU hidden size must be a multiple of 128"
-    nb = hd // SWIGLU_BLOCK
-    w = torch.stack([w1.view(nb, SWIGLU_BLOCK, k), w2.view(nb, SWIGLU_BLOCK, k)], dim=1).reshape(2 * hd, k)
+    assert w2.shape == (hd, k) and hd % block == 0, f"SwiGLU hidden size must be a multiple of {block}"
+    nb = hd // block
+    w = torch.stack([w1.view(nb, block, k), w2.view(nb, block, k)], dim=1).reshape(2 * hd, k)
     b = None
     if b1 is not None:
-        b = torch.stack([b1.view(nb, SWIGLU_BLOCK), b2.view(nb, SWIGLU_BLOCK)], dim=1).reshape(2 * hd)
+        b = torch.stack([b1.view(nb, block), b2.view(nb, block)], dim=1).reshape(2 * hd)
     return w.contiguous(), (b.contiguous() if b is not None else None)
 
 
-def unpack_swiglu(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    two_hd, k = w.shape
-    nb = two_hd // (2 * SWIGLU_BLOCK)
-    v = w.view(nb, 2, SWIGLU_BLOCK, k)
-    return v[:, 0].reshape(-1, k), v[:, 1].reshape(-1, k)
+def unpack_swiglu(w: torch.Tensor, block: int = SWIGLU_BLOCK) -> Tuple[torch.Tensor, torch.Tensor]:
+    two_hd = w.shape[0]
+    rest = tuple(w.shape[1:])
+    nb = two_hd // (2 * block)
+    v = w.reshape((nb, 2, block) + rest)
+    return v[:, 0].reshape((-1,) + rest), v[:, 1].reshape((-1,) + rest)
+
+
+def repack_swiglu(w: torch.Tensor, b: Optional[torch.Tensor], block_from: int = SWIGLU_BLOCK,
+                  block_to: int = 64) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    w1, w2 = unpack_swiglu(w, block_from)
+    b1 = b2 = None
+    if b is not None:
+        b1, b2 = unpack_swiglu(b, block_from)
+    return pack_swiglu(w1, w2, b1, b2, block_to)
 
 
 def fold_batchnorm_conv1x1(conv_w: torch.Tensor, conv_b: Optional[torch.Tensor], bn_w: torch.Tensor,

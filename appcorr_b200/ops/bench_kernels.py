@@ -44,6 +44,8 @@ def main(argv=None) -> None:
     ap.add_argument("--bn", type=int, default=None)
     ap.add_argument("--epi", default="bf16", choices=["bf16", "f32", "gelu"])
     ap.add_argument("--fp8", action="store_true", help="e4m3 operands (kind::f8f6f4); --ref times torch._scaled_mm")
+    ap.add_argument("--fp4", action="store_true",
+                    help="NVFP4 operands (kind::mxf4nvf4 block16); --ref times torch._scaled_mm on the same bytes")
     ap.add_argument("--B", type=int, default=8)
     ap.add_argument("--H", type=int, default=32)
     ap.add_argument("--Dh", type=int, default=128)
@@ -63,7 +65,19 @@ def main(argv=None) -> None:
         epi = {"bf16": K.EPI_BF16, "f32": K.EPI_F32, "gelu": K.EPI_GELU}[a.epi]
         out = torch.empty(a.M, a.N, device=dev, dtype=torch.float32 if a.epi == "f32" else torch.bfloat16)
         flops = 2.0 * a.M * a.N * a.K
-        if a.fp8:
+        if a.fp4:
+            x4 = torch.empty(a.M, a.K // 2, device=dev, dtype=torch.uint8)
+            xsf = torch.zeros(K.nvfp4_sf_bytes(a.M, a.K), device=dev, dtype=torch.uint8)
+            xs = torch.empty(a.M, device=dev)
+            K.quant_rows_nvfp4(x, x4, xsf, xs)
+            w4, (ws, wsf) = K.quantize_weight_nvfp4(w)
+            fn = lambda: K.gemm(x4, w4, out, epi=epi, a_scale=(xs, xsf), b_scale=(ws, wsf))  # noqa: E731
+            ref = None
+            if a.ref:
+                fa, fb = x4.view(torch.float4_e2m1fn_x2), w4.view(torch.float4_e2m1fn_x2)
+                sa, sb = xsf.view(torch.float8_e4m3fn), wsf.view(torch.float8_e4m3fn)
+                ref = lambda: torch._scaled_mm(fa, fb.T, sa, sb, out_dtype=torch.bfloat16)  # noqa: E731
+        elif a.fp8:
             x8 = torch.empty(a.M, a.K, device=dev, dtype=torch.float8_e4m3fn)
             sx = torch.empty(a.M, device=dev)
             K.quant_rows_e4m3(x, x8, sx)
@@ -74,7 +88,7 @@ def main(argv=None) -> None:
         else:
             fn = lambda: K.gemm(x, w, out, epi=epi, bn=a.bn)  # noqa: E731
             ref = (lambda: torch.matmul(x, w.T)) if a.ref else None  # noqa: E731
-        res.update(M=a.M, N=a.N, K=a.K, bn=a.bn, fp8=a.fp8)
+        res.update(M=a.M, N=a.N, K=a.K, bn=a.bn, fp8=a.fp8, fp4=a.fp4)
     elif a.op == "attention":
         q = torch.randn(a.B * a.Tq, a.H * a.Dh, device=dev).to(torch.bfloat16)
         k = torch.randn(a.B * a.Tk, a.H * a.Dh, device=dev).to(torch.bfloat16)
@@ -117,7 +131,7 @@ def main(argv=None) -> None:
         ag = [torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn) for _ in range(W)]
         ags = [torch.empty(M, device=dev) for _ in range(W)]
         fn = lambda: lib().sp_row(M, None, R, 0, W, D, [p.data_ptr() for p in parts], [0] * W, vec, vec, x, True,  # noqa: E731
-                                  None, x, True, aux, K.AUX_ADD, None, None, vec, vec, 1e-6, False, True,
+                                  None, x, True, aux, K.AUX_ADD, None, None, vec, vec, 1e-6, False, 1,
                                   [t.data_ptr() for t in ag], D, [t.data_ptr() for t in ags])
         flops = 0.0
         rows = R

@@ -41,13 +41,21 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
          aux_rows: Optional[torch.Tensor] = None, aux_mode: int = AUX_NONE,
          resid2: Optional[torch.Tensor] = None, bn: Optional[int] = None,
          max_ctas: int = 0, a_scale: Optional[torch.Tensor] = None,
-         b_scale: Optional[torch.Tensor] = None, rs: Optional[tuple] = None) -> torch.Tensor:
-    """out = epilogue(a @ w^T). `a` [M, K], `w` [N, K] (nn.Linear layout), both bf16 or both
-    e4m3; e4m3 operands carry fp32 scales a_scale [M] (per row) and b_scale [N] (per output
-    channel) that the epilogue applies to the fp32 accumulator before bias / activation.
+         b_scale=None, rs: Optional[tuple] = None) -> torch.Tensor:
+    """out = epilogue(a @ w^T). `a` [M, K], `w` [N, K] (nn.Linear layout), both bf16, both e4m3
+    or both NVFP4. e4m3 operands carry fp32 scales a_scale [M] (per row) and b_scale [N] (per
+    output channel) that the epilogue applies to the fp32 accumulator before bias / activation.
+    NVFP4 operands are uint8 [rows, K/2] (packed e2m1) and pass (row scale [rows] fp32, block
+    scales uint8) pairs as a_scale / b_scale (see quant_rows_nvfp4); their tile width is 128 and
+    a SwiGLU weight must be packed in 64-row blocks.
     rs = (slot_ptrs, rows_per_rank, rank, slot_rows, ld): reduce-scatter epilogue; row m goes to
     rank (out_rows[m] or m) // rows_per_rank, slot row rank * slot_rows + m (`out` unused)."""
     fp8 = a.dtype == torch.float8_e4m3fn
+    a_sf = b_sf = None
+    if isinstance(a_scale, tuple):
+        a_scale, a_sf = a_scale
+        b_scale, b_sf = b_scale
+        bn = 128
     if bn is None:
         bn = 256 if epi == EPI_SWIGLU else _pick_bn(w.shape[0], a.shape[0])
         if fp8 and bn == 64:
@@ -55,7 +63,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
     _count()
     lib().gemm(a, w, epi, bn, err_word(a.device), out=out, out_rows=out_rows, bias=bias, gamma=gamma,
                resid=resid, resid_rows=resid_rows, aux=aux, aux_rows=aux_rows, aux_mode=aux_mode,
-               resid2=resid2, max_ctas=max_ctas, a_scale=a_scale, b_scale=b_scale,
+               resid2=resid2, max_ctas=max_ctas, a_scale=a_scale, b_scale=b_scale, a_sf=a_sf, b_sf=b_sf,
                **({} if rs is None else dict(rs_out=list(rs[0]), rs_rows_per_rank=int(rs[1]), rs_rank=int(rs[2]),
                                              rs_slot_rows=int(rs[3]), rs_ld=int(rs[4]))))
     return out
@@ -65,8 +73,7 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
              k_out: torch.Tensor, v_out: torch.Tensor, *, head_dim: int, seq_len: int = 0,
              tok_idx: Optional[torch.Tensor] = None, kv_rows: Optional[torch.Tensor] = None,
              rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, n_prefix: int = 0,
-             bn: Optional[int] = None, a_scale: Optional[torch.Tensor] = None,
-             b_scale: Optional[torch.Tensor] = None, kv_dim: int = 0) -> None:
+             bn: Optional[int] = None, a_scale=None, b_scale=None, kv_dim: int = 0) -> None:
     """qkv projection with RoPE on q/k (tokens >= n_prefix) split into three BTHD buffers.
 
     q row m is written at q_out[m]; k/v rows at kv_rows[m] (or m). `rope` = (sin, cos) fp32
@@ -75,23 +82,31 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
     [q (N - 2 kv_dim) | k (kv_dim) | v (kv_dim)].
     """
     dim = w.shape[0] - 2 * kv_dim if kv_dim else w.shape[0] // 3
+    a_sf = b_sf = None
+    if isinstance(a_scale, tuple):  # NVFP4 operands: (row scale, block scales); 128-wide tiles
+        a_scale, a_sf = a_scale
+        b_scale, b_sf = b_scale
+        bn = 128
     if bn is None:  # widest tile that divides the q and the k / v widths (tiles never straddle)
         bn = next((t for t in (256, 128, 64) if dim % t == 0 and (kv_dim or dim) % t == 0), 128)
     sin, cos = rope if rope is not None else (None, None)
     _count()
     lib().gemm(a, w, EPI_QKV, bn, err_word(a.device), bias=bias, q_out=q_out, k_out=k_out, v_out=v_out,
                kv_rows=kv_rows, tok_idx=tok_idx, seq_len=seq_len, rope_sin=sin, rope_cos=cos,
-               n_prefix=n_prefix, head_dim=head_dim, a_scale=a_scale, b_scale=b_scale, kv_dim=kv_dim)
+               n_prefix=n_prefix, head_dim=head_dim, a_scale=a_scale, b_scale=b_scale, kv_dim=kv_dim,
+               a_sf=a_sf, b_sf=b_sf)
 
 
 def layernorm(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], eps: float, out: torch.Tensor,
               rows: Optional[torch.Tensor] = None, copy_out: Optional[torch.Tensor] = None,
-              scale8: Optional[torch.Tensor] = None, rms: bool = False) -> torch.Tensor:
+              scale8: Optional[torch.Tensor] = None, rms: bool = False,
+              sf: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out[i] = LN(x[rows[i]]) (rows=None: every row). copy_out[i] receives the raw gathered row.
-    An e4m3 `out` receives the bf16-rounded LN row divided by scale8[i] = amax_i / 448.
+    An e4m3 `out` receives the bf16-rounded LN row divided by scale8[i] = amax_i / 448; a uint8
+    `out` [n, D/2] receives it as NVFP4 (block scales into `sf`, row scale scale8[i]).
     rms=True: RMSNorm x * rsqrt(mean(x^2) + eps) * w (b must be None)."""
     _count()
-    lib().layernorm(x, rows, w, b, float(eps), out, copy_out, scale8, rms)
+    lib().layernorm(x, rows, w, b, float(eps), out, copy_out, scale8, rms, sf)
     return out
 
 
@@ -113,6 +128,86 @@ def quantize_weight_e4m3(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     sc = (wf.abs().amax(dim=1).clamp_min(1e-12) / 448.0).contiguous()
     w8 = (wf / sc[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).contiguous()
     return w8, sc
+
+
+# ---------------------------------------------------------------------------------------- NVFP4
+# Format: e2m1 values packed two per byte (element 2i in the low nibble), one ue4m3 scale per 16
+# elements of a row, and an fp32 row scale = row amax / (6 * 448) so every block scale fits ue4m3:
+# x ~= e2m1 * block_scale * row_scale. Block scales are stored in 128-row x 64-element tiles of
+# 512 bytes (tile (row // 128, k // 64) at ((row // 128) * (K // 64) + k // 64) * 512; inside a
+# tile row r, 16-element block j sits at (r % 32) * 16 + ((r % 128) // 32) * 4 + j % 4) -- the
+# blocked scale layout of CUTLASS / torch._scaled_mm, which is also the tcgen05.cp source pattern.
+# Reference: the Triton quantiser appcorr/models/dinov3/layers/triton_kernels/nvfp4_fused.py:54-145
+# (per-tensor second-level scale there; per-row here, which the GEMM epilogue folds per row).
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+# round-to-nearest-even boundaries between consecutive magnitudes: (threshold, upper code even)
+_E2M1_BOUNDS = ((0.25, False), (0.75, True), (1.25, False), (1.75, True), (2.5, False), (3.5, True), (5.0, False))
+
+
+def nvfp4_sf_bytes(rows: int, k: int) -> int:
+    """Bytes of the blocked scale tensor of a [rows, k] NVFP4 matrix."""
+    return ((rows + 127) // 128) * (k // 64) * 512
+
+
+def nvfp4_sf_index(rows: int, k: int, device=None) -> torch.Tensor:
+    """int64 [rows, k // 16]: byte offset of each block scale in the blocked layout."""
+    r = torch.arange(rows, device=device)[:, None]
+    j = torch.arange(k // 16, device=device)[None, :]
+    return (((r // 128) * (k // 64) + j // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + j % 4)
+
+
+def _e2m1_codes(y: torch.Tensor) -> torch.Tensor:
+    a = y.abs()
+    code = torch.zeros(y.shape, dtype=torch.uint8, device=y.device)
+    for t, incl in _E2M1_BOUNDS:
+        code += (a >= t if incl else a > t).to(torch.uint8)
+    return code | (torch.signbit(y).to(torch.uint8) << 3)
+
+
+def nvfp4_quantize_ref(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """PyTorch statement of the NVFP4 quantiser (same fp32 operation order as the CUDA kernels):
+    x [M, K] -> (packed uint8 [M, K/2], block scales uint8 [nvfp4_sf_bytes], row scale fp32 [M])."""
+    xf = x.float()
+    M, Kd = xf.shape
+    assert Kd % 64 == 0, "NVFP4 rows need K % 64 == 0"
+    rs = xf.abs().amax(1).clamp_min(1e-12) / (6.0 * 448.0)
+    inv_rs = 1.0 / rs
+    blk = xf.view(M, Kd // 16, 16)
+    bm = blk.abs().amax(2)
+    s = (bm * torch.tensor(1.0 / 6.0, dtype=torch.float32) * inv_rs[:, None]).clamp(max=448.0)
+    s8 = s.to(torch.float8_e4m3fn)
+    sd = s8.float()
+    mul = torch.where(sd > 0, 1.0 / (sd * rs[:, None]), torch.zeros_like(sd))
+    codes = _e2m1_codes((blk * mul[..., None]).view(M, Kd))
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()
+    sf = torch.zeros(nvfp4_sf_bytes(M, Kd), dtype=torch.uint8, device=x.device)
+    sf[nvfp4_sf_index(M, Kd, x.device).reshape(-1)] = s8.view(torch.uint8).reshape(-1)
+    return packed, sf, rs.contiguous()
+
+
+def nvfp4_dequantize(q: torch.Tensor, sf: torch.Tensor, rs: torch.Tensor) -> torch.Tensor:
+    """fp32 [M, K] values of an NVFP4 matrix (oracle for tests)."""
+    M, half = q.shape
+    Kd = 2 * half
+    table = torch.tensor(E2M1_VALUES + tuple(-v for v in E2M1_VALUES), dtype=torch.float32, device=q.device)
+    codes = torch.stack([q & 0xF, q >> 4], dim=2).view(M, Kd).long()
+    vals = table[codes]
+    s8 = sf[nvfp4_sf_index(M, Kd, q.device)].view(torch.float8_e4m3fn).float()
+    return (vals.view(M, Kd // 16, 16) * s8[..., None]).view(M, Kd) * rs[:M, None].float()
+
+
+def quant_rows_nvfp4(x: torch.Tensor, out: torch.Tensor, sf: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """NVFP4 rows of bf16 x [M, K]: out uint8 [M, K/2], sf (blocked block scales), scale fp32 [M]."""
+    _count()
+    lib().quant_rows_nvfp4(x, out, sf, scale)
+    return out
+
+
+def quantize_weight_nvfp4(w: torch.Tensor) -> Tuple[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
+    """One-time NVFP4 weight preparation: (w4 [N, K/2] uint8, (channel scale [N] fp32, block scales))
+    -- the (operand, scales) pair the GEMM wrappers take."""
+    q, sf, rs = nvfp4_quantize_ref(w)
+    return q, (rs, sf)
 
 
 def add_(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:

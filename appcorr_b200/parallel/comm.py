@@ -105,17 +105,19 @@ class TPComm:
                bias=None, gamma=None, resid=None, resid_tok: bool = True, resid2=None,
                out=None, out_tok: bool = True, aux=None, aux_mode: int = 0, x=None, copy_out=None,
                ln_w=None, ln_b=None, eps: float = 1e-6, rms: bool = False, ag: Optional[SymTensor] = None,
-               ag_scale: Optional[SymTensor] = None) -> None:
+               ag_scale: Optional[SymTensor] = None, ag_sf: Optional[SymTensor] = None) -> None:
         """Owner-side row kernel of the sequence-parallel layout (csrc/tp_sp.cu): finish the
         reduce-scatter of the partial rows `src` = (base pointers, row offsets), one per rank (or
         load x[tok]) on the rows this rank owns, then LayerNorm and all-gather the normalised
-        rows into every rank's `ag` (e4m3 + scales when ag_scale)."""
+        rows into every rank's `ag` (e4m3 + row scales when ag_scale; NVFP4 -- packed e2m1 rows,
+        row scales and blocked block scales -- when ag_sf is given too)."""
         _count()
-        fp8 = ag_scale is not None
+        mode = 0 if ag_scale is None else (2 if ag_sf is not None else 1)
         lib().sp_row(M, tok, rows_per_rank, self.rank, self.world, D, list(src[0]) if src else [],
                      list(src[1]) if src else [], bias, gamma, resid, resid_tok, resid2, out, out_tok, aux, aux_mode, x, copy_out,
-                     ln_w, ln_b, float(eps), rms, fp8, ag.ptrs if ag is not None else [],
-                     (ag.local.stride(0) if ag is not None else 0), ag_scale.ptrs if fp8 else [])
+                     ln_w, ln_b, float(eps), rms, mode, ag.ptrs if ag is not None else [],
+                     (ag.local.stride(0) if ag is not None else 0), ag_scale.ptrs if mode else [],
+                     ag_sf.ptrs if mode == 2 else [])
 
     def mean_f32(self, src: SymTensor, dst: torch.Tensor) -> None:
         _count()

@@ -155,8 +155,13 @@ class ViTEngineTP(ViTEngine):
         # symmetric buffers that peers store into
         xg = comm.empty((M, D), BF16)                       # gathered LN rows (bf16, or e4m3 in its first M*D bytes)
         xg8 = SymTensor(xg.local.view(torch.uint8).view(-1)[: M * D].view(M, D).view(torch.float8_e4m3fn), xg.ptrs)
+        # NVFP4 gather: packed e2m1 rows in the first M*D/2 bytes, blocked block scales alongside
+        xg4 = SymTensor(xg.local.view(torch.uint8).view(-1)[: M * D // 2].view(M, D // 2), xg.ptrs)
+        if "nvfp4" in self.precision.values():
+            sess.extra["sym_xg_sf"] = comm.empty((K.nvfp4_sf_bytes(M, D),), torch.uint8)
         sess.extra.update({
-            "R": R, "chan": comm.channel(), "sym_xg": xg, "sym_xg8": xg8, "sym_xg_scale": comm.empty((M,), torch.float32),
+            "R": R, "chan": comm.channel(), "sym_xg": xg, "sym_xg8": xg8, "sym_xg4": xg4,
+            "sym_xg_scale": comm.empty((M,), torch.float32),
             "sym_part": (comm.empty((self.world, M, D), BF16) if self.rs_mode == "push" else comm.empty((M, D), BF16)),
             "sym_slot": comm.empty((self.world, M, D), BF16) if self.rs_mode == "ce" else None,
             "sym_ps": comm.empty((B, sess.N), torch.float32),
@@ -174,12 +179,16 @@ class ViTEngineTP(ViTEngine):
     def _gathered(self, sess: Session, n: int):
         """The all-gathered GEMM operand rows [:n] (and their e4m3 scales)."""
         e = sess.extra
+        if self._fp4:
+            return e["sym_xg4"].local[:n], (e["sym_xg_scale"].local[:n], e["sym_xg_sf"].local)
         if self._fp8:
             return e["sym_xg8"].local[:n], e["sym_xg_scale"].local[:n]
         return e["sym_xg"].local[:n], None
 
     def _ag(self, sess: Session) -> Dict:
         e = sess.extra
+        if self._fp4:
+            return {"ag": e["sym_xg4"], "ag_scale": e["sym_xg_scale"], "ag_sf": e["sym_xg_sf"]}
         if self._fp8:
             return {"ag": e["sym_xg8"], "ag_scale": e["sym_xg_scale"]}
         return {"ag": e["sym_xg"]}
@@ -241,7 +250,7 @@ class ViTEngineTP(ViTEngine):
         with tm("a.attn"):
             self._attention_with_score(sess, l, self.local_heads, score, e["sym_ps"].local)
         with tm("a.quant"):
-            a, sa = self._act(sess, sess.o)
+            a, sa = self._act(sess, sess.o, "proj")
         w, ws = self._w(lw, "proj")
         with tm("a.proj"):
             self._row_gemm(sess, a, w, None, sa, ws, M)
@@ -374,7 +383,7 @@ class ViTEngineTP(ViTEngine):
         K.qkv_gemm(a, w, lw.qkv_b, q, sess.kc[l], sess.vc[l], head_dim=Dh, tok_idx=upd.view(-1),
                    kv_rows=rows, rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=self.local_heads, Dh=Dh)
-        a, sa = self._act(sess, o)
+        a, sa = self._act(sess, o, "proj")
         w, ws = self._w(lw, "proj")
         self._row_gemm(sess, a, w, rows, sa, ws, MT)
         comm.barrier(e["chan"])

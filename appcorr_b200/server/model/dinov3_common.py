@@ -50,8 +50,8 @@ class DINOv3BackboneMixin:
     def engine_precision(config: Any) -> Dict[str, str]:
         """Config precision -> engine precision per pass. "auto" selects e4m3 (the reference
         picks FP8 at >= 3072 rows, dinov3_precision.py:172-200, which every batched approx pass
-        of the served models reaches). NVFP4 ("fp4") runs on the e4m3 GEMM path."""
-        m = {"bf16": "bf16", "fp8": "fp8", "auto": "fp8", "fp4": "fp8"}
+        of the served models reaches). "fp4" / "nvfp4" select the NVFP4 block-scaled GEMMs."""
+        m = {"bf16": "bf16", "fp8": "fp8", "auto": "fp8", "fp4": "nvfp4", "nvfp4": "nvfp4"}
         ap = m.get(str(getattr(config, "precision", "bf16")).lower(), "bf16")
         cp = m.get(str(getattr(config, "correct_precision", "bf16")).lower(), "bf16")
         return {"approx": ap, "correct": cp}

@@ -41,6 +41,7 @@ class Qwen25VLExecutor(ModelExecutor):
         self.n_after = int(profile.get("n_text", 128)) - self.n_before
         model = Qwen25VL.random_on(self.cfg, self.device, seed)
         prec = DINOv3BackboneMixin.engine_precision(config)["approx"]
+        prec = "fp8" if prec == "nvfp4" else prec  # the LLM engine's low-precision path is e4m3
         tp = int(getattr(config, "tp_size", 1) or 1)
         if tp > 1:
             import torch.distributed as dist

@@ -55,7 +55,7 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true",
                     help="1 GPU: time the device step eagerly instead of replaying its CUDA graph")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--precision", default="fp8", choices=["bf16", "fp8"],
+    ap.add_argument("--precision", default="fp8", choices=["bf16", "fp8", "nvfp4"],
                     help="GEMM operand precision of the approx and correct passes (ours; the reference arm "
                          "runs its default bf16 path: its fp8/fp4 approx controllers need torchao)")
     ap.add_argument("--workload", default="vit7b_seg", choices=["vit7b_seg", "vlm"],
@@ -170,13 +170,18 @@ def max_over_ranks(v: float, world: int) -> float:
 
 
 # ----------------------------------------------------------------------------- our implementation
+def _cfg_precision(args) -> str:
+    """Experiment-config spelling of --precision (the reference's config calls NVFP4 "fp4")."""
+    return "fp4" if args.precision == "nvfp4" else args.precision
+
+
 def make_config(args, world: int = 1):
     sys.path.insert(0, ROOT)
     from appcorr_b200.common.protocol import ExperimentConfig
 
     tp = world if (world > 1 and args.parallel == "tp") else 1
     return ExperimentConfig(
-        tp_size=tp, precision=args.precision, correct_precision=args.precision,
+        tp_size=tp, precision=_cfg_precision(args), correct_precision=_cfg_precision(args),
         exp_id="bench", model_name="dinov3_segmentor_linhead", batch_size=args.batch,
         image_shape=(args.res, args.res, 3), input_profile_name="dinov3_ade20k_linhead_official",
         input_profile_kwargs={"backbone_arch": args.arch, "server_inference_mode": "whole"},
@@ -336,7 +341,7 @@ def run_vlm(args, rank, world):
     tp = world if (world > 1 and args.parallel == "tp") else 1
     cfg = ExperimentConfig(
         exp_id="bench_vlm", model_name="qwen25vl", batch_size=1, image_shape=(res, res, 3), tp_size=tp,
-        precision=args.precision, correct_precision=args.precision,
+        precision=_cfg_precision(args), correct_precision=_cfg_precision(args),
         input_profile_kwargs={"vlm_arch": "qwen25vl7b", "n_text": 128, "n_text_before": 16, "seed": 0},
         scheduler_policy_name="GroupTrigger", transmission_policy_name="ProgressiveLaplacian",
         transmission_kwargs={"pyramid_levels": [1, 0], "num_groups": 1, "grouping_strategy": "grid"},
@@ -588,7 +593,9 @@ def main():
                 "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
                 "dtype": ("bf16" if args.precision == "bf16" else
                           "fp8-e4m3 GEMM operands (per-row activation / per-channel weight scales, fp32 "
-                          "accumulate), bf16 attention and residual stream"),
+                          "accumulate), bf16 attention and residual stream" if args.precision == "fp8" else
+                          "nvfp4 qkv / fc1 / fc2 GEMM operands (e2m1 + ue4m3 per 16 + fp32 per row / channel), "
+                          "e4m3 attn.proj, fp32 accumulate, bf16 attention and residual stream"),
                 "data": "synthetic images (clipped N(128,60^2)), random-init weights",
                 "config": cfg_out, "gpu_launches": int(launches * args.steps), "clocks": clk, "e2e": e2e}
         print(json.dumps(line))

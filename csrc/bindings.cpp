@@ -39,22 +39,41 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
              optional<Tensor> tok_idx, int64_t seq_len, optional<Tensor> rope_sin, optional<Tensor> rope_cos,
              int64_t n_prefix, int64_t head_dim, int64_t max_ctas, optional<Tensor> a_scale,
              optional<Tensor> b_scale, int64_t kv_dim, std::vector<int64_t> rs_out, int64_t rs_rows_per_rank,
-             int64_t rs_rank, int64_t rs_slot_rows, int64_t rs_ld) {
+             int64_t rs_rank, int64_t rs_slot_rows, int64_t rs_ld, optional<Tensor> a_sf, optional<Tensor> b_sf) {
   check_cuda(A, "A");
   check_cuda(B, "B");
-  const bool fp8 = A.scalar_type() == at::kFloat8_e4m3fn;
-  TORCH_CHECK((A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16) ||
-                  (fp8 && B.scalar_type() == at::kFloat8_e4m3fn),
-              "gemm expects bf16 x bf16 or e4m3 x e4m3 operands");
-  TORCH_CHECK(fp8 == (a_scale.has_value() && b_scale.has_value()), "e4m3 operands need a_scale [M] and b_scale [N]");
+  // kind 0: bf16; 1: e4m3; 2: NVFP4 (uint8 rows of packed e2m1 pairs + ue4m3 block scales a_sf / b_sf)
+  const int kind = A.scalar_type() == at::kFloat8_e4m3fn ? 1 : (A.scalar_type() == at::kByte ? 2 : 0);
+  const bool fp8 = kind != 0;  // both low-precision kinds carry a_scale / b_scale
+  TORCH_CHECK((kind == 0 && A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16) ||
+                  (kind == 1 && B.scalar_type() == at::kFloat8_e4m3fn) || (kind == 2 && B.scalar_type() == at::kByte),
+              "gemm expects bf16 x bf16, e4m3 x e4m3 or nvfp4 (uint8) x nvfp4 operands");
+  TORCH_CHECK(fp8 == (a_scale.has_value() && b_scale.has_value()),
+              "e4m3 / nvfp4 operands need a_scale [M] and b_scale [N]");
+  TORCH_CHECK((kind == 2) == (a_sf.has_value() && b_sf.has_value()), "nvfp4 operands need a_sf and b_sf");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm: A [M,K], B [N,K]");
   TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm operands must have unit inner stride");
   TORCH_CHECK(err.scalar_type() == at::kInt && err.is_cuda(), "err must be a CUDA int32 tensor");
   c10::cuda::CUDAGuard guard(A.device());
   const int M = static_cast<int>(A.size(0));
-  const int K = static_cast<int>(A.size(1));
+  const int K = static_cast<int>(A.size(1)) * (kind == 2 ? 2 : 1);
   int N = static_cast<int>(B.size(0));
-  TORCH_CHECK(K % (fp8 ? 16 : 8) == 0, "gemm: K rows must be a multiple of 16 bytes");
+  TORCH_CHECK(K % (kind == 1 ? 16 : 8) == 0, "gemm: K rows must be a multiple of 16 bytes");
+  const uint8_t* sfa = nullptr;
+  const uint8_t* sfb = nullptr;
+  if (kind == 2) {
+    TORCH_CHECK(K % 256 == 0, "nvfp4 gemm: K must be a multiple of 256");
+    const long tile_bytes = static_cast<long>(K / 64) * 512;
+    for (auto* t : {&a_sf, &b_sf}) {
+      TORCH_CHECK((*t)->is_cuda() && (*t)->scalar_type() == at::kByte && (*t)->is_contiguous() &&
+                      (reinterpret_cast<uintptr_t>((*t)->data_ptr()) & 15) == 0,
+                  "nvfp4 scales: contiguous uint8, 16-byte aligned");
+    }
+    TORCH_CHECK(a_sf->numel() >= ((M + 127) / 128) * tile_bytes, "a_sf: ceil(M/128) x K/64 x 512 bytes");
+    TORCH_CHECK(b_sf->numel() >= ((N + 127) / 128) * tile_bytes, "b_sf: ceil(N/128) x K/64 x 512 bytes");
+    sfa = a_sf->data_ptr<uint8_t>();
+    sfb = b_sf->data_ptr<uint8_t>();
+  }
   if (fp8) {
     TORCH_CHECK(a_scale->scalar_type() == at::kFloat && a_scale->is_contiguous() && a_scale->numel() >= M,
                 "a_scale: fp32 [M]");
@@ -91,6 +110,9 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
   ep.head_dim = static_cast<int>(head_dim);
   ep.a_scale = fp8 ? a_scale->data_ptr<float>() : nullptr;
   ep.b_scale = fp8 ? b_scale->data_ptr<float>() : nullptr;
+  ep.sfa = sfa;
+  ep.sfb = sfb;
+  ep.sf_kt = K / 64;
   if (!rs_out.empty()) {
     TORCH_CHECK(epi == EPI_BF16 && rs_out.size() <= 8 && rs_rows_per_rank > 0 && rs_ld % 8 == 0,
                 "gemm: the reduce-scatter epilogue is EPI_BF16 with 1..8 slot buffers");
@@ -132,7 +154,7 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
   }
   if (M == 0) return;
   gemm_dispatch(static_cast<int>(epi), static_cast<int>(bn), A, B, M, N, K, ep, err.data_ptr<int>(),
-                static_cast<int>(max_ctas), fp8);
+                static_cast<int>(max_ctas), kind);
 }
 
 }  // namespace appcorr
@@ -150,7 +172,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("n_prefix") = 0, py::arg("head_dim") = 128, py::arg("max_ctas") = 0,
         py::arg("a_scale") = py::none(), py::arg("b_scale") = py::none(), py::arg("kv_dim") = 0,
         py::arg("rs_out") = std::vector<int64_t>{}, py::arg("rs_rows_per_rank") = 0, py::arg("rs_rank") = 0,
-        py::arg("rs_slot_rows") = 0, py::arg("rs_ld") = 0);
+        py::arg("rs_slot_rows") = 0, py::arg("rs_ld") = 0, py::arg("a_sf") = py::none(), py::arg("b_sf") = py::none());
   m.attr("EPI_BF16") = static_cast<int>(EPI_BF16);
   m.attr("EPI_F32") = static_cast<int>(EPI_F32);
   m.attr("EPI_GELU") = static_cast<int>(EPI_GELU);

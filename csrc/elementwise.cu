@@ -79,11 +79,14 @@ constexpr float kE4m3Max = 448.f;
 
 // FP8 = true: the normalised row is emitted as e4m3 (out8, stride ldo bytes) with one fp32
 // scale per row (scale8[r]) instead of bf16, ready for the e4m3 GEMM.
-template <bool FP8>
+// OUTK = 2: NVFP4 row (packed e2m1, out8 row stride ldo bytes) + ue4m3 block scales (sf, blocked
+// layout) + fp32 row scale (scale8[r] = amax / (6 * 448)).
+template <int OUTK>
 __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
     const bf16* __restrict__ x, long ldx, const int* __restrict__ rows, const bf16* __restrict__ w,
     const bf16* __restrict__ b, float eps, bf16* __restrict__ out, long ldo, bf16* __restrict__ copy_out,
-    long ldc, int D, int nrows, uint8_t* __restrict__ out8, float* __restrict__ scale8, int rms) {
+    long ldc, int D, int nrows, uint8_t* __restrict__ out8, float* __restrict__ scale8, int rms,
+    uint8_t* __restrict__ sf = nullptr) {
   __shared__ float red[kLnThreads / 32];
   const int r = blockIdx.x;
   if (r >= nrows) return;
@@ -141,7 +144,30 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
       }
     }
   }
-  if constexpr (FP8) {
+  if constexpr (OUTK == 2) {
+    // vector c covers elements 8c..8c+7; 16-element block c/2 = this lane and its xor-1 partner
+    amax = block_max<kLnThreads>(amax, red);
+    const float rs = fmaxf(amax, 1e-12f) / kNvfp4RowDiv;
+    const float inv_rs = 1.f / rs;
+    if (threadIdx.x == 0) scale8[r] = rs;
+    uint32_t* orow = reinterpret_cast<uint32_t*>(out8 + (long)r * ldo);
+#pragma unroll
+    for (int i = 0; i < kLnMaxVec; ++i) {
+      const int c = threadIdx.x + i * kLnThreads;
+      float bm = 0.f;
+      if (c < nvec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) bm = fmaxf(bm, fabsf(v[i][j]));
+      }
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));  // nvec is even: partners are both live
+      if (c < nvec) {
+        float mul;
+        const uint32_t sb = nvfp4_block_scale(bm, inv_rs, rs, mul);
+        orow[c] = pack_e2m1x8(v[i], mul);
+        if ((c & 1) == 0) sf[nvfp4_sf_offset(r, c >> 1, D >> 6)] = static_cast<uint8_t>(sb);
+      }
+    }
+  } else if constexpr (OUTK == 1) {
     amax = block_max<kLnThreads>(amax, red);
     const float sc = fmaxf(amax, 1e-12f) / kE4m3Max;
     const float inv = 1.f / sc;
@@ -206,26 +232,129 @@ __global__ void __launch_bounds__(kLnThreads) quant_rows_e4m3_kernel(const bf16*
   }
 }
 
+// Rows longer than the register-resident kernel holds (K > 8192, e.g. a 18944-wide MLP hidden):
+// pass 1 finds the amax, pass 2 re-reads the row (L1/L2 hits) and quantises.
+__global__ void __launch_bounds__(kLnThreads) quant_rows_e4m3_long_kernel(const bf16* __restrict__ x, long ldx,
+                                                                          uint8_t* __restrict__ out, long ldo,
+                                                                          float* __restrict__ scale, int K) {
+  __shared__ float red[kLnThreads / 32];
+  const int r = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (long)r * ldx);
+  float amax = 0.f;
+  for (int c = threadIdx.x; c < (K >> 3); c += kLnThreads) {
+    const uint4 u = xr[c];
+    const uint32_t* p = &u.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(p[j]);
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  amax = block_max<kLnThreads>(amax, red);
+  const float sc = fmaxf(amax, 1e-12f) / kE4m3Max;
+  const float inv = 1.f / sc;
+  if (threadIdx.x == 0) scale[r] = sc;
+  uint2* orow = reinterpret_cast<uint2*>(out + (long)r * ldo);
+  for (int c = threadIdx.x; c < (K >> 3); c += kLnThreads) {
+    const uint4 u = xr[c];
+    const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+    orow[c] = make_uint2(pack_e4m3x4(a.x * inv, a.y * inv, b.x * inv, b.y * inv),
+                         pack_e4m3x4(cc.x * inv, cc.y * inv, d.x * inv, d.y * inv));
+  }
+}
+
 void quant_rows_e4m3_op(const at::Tensor& x, at::Tensor& out, at::Tensor& scale) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
               "quant_rows_e4m3: bf16 [M,K] CUDA x");
   const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1));
-  TORCH_CHECK(K % 16 == 0 && K <= kLnThreads * kLnMaxVec * 8, "quant_rows_e4m3: K % 16 == 0 and K <= 8192");
+  TORCH_CHECK(K % 16 == 0, "quant_rows_e4m3: K % 16 == 0");
   TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && out.size(0) >= M && out.size(1) == K && out.stride(1) == 1,
               "quant_rows_e4m3: out e4m3 [M,K]");
   TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.numel() >= M, "quant_rows_e4m3: scale fp32 [M]");
   TORCH_CHECK(x.stride(0) % 8 == 0 && out.stride(0) % 16 == 0, "quant_rows_e4m3: 16-byte aligned rows");
   if (M == 0) return;
   c10::cuda::CUDAGuard g(x.device());
-  quant_rows_e4m3_kernel<<<M, kLnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  auto kern = K <= kLnThreads * kLnMaxVec * 8 ? quant_rows_e4m3_kernel : quant_rows_e4m3_long_kernel;
+  kern<<<M, kLnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), reinterpret_cast<uint8_t*>(out.data_ptr()),
       out.stride(0), scale.data_ptr<float>(), K);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// bf16 rows -> NVFP4 rows (any K % 64 == 0): pass 1 finds the row amax, pass 2 quantises one
+// 16-element block per thread step (re-reading the row from L1/L2).
+__global__ void __launch_bounds__(kLnThreads) quant_rows_nvfp4_kernel(const bf16* __restrict__ x, long ldx,
+                                                                      uint8_t* __restrict__ out, long ldo,
+                                                                      uint8_t* __restrict__ sf,
+                                                                      float* __restrict__ scale, int K) {
+  __shared__ float red[kLnThreads / 32];
+  const int r = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (long)r * ldx);
+  float amax = 0.f;
+  for (int c = threadIdx.x; c < (K >> 3); c += kLnThreads) {
+    const uint4 u = xr[c];
+    const uint32_t* p = &u.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(p[j]);
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  amax = block_max<kLnThreads>(amax, red);
+  const float rs = fmaxf(amax, 1e-12f) / kNvfp4RowDiv;
+  const float inv_rs = 1.f / rs;
+  if (threadIdx.x == 0) scale[r] = rs;
+  uint2* orow = reinterpret_cast<uint2*>(out + (long)r * ldo);
+  for (int blk = threadIdx.x; blk < (K >> 4); blk += kLnThreads) {
+    float v[16];
+    float bm = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 u = xr[2 * blk + h];
+      const uint32_t* p = &u.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(p[j]);
+        v[8 * h + 2 * j] = f.x;
+        v[8 * h + 2 * j + 1] = f.y;
+        bm = fmaxf(bm, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+    float mul;
+    const uint32_t sb = nvfp4_block_scale(bm, inv_rs, rs, mul);
+    orow[blk] = make_uint2(pack_e2m1x8(v, mul), pack_e2m1x8(v + 8, mul));
+    sf[nvfp4_sf_offset(r, blk, K >> 6)] = static_cast<uint8_t>(sb);
+  }
+}
+
+static void check_nvfp4_out(const at::Tensor& out, const at::Tensor& sf, int M, int K, const char* who) {
+  TORCH_CHECK(out.scalar_type() == at::kByte && out.dim() == 2 && out.size(0) >= M && out.size(1) == K / 2 &&
+                  out.stride(1) == 1 && out.stride(0) % 16 == 0,
+              who, ": out uint8 [M, K/2] with 16-byte aligned rows");
+  TORCH_CHECK(K % 64 == 0, who, ": K % 64 == 0");
+  TORCH_CHECK(sf.scalar_type() == at::kByte && sf.is_contiguous() &&
+                  sf.numel() >= (long)((M + 127) / 128) * (K / 64) * 512,
+              who, ": sf uint8 of ceil(M/128) * K/64 * 512 bytes");
+}
+
+void quant_rows_nvfp4_op(const at::Tensor& x, at::Tensor& out, at::Tensor& sf, at::Tensor& scale) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 &&
+                  x.stride(0) % 8 == 0,
+              "quant_rows_nvfp4: bf16 [M,K] CUDA x with 16-byte aligned rows");
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1));
+  check_nvfp4_out(out, sf, M, K, "quant_rows_nvfp4");
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.numel() >= M, "quant_rows_nvfp4: scale fp32 [M]");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard g(x.device());
+  quant_rows_nvfp4_kernel<<<M, kLnThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), out.data_ptr<uint8_t>(), out.stride(0),
+      sf.data_ptr<uint8_t>(), scale.data_ptr<float>(), K);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at::Tensor& w,
                   c10::optional<at::Tensor> b_opt, double eps, at::Tensor& out, c10::optional<at::Tensor> copy_out, c10::optional<at::Tensor> scale8,
-                  bool rms) {
+                  bool rms, c10::optional<at::Tensor> sf) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "layernorm: bf16 CUDA x");
   const int D = static_cast<int>(x.size(-1));
   TORCH_CHECK(D % 8 == 0 && D <= kLnThreads * kLnMaxVec * 8, "layernorm: D % 8 == 0 and D <= 8192");
@@ -248,9 +377,15 @@ void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at:
     cp = reinterpret_cast<bf16*>(copy_out->data_ptr());
     ldc = copy_out->stride(0);
   }
-  const bool fp8 = out.scalar_type() == at::kFloat8_e4m3fn;
-  TORCH_CHECK(fp8 || out.scalar_type() == at::kBFloat16, "layernorm: out bf16 or e4m3");
-  TORCH_CHECK(fp8 == scale8.has_value(), "layernorm: e4m3 output needs scale8 [nrows]");
+  const bool fp4 = out.scalar_type() == at::kByte;
+  const bool fp8 = out.scalar_type() == at::kFloat8_e4m3fn || fp4;
+  TORCH_CHECK(fp8 || out.scalar_type() == at::kBFloat16, "layernorm: out bf16, e4m3 or nvfp4 (uint8)");
+  TORCH_CHECK(fp8 == scale8.has_value(), "layernorm: e4m3 / nvfp4 output needs scale8 [nrows]");
+  TORCH_CHECK(fp4 == sf.has_value(), "layernorm: nvfp4 output needs sf (block scales)");
+  if (fp4) {
+    check_nvfp4_out(out, *sf, nrows, D, "layernorm");
+    TORCH_CHECK(D <= kLnThreads * kLnMaxVec * 8, "layernorm: D <= 8192");
+  }
   if (fp8) {
     TORCH_CHECK(scale8->scalar_type() == at::kFloat && scale8->numel() >= nrows, "layernorm: scale8 fp32 [nrows]");
     TORCH_CHECK(out.stride(0) % 8 == 0, "layernorm: e4m3 rows must be 8-byte aligned");
@@ -258,13 +393,18 @@ void layernorm_op(const at::Tensor& x, c10::optional<at::Tensor> rows, const at:
   if (nrows == 0) return;
   c10::cuda::CUDAGuard g(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  if (fp8)
-    layernorm_kernel<true><<<nrows, kLnThreads, 0, st>>>(
+  if (fp4)
+    layernorm_kernel<2><<<nrows, kLnThreads, 0, st>>>(
+        reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
+        bptr, static_cast<float>(eps), nullptr, out.stride(0), cp, ldc, D,
+        nrows, out.data_ptr<uint8_t>(), scale8->data_ptr<float>(), rms ? 1 : 0, sf->data_ptr<uint8_t>());
+  else if (fp8)
+    layernorm_kernel<1><<<nrows, kLnThreads, 0, st>>>(
         reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
         bptr, static_cast<float>(eps), nullptr, out.stride(0), cp, ldc, D,
         nrows, reinterpret_cast<uint8_t*>(out.data_ptr()), scale8->data_ptr<float>(), rms ? 1 : 0);
   else
-    layernorm_kernel<false><<<nrows, kLnThreads, 0, st>>>(
+    layernorm_kernel<0><<<nrows, kLnThreads, 0, st>>>(
         reinterpret_cast<const bf16*>(x.data_ptr()), ldx, rp, reinterpret_cast<const bf16*>(w.data_ptr()),
         bptr, static_cast<float>(eps), reinterpret_cast<bf16*>(out.data_ptr()),
         out.stride(0), cp, ldc, D, nrows, nullptr, nullptr, rms ? 1 : 0);
@@ -870,8 +1010,10 @@ void register_elementwise_ops(pybind11::module_& m) {
   m.def("head_mean", &head_mean_op);
   namespace py = pybind11;
   m.def("layernorm", &layernorm_op, py::arg("x"), py::arg("rows"), py::arg("w"), py::arg("b"), py::arg("eps"),
-        py::arg("out"), py::arg("copy_out") = py::none(), py::arg("scale8") = py::none(), py::arg("rms") = false);
+        py::arg("out"), py::arg("copy_out") = py::none(), py::arg("scale8") = py::none(), py::arg("rms") = false,
+        py::arg("sf") = py::none());
   m.def("quant_rows_e4m3", &quant_rows_e4m3_op, py::arg("x"), py::arg("out"), py::arg("scale"));
+  m.def("quant_rows_nvfp4", &quant_rows_nvfp4_op, py::arg("x"), py::arg("out"), py::arg("sf"), py::arg("scale"));
   m.def("add_", &add_inplace_op);
   m.def("row_sqdist", &row_sqdist_op, py::arg("a"), py::arg("b"), py::arg("out"));
   m.def("patch_im2col", &patch_im2col_op, py::arg("img"), py::arg("patch"), py::arg("mean"), py::arg("std"),

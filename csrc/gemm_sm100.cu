@@ -316,16 +316,71 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
   return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// KIND 2: NVFP4 x NVFP4 (kind::mxf4nvf4, block16): e2m1 pairs packed two per byte (element 2i in
+// the low nibble), 256-element K blocks (again 128-byte rows), one ue4m3 scale per 16 elements
+// of each row. The scales live in TMEM: per 64-element MMA step, row r's four scales sit in
+// column r / 32, lane r % 32 of every 32-lane quarter (byte s = the s-th 16-element block).
+// The blocked global layout (128-row x 64-element tiles of 512 bytes, row r at byte
+// (r % 32) * 16 + ((r % 128) / 32) * 4) is exactly the source pattern of tcgen05.cp 32x128b.warpx4,
+// so each 512-byte tile moves to TMEM with one copy.
+__device__ __forceinline__ void umma_f4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t tmem_sfa, uint32_t tmem_sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+
+// Instruction descriptor for kind::mxf4nvf4: A / B format E2M1 (1), scale format UE4M3 (bit 23 = 0),
+// dense K = 64, both operands K-major, scale-factor ids 0. The accumulator is always fp32.
+__host__ __device__ constexpr uint32_t idesc_nvf4_f32(int M, int N) {
+  return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Shared-memory descriptor of a 32-row x 16-byte scale tile (no swizzle, K-major core matrices of
+// 8 rows x 16 bytes stacked every 128 bytes).
+__device__ __forceinline__ uint64_t sf_tile_desc(uint32_t smem_byte_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>(128 >> 4) << 16;   // LBO (a single core matrix along K)
+  d |= static_cast<uint64_t>(128 >> 4) << 32;   // SBO: next 8-row core matrix
+  d |= static_cast<uint64_t>(1) << 46;          // descriptor version for sm_100
+  return d;                                     // layout type 0 = no swizzle
+}
+
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Plain (non-tensor, non-multicast) bulk copy global -> this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 template <int BN, int STAGES, int EPI, int KIND = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmShape shp, GemmEpilogue ep) {
+  constexpr bool F4 = KIND == 2;
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
   constexpr uint32_t B_BYTES = BN * kBK * 2;
-  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  constexpr uint32_t TMEM_COLS = TmemCols<BN>::value;
-  constexpr uint32_t IDESC = KIND == 1 ? idesc_e4m3_f32(kBM, BN) : idesc_bf16_f32(kBM, BN);
-  constexpr int BKE = KIND == 1 ? 128 : kBK;  // K elements per stage (128 bytes per row)
+  constexpr uint32_t SFA_BYTES = F4 ? kBM * 16 : 0;  // 4 x 512-byte scale tiles per stage
+  constexpr uint32_t SFB_BYTES = F4 ? BN * 16 : 0;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  // F4: two accumulators, then one 16 + BN/8 column scale slot per stage
+  constexpr uint32_t SF_COLS = 16 + BN / 8;
+  static_assert(!F4 || 2 * BN + STAGES * SF_COLS <= 512, "NVFP4 TMEM budget");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+  constexpr uint32_t TMEM_COLS = F4 ? 512 : TmemCols<BN>::value;
+  constexpr uint32_t IDESC = KIND == 2 ? idesc_nvf4_f32(kBM, BN)
+                                       : (KIND == 1 ? idesc_e4m3_f32(kBM, BN) : idesc_bf16_f32(kBM, BN));
+  constexpr int BKE = KIND == 2 ? 256 : (KIND == 1 ? 128 : kBK);  // K elements per stage (128-byte rows)
+  constexpr int BKX = KIND == 0 ? kBK : 128;                       // the same in tensor-map columns
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -377,8 +432,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb = smem_addr(&full[s]);
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
-          tma_load_2d(sa, &tmA, fb, kb * BKE, mb * kBM);
-          tma_load_2d(sa + A_BYTES, &tmB, fb, kb * BKE, nb * BN);
+          tma_load_2d(sa, &tmA, fb, kb * BKX, mb * kBM);
+          tma_load_2d(sa + A_BYTES, &tmB, fb, kb * BKX, nb * BN);
+          if constexpr (F4) {
+            const uint32_t sf = sa + A_BYTES + B_BYTES;
+            bulk_g2s(sf, ep.sfa + ((long)mb * ep.sf_kt + kb * 4) * 512, SFA_BYTES, fb);
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              bulk_g2s(sf + SFA_BYTES + j * 2048, ep.sfb + ((long)(nb * (BN / 128) + j) * ep.sf_kt + kb * 4) * 512,
+                       2048, fb);
+          }
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
       }
@@ -407,9 +470,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
+          uint32_t sf_col = 0;
+          if constexpr (F4) {  // stage the scale tiles into this stage's TMEM slot (ordered before the MMAs)
+            sf_col = tmem_base + 2 * BN + s * SF_COLS;
+            const uint32_t sfs = sb + B_BYTES;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              tmem_cp_sf(sf_col + k * 4, sf_tile_desc(sfs + k * 512));
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j)
+                tmem_cp_sf(sf_col + 16 + k * (BN / 32) + j * 4, sf_tile_desc(sfs + SFA_BYTES + j * 2048 + k * 512));
+            }
+          }
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 4 MMAs of 32 bytes of K per 128-byte stage row
-            if constexpr (KIND == 1)
+            if constexpr (KIND == 2)
+              umma_f4(d_tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC, sf_col + k * 4,
+                      sf_col + 16 + k * (BN / 32), (kb | k) != 0 ? 1u : 0u);
+            else if constexpr (KIND == 1)
               umma_f8(d_tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
                       (kb | k) != 0 ? 1u : 0u);
             else
@@ -663,7 +741,7 @@ int num_sms() {
 template <int BN, int STAGES, int EPI, int KIND = 0>
 void launch_gemm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const GemmEpilogue& ep,
                  int* err, int max_ctas, cudaStream_t stream) {
-  constexpr uint32_t STAGE_BYTES = (kBM + BN) * kBK * 2;
+  constexpr uint32_t STAGE_BYTES = (kBM + BN) * kBK * 2 + (KIND == 2 ? (kBM + BN) * 16 : 0);
   constexpr size_t SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   auto kern = gemm_bf16_tn_kernel<BN, STAGES, EPI, KIND>;
   static bool configured = false;
@@ -675,6 +753,9 @@ void launch_gemm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, 
   if constexpr (KIND == 1) {
     ta = make_tmap_u8_2d(A.data_ptr(), M, K, A.stride(0), kBM, 128);
     tb = make_tmap_u8_2d(B.data_ptr(), B.size(0), K, B.stride(0), BN, 128);
+  } else if constexpr (KIND == 2) {  // packed e2m1: K / 2 bytes per row
+    ta = make_tmap_u8_2d(A.data_ptr(), M, K / 2, A.stride(0), kBM, 128);
+    tb = make_tmap_u8_2d(B.data_ptr(), B.size(0), K / 2, B.stride(0), BN, 128);
   } else {
     ta = make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), kBM, kBK);
     tb = make_tmap_bf16_2d(B.data_ptr(), B.size(0), K, B.stride(0), BN, kBK);
@@ -745,10 +826,37 @@ void gemm_dispatch_fp8(int epi, int bn, const at::Tensor& A, const at::Tensor& B
   }
 }
 
+// NVFP4: one 128 x 128 tile shape (two accumulators + six stage scale slots fill the 512 TMEM
+// columns). The SwiGLU epilogue then expects w1 || w2 interleaved in 64-row blocks.
+void gemm_dispatch_fp4(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
+                       const GemmEpilogue& ep, int* err, int max_ctas) {
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(bn == 128, "nvfp4 gemm: BN 128");
+  switch (epi) {
+#define APPCORR_GEMM4_CASE(E)                                    \
+  case E:                                                        \
+    launch_gemm<128, 6, E, 2>(A, B, M, N, K, ep, err, max_ctas, st); \
+    break;
+    APPCORR_GEMM4_CASE(EPI_BF16)
+    APPCORR_GEMM4_CASE(EPI_F32)
+    APPCORR_GEMM4_CASE(EPI_GELU)
+    APPCORR_GEMM4_CASE(EPI_RESID)
+    APPCORR_GEMM4_CASE(EPI_QKV)
+    APPCORR_GEMM4_CASE(EPI_SWIGLU)
+#undef APPCORR_GEMM4_CASE
+    default:
+      TORCH_CHECK(false, "unknown epilogue ", epi);
+  }
+}
+
 void gemm_dispatch(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
-                   const GemmEpilogue& ep, int* err, int max_ctas, bool fp8) {
-  if (fp8) {
+                   const GemmEpilogue& ep, int* err, int max_ctas, int kind) {
+  if (kind == 1) {
     gemm_dispatch_fp8(epi, bn, A, B, M, N, K, ep, err, max_ctas);
+    return;
+  }
+  if (kind == 2) {
+    gemm_dispatch_fp4(epi, bn, A, B, M, N, K, ep, err, max_ctas);
     return;
   }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();

@@ -49,6 +49,11 @@ struct GemmEpilogue {
   int rs_rows_per_rank;
   int rs_rank;
   long rs_slot_rows;
+  // NVFP4 operands (e2m1 pairs + ue4m3 scales per 16 elements): scale bytes of A and B in the
+  // 128-row x 64-element blocked layout, sf_kt = K / 64 blocks per 128-row tile
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int sf_kt;
 };
 
 struct GemmShape {
@@ -58,7 +63,7 @@ struct GemmShape {
 
 
 void gemm_dispatch(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
-                   const GemmEpilogue& ep, int* err, int max_ctas, bool fp8);
+                   const GemmEpilogue& ep, int* err, int max_ctas, int kind);
 CUtensorMap make_tmap_bf16_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
                               int box_cols);
 CUtensorMap make_tmap_u8_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols);

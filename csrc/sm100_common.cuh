@@ -9,6 +9,8 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 namespace appcorr {
@@ -216,6 +218,44 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | (1u << 10)                                // B format = BF16
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+}
+
+// ---------------------------------------------------------------- NVFP4 (e2m1 + ue4m3 per 16 elements)
+// Two-level scaling: x ~= e2m1 * ue4m3_block_scale * row_scale, row_scale = row amax / (6 * 448), so
+// every block scale lands in the ue4m3 range. Scale bytes use the 128-row x 64-element blocked
+// layout read by the NVFP4 GEMM (512 bytes per tile; row r at (r % 32) * 16 + ((r % 128) / 32) * 4,
+// then the 16-element block index mod 4).
+constexpr float kNvfp4Max = 6.f;
+constexpr float kNvfp4RowDiv = 6.f * 448.f;
+
+__device__ __forceinline__ long nvfp4_sf_offset(int row, int kb16, int sf_kt) {
+  return ((long)(row >> 7) * sf_kt + (kb16 >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (kb16 & 3);
+}
+
+// Round-to-nearest-even e2m1 pair, element `lo` in the low nibble.
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Eight values * mul -> four bytes of packed e2m1 (element 0 in the lowest nibble).
+__device__ __forceinline__ uint32_t pack_e2m1x8(const float* v, float mul) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) r |= cvt_e2m1x2(v[2 * j] * mul, v[2 * j + 1] * mul) << (8 * j);
+  return r;
+}
+
+// ue4m3 block scale of a 16-element block with |x| <= bamax (byte), and the multiplier that maps
+// the block's values onto the e2m1 grid (0 for an all-zero block).
+__device__ __forceinline__ uint32_t nvfp4_block_scale(float bamax, float inv_rs, float rs, float& mul) {
+  const float s = bamax * (1.f / kNvfp4Max) * inv_rs;
+  const uint32_t b = __nv_cvt_float2_to_fp8x2(make_float2(s, 0.f), __NV_SATFINITE, __NV_E4M3) & 0xFFu;
+  const __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+  const float sd = __half2float(__half(hr));
+  mul = sd > 0.f ? 1.f / (sd * rs) : 0.f;
+  return b;
 }
 
 // ---------------------------------------------------------------- numerics helpers

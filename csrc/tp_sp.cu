@@ -73,10 +73,11 @@ struct SpArgs {
   const bf16* ln_b;
   float eps;
   int rms;
-  int fp8;
-  void* ag[kSpMaxRanks];    // gather buffers (row i), bf16 or e4m3
-  long ld_ag;               // elements
+  int fp8;                  // gather format: 0 bf16, 1 e4m3 + row scale, 2 NVFP4 (+ block scales)
+  void* ag[kSpMaxRanks];    // gather buffers (row i), bf16, e4m3 or packed e2m1
+  long ld_ag;               // elements (bf16 / e4m3) or bytes (NVFP4)
   float* ag_scale[kSpMaxRanks];
+  uint8_t* ag_sf[kSpMaxRanks];  // NVFP4 block scales (blocked layout, K = D)
 };
 
 __device__ __forceinline__ void sp_unpack8(const uint4& u, float (&v)[8]) {
@@ -235,7 +236,39 @@ __device__ __forceinline__ void sp_row_one(const SpArgs& a, int i, float* red) {
     }
     vb[k] = sp_pack8(v);  // the normalised row, bf16-rounded (the bf16 path's GEMM operand)
   }
-  if (a.fp8) {
+  if (a.fp8 == 2) {
+    // NVFP4: 16-element blocks = vector pairs (c, c ^ 1) of neighbouring lanes; the four block
+    // scales of a 64-element tile (lanes c..c+7) go out as one 4-byte store per rank
+    amax = sp_block_reduce<true>(amax, red);
+    const float rs = fmaxf(amax, 1e-12f) / kNvfp4RowDiv;
+    const float inv_rs = 1.f / rs;
+    if (threadIdx.x < W) a.ag_scale[threadIdx.x][i] = rs;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int c = threadIdx.x + k * kSpThreads;
+      const bool live = c < nvec;  // D % 64 == 0: a lane octet is live or dead as a whole
+      float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (live) sp_unpack8(vb[k], v);
+      float bm = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bm = fmaxf(bm, fabsf(v[j]));
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+      float mul;
+      const uint32_t sb = nvfp4_block_scale(bm, inv_rs, rs, mul);
+      const uint32_t pk = pack_e2m1x8(v, mul);
+      const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 2);
+      const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 4);
+      const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 6);
+      if (!live) continue;
+      const uint32_t sw = sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
+      const long so = nvfp4_sf_offset(i, c >> 1, a.D >> 6);
+#pragma unroll
+      for (int r = 0; r < W; ++r) {
+        reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(a.ag[r]) + (long)i * a.ld_ag)[c] = pk;
+        if ((c & 7) == 0) *reinterpret_cast<uint32_t*>(a.ag_sf[r] + so) = sw;
+      }
+    }
+  } else if (a.fp8) {
     amax = sp_block_reduce<true>(amax, red);
     const float sc = fmaxf(amax, 1e-12f) / 448.f;
     const float inv = 1.f / sc;
@@ -283,7 +316,8 @@ void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, 
                c10::optional<at::Tensor> resid2, c10::optional<at::Tensor> out, bool out_tok,
                c10::optional<at::Tensor> aux, int64_t aux_mode, c10::optional<at::Tensor> x,
                c10::optional<at::Tensor> copy_out, c10::optional<at::Tensor> ln_w, c10::optional<at::Tensor> ln_b,
-               double eps, bool rms, bool fp8, std::vector<int64_t> ag, int64_t ld_ag, std::vector<int64_t> ag_scale) {
+               double eps, bool rms, int64_t fp8, std::vector<int64_t> ag, int64_t ld_ag, std::vector<int64_t> ag_scale,
+               std::vector<int64_t> ag_sf) {
   TORCH_CHECK(D % 8 == 0 && D <= kSpThreads * kSpMaxVec * 8, "sp_row: D % 8 == 0 and D <= 8192");
   TORCH_CHECK(world >= 1 && world <= kSpMaxRanks, "sp_row: 1..8 ranks");
   SpArgs a{};
@@ -327,7 +361,8 @@ void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, 
   a.ln_b = sp_opt<const bf16>(ln_b);
   a.eps = static_cast<float>(eps);
   a.rms = rms ? 1 : 0;
-  a.fp8 = fp8 ? 1 : 0;
+  TORCH_CHECK(fp8 >= 0 && fp8 <= 2, "sp_row: gather format 0 (bf16), 1 (e4m3) or 2 (nvfp4)");
+  a.fp8 = static_cast<int>(fp8);
   if (a.ln_w) {
     TORCH_CHECK(static_cast<int64_t>(ag.size()) == world, "sp_row: one gather buffer per rank");
     for (int r = 0; r < world; ++r) a.ag[r] = reinterpret_cast<void*>(ag[r]);
@@ -335,6 +370,11 @@ void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, 
     if (fp8) {
       TORCH_CHECK(static_cast<int64_t>(ag_scale.size()) == world, "sp_row: one scale buffer per rank");
       for (int r = 0; r < world; ++r) a.ag_scale[r] = reinterpret_cast<float*>(ag_scale[r]);
+    }
+    if (fp8 == 2) {
+      TORCH_CHECK(D % 64 == 0 && static_cast<int64_t>(ag_sf.size()) == world && ld_ag % 16 == 0,
+                  "sp_row: nvfp4 gather needs D % 64 == 0, one block-scale buffer per rank, 16-byte rows");
+      for (int r = 0; r < world; ++r) a.ag_sf[r] = reinterpret_cast<uint8_t*>(ag_sf[r]);
     }
   }
   if (M == 0) return;
@@ -375,7 +415,8 @@ void register_sp_ops(pybind11::module_& m) {
         py::arg("world"), py::arg("D"), py::arg("src"), py::arg("src_off"), py::arg("bias"), py::arg("gamma"),
         py::arg("resid"), py::arg("resid_tok"), py::arg("resid2"), py::arg("out"), py::arg("out_tok"),
         py::arg("aux"), py::arg("aux_mode"), py::arg("x"), py::arg("copy_out"), py::arg("ln_w"), py::arg("ln_b"),
-        py::arg("eps"), py::arg("rms"), py::arg("fp8"), py::arg("ag"), py::arg("ld_ag"), py::arg("ag_scale"));
+        py::arg("eps"), py::arg("rms"), py::arg("fp8"), py::arg("ag"), py::arg("ld_ag"), py::arg("ag_scale"),
+        py::arg("ag_sf") = std::vector<int64_t>{});
 }
 
 }  // namespace appcorr

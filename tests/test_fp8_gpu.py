@@ -37,9 +37,10 @@ def _quant(x):
     return q, s
 
 
-def test_quant_rows_e4m3_matches_torch_cast():
+@pytest.mark.parametrize("K", [1024, 18944])
+def test_quant_rows_e4m3_matches_torch_cast(K):
     torch.manual_seed(0)
-    x = _rand(333, 1024, scale=3.0)
+    x = _rand(333, K, scale=3.0)
     q, s = _quant(x)
     ref_s = x.float().abs().amax(1) / 448.0
     torch.testing.assert_close(s, ref_s, rtol=1e-6, atol=0)

@@ -68,7 +68,8 @@ def _worker(rank, world, port, q, precision="bf16", rs_mode="pull", microbatch=2
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("precision,rs_mode,microbatch", [("bf16", "pull", 2), ("bf16", "pull", 1), ("bf16", "push", 2),
-                                                          ("bf16", "ce", 1), ("fp8", "pull", 2)])
+                                                          ("bf16", "ce", 1), ("fp8", "pull", 2),
+                                                          ("nvfp4", "pull", 2)])
 def test_tp2_matches_single_gpu(precision, rs_mode, microbatch):
     import torch.multiprocessing as mp
 
@@ -84,7 +85,7 @@ def test_tp2_matches_single_gpu(precision, rs_mode, microbatch):
         assert p.exitcode == 0
     # fp8: per-channel weight scales differ between a full and a split weight, so the two runs
     # quantise differently; compare at the fp8 noise level
-    tol = (2e-2, 3e-2, 1e-2) if precision == "bf16" else (1.2e-1, 1.2e-1, 1e-1)
+    tol = {"bf16": (2e-2, 3e-2, 1e-2), "fp8": (1.2e-1, 1.2e-1, 1e-1), "nvfp4": (2e-1, 2e-1, 2e-1)}[precision]
     for rank, a, c, ps in res:
         assert a < tol[0] and c < tol[1] and ps < tol[2], (rank, a, c, ps)
 
