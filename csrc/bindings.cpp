@@ -1,3 +1,4 @@
+#include <cstdlib>
 // Python bindings of the appcorr_b200 native extension (`appcorr_b200._C`).
 //
 // Every op here launches hand-written sm_100a kernels on the current CUDA stream. Tensor

@@ -4,13 +4,14 @@
 // activation matrix (row-major, K contiguous) and B an nn.Linear weight (row-major [out, in]),
 // so both operands are K-major.
 //
-// Structure (one CTA per SM, 6 warps):
+// Structure (one CTA per SM, 10 warps; 14 for NVFP4):
 //   warp 0      TMA producer: streams 128xBK A tiles and BNxBK B tiles into a STAGES-deep ring
 //               of 128-byte-swizzled shared-memory buffers, signalling `full[s]` by tx-count.
 //   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two
 //               TMEM accumulators, commits `empty[s]` per stage and `tfull[acc]` per tile.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per
-//               thread), fused elementwise work, direct global stores; then `tempty[acc]`.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per
+//               thread, two warps per lane quarter splitting the columns), fused elementwise
+//               work, direct global stores; then `tempty[acc]`.
 // Two accumulators let the epilogue of tile t overlap the main loop of tile t+1.
 //
 // The fused epilogues replace the separate elementwise launches of the reference block
@@ -124,9 +125,10 @@ __device__ __forceinline__ void scale_acc(float (&v)[32], const GemmEpilogue& ep
 }
 
 // Epilogue for one 128 x BN accumulator; each thread owns one row (`m`, possibly >= M).
+// part / nparts: this warp takes every nparts-th 32-column chunk (several warps share a lane quarter).
 template <int BN, int EPI>
 __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, const GemmShape& shp,
-                                             const GemmEpilogue& ep) {
+                                             const GemmEpilogue& ep, int part = 0, int nparts = 1) {
   const bool row_ok = m < shp.M;
   const float rs = (ep.a_scale != nullptr && row_ok) ? ep.a_scale[m] : 1.f;
   if constexpr (EPI == EPI_SWIGLU) {
@@ -135,7 +137,7 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
     const int nout0 = n0 / 2;
     const int orow = row_ok ? (ep.out_rows ? ep.out_rows[m] : m) : -1;
 #pragma unroll 1
-    for (int c = 0; c < H / 32; ++c) {
+    for (int c = part; c < H / 32; c += nparts) {
       uint32_t r1[32], r2[32];
       tmem_ld32(taddr + c * 32, r1);
       tmem_ld32(taddr + H + c * 32, r2);
@@ -176,7 +178,7 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
     }
     if (which == 2) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = part; c < BN / 32; c += nparts) {
         uint32_t r[32];
         tmem_ld32(taddr + c * 32, r);
         tmem_wait_ld();
@@ -192,10 +194,12 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
       const int half = Dh >> 1;
       const bool rope = row_ok && ep.rope_sin != nullptr && tok >= ep.n_prefix;
       const int rrow = tok - ep.n_prefix;
+      int it = 0;
 #pragma unroll 1
       for (int hb = 0; hb < BN; hb += Dh) {
 #pragma unroll 1
         for (int c = 0; c < half; c += 32) {
+          if (it++ % nparts != part) continue;
           uint32_t rl[32], rh[32];
           tmem_ld32(taddr + hb + c, rl);
           tmem_ld32(taddr + hb + half + c, rh);
@@ -243,7 +247,7 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
       }
     }
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = part; c < BN / 32; c += nparts) {
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
       tmem_wait_ld();
@@ -320,9 +324,8 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
 // the low nibble), 256-element K blocks (again 128-byte rows), one ue4m3 scale per 16 elements
 // of each row. The scales live in TMEM: per 64-element MMA step, row r's four scales sit in
 // column r / 32, lane r % 32 of every 32-lane quarter (byte s = the s-th 16-element block).
-// The blocked global layout (128-row x 64-element tiles of 512 bytes, row r at byte
-// (r % 32) * 16 + ((r % 128) / 32) * 4) is exactly the source pattern of tcgen05.cp 32x128b.warpx4,
-// so each 512-byte tile moves to TMEM with one copy.
+// In the blocked global layout (128-row x 64-element tiles of 512 bytes, row r at byte
+// (r % 32) * 16 + ((r % 128) / 32) * 4) lane a's 16 bytes of a tile are exactly its four columns.
 __device__ __forceinline__ void umma_f4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t tmem_sfa, uint32_t tmem_sfb, uint32_t accumulate) {
   asm volatile(
@@ -340,21 +343,6 @@ __host__ __device__ constexpr uint32_t idesc_nvf4_f32(int M, int N) {
   return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-// Shared-memory descriptor of a 32-row x 16-byte scale tile (no swizzle, K-major core matrices of
-// 8 rows x 16 bytes stacked every 128 bytes).
-__device__ __forceinline__ uint64_t sf_tile_desc(uint32_t smem_byte_addr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFF);
-  d |= static_cast<uint64_t>(128 >> 4) << 16;   // LBO (a single core matrix along K)
-  d |= static_cast<uint64_t>(128 >> 4) << 32;   // SBO: next 8-row core matrix
-  d |= static_cast<uint64_t>(1) << 46;          // descriptor version for sm_100
-  return d;                                     // layout type 0 = no swizzle
-}
-
-__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
 // Plain (non-tensor, non-multicast) bulk copy global -> this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
@@ -362,8 +350,19 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                : "memory");
 }
 
+// NVFP4 adds four scale warps (10..13): they move each stage's block scales from shared memory into
+// the stage's TMEM scale slot with tcgen05.st (one warp per 32-lane quarter; the MMA reads every
+// row's scales replicated in all four quarters) and release the stage to the MMA warp through
+// `sfull[s]`. (Staging them with tcgen05.cp from the MMA thread put eight copies per stage in
+// the MMA issue stream and cost about a quarter of the GEMM's time.)
+// Eight epilogue warps (2..9): two per TMEM lane quarter, each draining half of the columns, so a
+// heavy epilogue (residual + increment, SwiGLU, RoPE) stays shorter than the next tile's main loop.
+constexpr int kEpiWarps = 8;
+template <int KIND>
+constexpr int gemm_threads() { return 64 + kEpiWarps * 32 + (KIND == 2 ? 128 : 0); }
+
 template <int BN, int STAGES, int EPI, int KIND = 0>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmShape shp, GemmEpilogue ep) {
   constexpr bool F4 = KIND == 2;
@@ -388,7 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* sfull = tempty + 2;  // F4: scales of stage s are in TMEM (4 scale warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sfull + (F4 ? STAGES : 0));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -397,10 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_addr(&full[s]), 1);
       mbar_init(smem_addr(&empty[s]), 1);
+      if constexpr (F4) mbar_init(smem_addr(&sfull[s]), 4);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_addr(&tfull[a]), 1);
-      mbar_init(smem_addr(&tempty[a]), 128);
+      mbar_init(smem_addr(&tempty[a]), kEpiWarps * 32);
     }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -467,21 +468,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
+          if constexpr (F4)
+            if (!mbar_wait(smem_addr(&sfull[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
-          uint32_t sf_col = 0;
-          if constexpr (F4) {  // stage the scale tiles into this stage's TMEM slot (ordered before the MMAs)
-            sf_col = tmem_base + 2 * BN + s * SF_COLS;
-            const uint32_t sfs = sb + B_BYTES;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              tmem_cp_sf(sf_col + k * 4, sf_tile_desc(sfs + k * 512));
-#pragma unroll
-              for (int j = 0; j < BN / 128; ++j)
-                tmem_cp_sf(sf_col + 16 + k * (BN / 32) + j * 4, sf_tile_desc(sfs + SFA_BYTES + j * 2048 + k * 512));
-            }
-          }
+          const uint32_t sf_col = tmem_base + 2 * BN + s * SF_COLS;  // F4: this stage's scale slot
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 4 MMAs of 32 bytes of K per 128-byte stage row
             if constexpr (KIND == 2)
@@ -503,6 +495,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       (void)issued;
     }
+  } else if (F4 && warp >= 2 + kEpiWarps) {
+    // scale warps: lane a of quarter q writes, for every 64-element step k, the words of rows
+    // 32b + a (b = 0..3) -- bytes k*512 + a*16 .. +15 of the blocked tile -- into columns
+    // k*4 + b of the slot (A), then the same for B's rows after 16 columns
+    if constexpr (F4) {
+      static_assert(SF_COLS == 32, "one 32-column tcgen05.st per stage (BN = 128)");
+      const int q = warp & 3;
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutEpilogue)) { ok = false; break; }
+          const uint8_t* sfs = smem + s * STAGE_BYTES + A_BYTES + B_BYTES;
+          uint32_t r[32];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {  // k < 4: A tiles, k >= 4: B tiles (2048 bytes further)
+            const uint4 u = *reinterpret_cast<const uint4*>(sfs + (k >> 2) * SFA_BYTES + (k & 3) * 512 + lane * 16);
+            r[4 * k] = u.x;
+            r[4 * k + 1] = u.y;
+            r[4 * k + 2] = u.z;
+            r[4 * k + 3] = u.w;
+          }
+          tmem_st32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + 2 * BN + s * SF_COLS, r);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_addr(&sfull[s]));
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+      }
+    }
   } else {
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = q * 32 + lane;
@@ -516,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      run_epilogue<BN, EPI>(taddr, mb * kBM + row_in_tile, nb * BN, shp, ep);
+      run_epilogue<BN, EPI>(taddr, mb * kBM + row_in_tile, nb * BN, shp, ep, (warp - 2) / 4, kEpiWarps / 4);
       tc_fence_before();
       mbar_arrive(smem_addr(&tempty[acc]));
     }
@@ -764,7 +789,7 @@ void launch_gemm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, 
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
   if (grid <= 0) return;
-  kern<<<grid, kThreads, SMEM, stream>>>(ta, tb, shp, ep);
+  kern<<<grid, gemm_threads<KIND>(), SMEM, stream>>>(ta, tb, shp, ep);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
