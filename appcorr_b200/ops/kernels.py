@@ -46,8 +46,8 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
     or both NVFP4. e4m3 operands carry fp32 scales a_scale [M] (per row) and b_scale [N] (per
     output channel) that the epilogue applies to the fp32 accumulator before bias / activation.
     NVFP4 operands are uint8 [rows, K/2] (packed e2m1) and pass (row scale [rows] fp32, block
-    scales uint8) pairs as a_scale / b_scale (see quant_rows_nvfp4); their tile width is 128 and
-    a SwiGLU weight must be packed in 64-row blocks.
+    scales uint8) pairs as a_scale / b_scale (see quant_rows_nvfp4); their tile width is 256 when
+    N allows it (always for SwiGLU, whose packing block is then the usual 128), else 128.
     rs = (slot_ptrs, rows_per_rank, rank, slot_rows, ld): reduce-scatter epilogue; row m goes to
     rank (out_rows[m] or m) // rows_per_rank, slot row rank * slot_rows + m (`out` unused)."""
     fp8 = a.dtype == torch.float8_e4m3fn
@@ -55,7 +55,8 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
     if isinstance(a_scale, tuple):
         a_scale, a_sf = a_scale
         b_scale, b_sf = b_scale
-        bn = 128
+        if bn is None:
+            bn = 256 if (epi == EPI_SWIGLU or w.shape[0] % 256 == 0) else 128
     if bn is None:
         bn = 256 if epi == EPI_SWIGLU else _pick_bn(w.shape[0], a.shape[0])
         if fp8 and bn == 64:
@@ -83,10 +84,11 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
     """
     dim = w.shape[0] - 2 * kv_dim if kv_dim else w.shape[0] // 3
     a_sf = b_sf = None
-    if isinstance(a_scale, tuple):  # NVFP4 operands: (row scale, block scales); 128-wide tiles
+    if isinstance(a_scale, tuple):  # NVFP4 operands: (row scale, block scales); 256- or 128-wide tiles
         a_scale, a_sf = a_scale
         b_scale, b_sf = b_scale
-        bn = 128
+        if bn is None:
+            bn = 256 if dim % 256 == 0 and (kv_dim or dim) % 256 == 0 else 128
     if bn is None:  # widest tile that divides the q and the k / v widths (tiles never straddle)
         bn = next((t for t in (256, 128, 64) if dim % t == 0 and (kv_dim or dim) % t == 0), 128)
     sin, cos = rope if rope is not None else (None, None)

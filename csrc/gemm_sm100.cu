@@ -373,7 +373,11 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
   // F4: two accumulators, then one 16 + BN/8 column scale slot per stage
   constexpr uint32_t SF_COLS = 16 + BN / 8;
-  static_assert(!F4 || 2 * BN + STAGES * SF_COLS <= 512, "NVFP4 TMEM budget");
+  // accumulators: two (the epilogue of tile t overlaps the main loop of t+1), except NVFP4 with
+  // BN = 256, whose 256-column accumulator leaves room for one only beside the scale slots (the
+  // producer keeps prefetching the next tile's stages while the epilogue drains it)
+  constexpr int NACC = (F4 && BN == 256) ? 1 : 2;
+  static_assert(!F4 || NACC * BN + STAGES * SF_COLS <= 512, "NVFP4 TMEM budget");
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
   constexpr uint32_t TMEM_COLS = F4 ? 512 : TmemCols<BN>::value;
   constexpr uint32_t IDESC = KIND == 2 ? idesc_nvf4_f32(kBM, BN)
@@ -460,8 +464,8 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
       int t_local = 0;
       bool issued = false;
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++t_local) {
-        const int acc = t_local & 1;
-        const uint32_t acc_ph = (t_local >> 1) & 1;
+        const int acc = NACC == 2 ? (t_local & 1) : 0;
+        const uint32_t acc_ph = NACC == 2 ? ((t_local >> 1) & 1) : (t_local & 1);
         if (!mbar_wait(smem_addr(&tempty[acc]), acc_ph ^ 1, shp.err, kErrTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -473,7 +477,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
           tc_fence_after();
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
-          const uint32_t sf_col = tmem_base + 2 * BN + s * SF_COLS;  // F4: this stage's scale slot
+          const uint32_t sf_col = tmem_base + NACC * BN + s * SF_COLS;  // F4: this stage's scale slot
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 4 MMAs of 32 bytes of K per 128-byte stage row
             if constexpr (KIND == 2)
@@ -500,7 +504,10 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
     // 32b + a (b = 0..3) -- bytes k*512 + a*16 .. +15 of the blocked tile -- into columns
     // k*4 + b of the slot (A), then the same for B's rows after 16 columns
     if constexpr (F4) {
-      static_assert(SF_COLS == 32, "one 32-column tcgen05.st per stage (BN = 128)");
+      // slot columns in groups of four: group g < 4 is A's 64-element step g; group 4 + g' is B's
+      // step g' / (BN / 128), 128-row tile g' % (BN / 128) -- one 16-byte load per group per lane
+      constexpr int NG = SF_COLS / 4;
+      static_assert(NG == 8 || NG == 12, "scale slot of 32 (BN 128) or 48 (BN 256) columns");
       const int q = warp & 3;
       int s = 0;
       uint32_t ph = 0;
@@ -509,16 +516,21 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutEpilogue)) { ok = false; break; }
           const uint8_t* sfs = smem + s * STAGE_BYTES + A_BYTES + B_BYTES;
-          uint32_t r[32];
+          uint32_t r[32], r2[16];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {  // k < 4: A tiles, k >= 4: B tiles (2048 bytes further)
-            const uint4 u = *reinterpret_cast<const uint4*>(sfs + (k >> 2) * SFA_BYTES + (k & 3) * 512 + lane * 16);
-            r[4 * k] = u.x;
-            r[4 * k + 1] = u.y;
-            r[4 * k + 2] = u.z;
-            r[4 * k + 3] = u.w;
+          for (int g = 0; g < NG; ++g) {
+            const int gb = g - 4;
+            const int off = g < 4 ? g * 512 : SFA_BYTES + (gb % (BN / 128)) * 2048 + (gb / (BN / 128)) * 512;
+            const uint4 u = *reinterpret_cast<const uint4*>(sfs + off + lane * 16);
+            uint32_t* dst = g < 8 ? &r[4 * g] : &r2[4 * (g - 8)];
+            dst[0] = u.x;
+            dst[1] = u.y;
+            dst[2] = u.z;
+            dst[3] = u.w;
           }
-          tmem_st32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + 2 * BN + s * SF_COLS, r);
+          const uint32_t ta = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + NACC * BN + s * SF_COLS;
+          tmem_st32(ta, r);
+          if constexpr (NG == 12) tmem_st16(ta + 32, r2);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
@@ -535,8 +547,8 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++t_local) {
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
-      const int acc = t_local & 1;
-      const uint32_t acc_ph = (t_local >> 1) & 1;
+      const int acc = NACC == 2 ? (t_local & 1) : 0;
+      const uint32_t acc_ph = NACC == 2 ? ((t_local >> 1) & 1) : (t_local & 1);
       // All lanes wait (tcgen05.ld below is warp-collective).
       if (!mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
@@ -851,16 +863,18 @@ void gemm_dispatch_fp8(int epi, int bn, const at::Tensor& A, const at::Tensor& B
   }
 }
 
-// NVFP4: one 128 x 128 tile shape (two accumulators + six stage scale slots fill the 512 TMEM
-// columns). The SwiGLU epilogue then expects w1 || w2 interleaved in 64-row blocks.
+// NVFP4 tiles: 128 x 256 (one accumulator + four stage scale slots, the default) or 128 x 128 (two
+// accumulators + six slots) in the 512 TMEM columns. The SwiGLU epilogue's w1 || w2 interleave
+// block is BN / 2 rows (128 for the 256-wide tile).
 void gemm_dispatch_fp4(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
                        const GemmEpilogue& ep, int* err, int max_ctas) {
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  TORCH_CHECK(bn == 128, "nvfp4 gemm: BN 128");
+  TORCH_CHECK(bn == 128 || bn == 256, "nvfp4 gemm: BN 128 or 256");
   switch (epi) {
-#define APPCORR_GEMM4_CASE(E)                                    \
-  case E:                                                        \
-    launch_gemm<128, 6, E, 2>(A, B, M, N, K, ep, err, max_ctas, st); \
+#define APPCORR_GEMM4_CASE(E)                                                         \
+  case E:                                                                             \
+    if (bn == 256) launch_gemm<256, 4, E, 2>(A, B, M, N, K, ep, err, max_ctas, st);   \
+    else launch_gemm<128, 6, E, 2>(A, B, M, N, K, ep, err, max_ctas, st);             \
     break;
     APPCORR_GEMM4_CASE(EPI_BF16)
     APPCORR_GEMM4_CASE(EPI_F32)

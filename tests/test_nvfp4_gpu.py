@@ -70,16 +70,16 @@ def test_layernorm_nvfp4(D, rms):
     _bytes_match(q, sf, s, K.nvfp4_quantize_ref(ln))
 
 
-@pytest.mark.parametrize("M,N,Kd", [(1, 128, 256), (300, 512, 1024), (1029, 1024, 4096), (2500, 256, 768),
-                                    (200, 384, 18944)])
-def test_gemm_nvfp4_bias(M, N, Kd):
+@pytest.mark.parametrize("M,N,Kd,bn", [(1, 128, 256, None), (300, 512, 1024, None), (1029, 1024, 4096, None),
+                                       (1029, 1024, 4096, 128), (2500, 256, 768, None), (200, 384, 18944, None)])
+def test_gemm_nvfp4_bias(M, N, Kd, bn):
     K = _k()
     torch.manual_seed(2)
     a4, a_sf, a_s = _quant(_rand(M, Kd))
     w4, (w_s, w_sf) = K.quantize_weight_nvfp4(_rand(N, Kd, scale=Kd ** -0.5))
     bias = _rand(N, scale=0.1)
     out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-    K.gemm(a4, w4, out, bias=bias, a_scale=(a_s, a_sf), b_scale=(w_s, w_sf))
+    K.gemm(a4, w4, out, bias=bias, a_scale=(a_s, a_sf), b_scale=(w_s, w_sf), bn=bn)
     ref = K.nvfp4_dequantize(a4, a_sf, a_s) @ K.nvfp4_dequantize(w4, w_sf, w_s).T + bias.float()
     _close(out, ref)
 
@@ -94,11 +94,11 @@ def test_gemm_nvfp4_swiglu_resid_qkv():
     ad = K.nvfp4_dequantize(a4, a_sf, a_s)
     w1, w2 = _rand(Hd, D, scale=D ** -0.5), _rand(Hd, D, scale=D ** -0.5)
     b1, b2 = _rand(Hd, scale=0.1), _rand(Hd, scale=0.1)
-    wp, bp = pack_swiglu(w1, w2, b1, b2, block=64)
+    wp, bp = pack_swiglu(w1, w2, b1, b2)
     w4, (ws, wsf) = K.quantize_weight_nvfp4(wp)
     h = torch.empty(M, Hd, device=DEV, dtype=torch.bfloat16)
     K.gemm(a4, w4, h, epi=K.EPI_SWIGLU, bias=bp, a_scale=(a_s, a_sf), b_scale=(ws, wsf))
-    w1d, w2d = unpack_swiglu(K.nvfp4_dequantize(w4, wsf, ws), 64)
+    w1d, w2d = unpack_swiglu(K.nvfp4_dequantize(w4, wsf, ws))
     x1 = ad @ w1d.T + b1.float()
     x2 = ad @ w2d.T + b2.float()
     _close(h, torch.nn.functional.silu(x1) * x2, rtol=3e-2, atol=3e-2)
