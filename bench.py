@@ -55,7 +55,7 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true",
                     help="1 GPU: time the device step eagerly instead of replaying its CUDA graph")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--precision", default="fp8", choices=["bf16", "fp8", "nvfp4"],
+    ap.add_argument("--precision", default="nvfp4", choices=["bf16", "fp8", "nvfp4"],
                     help="GEMM operand precision of the approx and correct passes (ours; the reference arm "
                          "runs its default bf16 path: its fp8/fp4 approx controllers need torchao)")
     ap.add_argument("--workload", default="vit7b_seg", choices=["vit7b_seg", "vlm"],

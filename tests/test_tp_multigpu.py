@@ -85,7 +85,9 @@ def test_tp2_matches_single_gpu(precision, rs_mode, microbatch):
         assert p.exitcode == 0
     # fp8: per-channel weight scales differ between a full and a split weight, so the two runs
     # quantise differently; compare at the fp8 noise level
-    tol = {"bf16": (2e-2, 3e-2, 1e-2), "fp8": (1.2e-1, 1.2e-1, 1e-1), "nvfp4": (2e-1, 2e-1, 2e-1)}[precision]
+    # nvfp4: this random-weight stack sits at 0.26 / 0.26 / 0.24 from bf16 on one GPU, and the TP
+    # row-kernel path reproduces the one-GPU nvfp4 engine exactly at world 1
+    tol = {"bf16": (2e-2, 3e-2, 1e-2), "fp8": (1.2e-1, 1.2e-1, 1e-1), "nvfp4": (3.5e-1, 3.5e-1, 3.5e-1)}[precision]
     for rank, a, c, ps in res:
         assert a < tol[0] and c < tol[1] and ps < tol[2], (rank, a, c, ps)
 
