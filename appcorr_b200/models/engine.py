@@ -31,7 +31,7 @@ from ..common.protocol import LAYERMEAN_SERVER_PSCORES
 from ..ops import kernels as K
 from .dinov3.layers import linear_bias
 from .dinov3.vit import DinoVisionTransformer, ViTConfig
-from .weights import pack_swiglu
+from .weights import SWIGLU_BLOCK, pack_swiglu, repack_swiglu
 
 BF16 = torch.bfloat16
 
@@ -54,7 +54,8 @@ class LayerW:
     ls2: torch.Tensor
     # e4m3 copies (w8 [N, K], per-output-channel fp32 scale [N]) for the fp8 GEMM path
     q8: Optional[Dict[str, Tuple[torch.Tensor, torch.Tensor]]] = None
-    # NVFP4 copies (w4 [N, K/2], (channel scale [N], block scales)) of qkv / fc1 / fc2
+    # NVFP4 copies (w4 [N, K/2], (channel scale [N], block scales)) of qkv / fc1 / fc2, and the
+    # fc1 bias matching the NVFP4 fc1 packing ("fc1_b")
     q4: Optional[Dict[str, object]] = None
 
 
@@ -224,14 +225,17 @@ def quantize_layer_e4m3(lw: LayerW) -> None:
     lw.q8 = {n: K.quantize_weight_e4m3(getattr(lw, n + "_w")) for n in _Q8_NAMES}
 
 
-def quantize_layer_nvfp4(lw: LayerW) -> None:
-    """Attach NVFP4 copies of qkv / fc1 / fc2 (a packed SwiGLU fc1 keeps its 128-row blocks: the
-    NVFP4 SwiGLU GEMM runs 256-wide tiles)."""
-    q4: Dict[str, object] = {}
+def quantize_layer_nvfp4(lw: LayerW, swiglu: bool) -> None:
+    """Attach NVFP4 copies of qkv / fc1 / fc2. A packed SwiGLU fc1 is re-packed in 64-row blocks:
+    the NVFP4 SwiGLU GEMM runs 128-wide tiles (two accumulators, so its epilogue overlaps the next
+    tile; measured 20.4 ms per ViT-7B step against 24.0 ms for 256-wide tiles with one)."""
+    q4: Dict[str, object] = {"fc1_b": lw.fc1_b}
     for n in _Q4_NAMES:
         w = getattr(lw, n + "_w")
         if w.shape[1] % 256:
             raise ValueError(f"nvfp4 precision needs GEMM K % 256 == 0 ({n}: K = {w.shape[1]})")
+        if n == "fc1" and swiglu:
+            w, q4["fc1_b"] = repack_swiglu(w, lw.fc1_b, SWIGLU_BLOCK, 64)
         q4[n] = K.quantize_weight_nvfp4(w)
     lw.q4 = q4
 
@@ -262,7 +266,7 @@ class ViTEngine:
             if low and lw.q8 is None:
                 quantize_layer_e4m3(lw)
             if "nvfp4" in low and lw.q4 is None:
-                quantize_layer_nvfp4(lw)
+                quantize_layer_nvfp4(lw, self.cfg.is_swiglu)
         self._fp8 = False  # precision of the pass being run: e4m3 or NVFP4 operands
         self._fp4 = False  # NVFP4 for the _Q4_NAMES GEMMs
         self.taps: Tuple[int, ...] = ()  # layers whose output is kept for dense heads
@@ -312,6 +316,9 @@ class ViTEngine:
         if self._fp8:
             return lw.q8[name]
         return getattr(lw, name + "_w"), None
+
+    def _fc1_bias(self, lw: LayerW):
+        return lw.q4["fc1_b"] if self._fp4 else lw.fc1_b
 
     def _ensure_fp8_scratch(self, sess: Session) -> None:
         e = sess.extra
@@ -415,7 +422,7 @@ class ViTEngine:
     def _mlp(self, lw: LayerW, xin: torch.Tensor, hbuf: torch.Tensor, a_scale=None) -> torch.Tensor:
         w, ws = self._w(lw, "fc1")
         epi = K.EPI_SWIGLU if self.cfg.is_swiglu else K.EPI_GELU
-        K.gemm(xin, w, hbuf, epi=epi, bias=lw.fc1_b, a_scale=a_scale, b_scale=ws)
+        K.gemm(xin, w, hbuf, epi=epi, bias=self._fc1_bias(lw), a_scale=a_scale, b_scale=ws)
         return hbuf
 
     def approx_layer(self, sess: Session, l: int, x: torch.Tensor, x_out: torch.Tensor, server_pscore: str) -> None:

@@ -38,6 +38,16 @@ def unpack_swiglu(w: torch.Tensor, block: int = SWIGLU_BLOCK) -> Tuple[torch.Ten
     return v[:, 0].reshape((-1,) + rest), v[:, 1].reshape((-1,) + rest)
 
 
+def repack_swiglu(w: torch.Tensor, b: Optional[torch.Tensor], block_from: int = SWIGLU_BLOCK,
+                  block_to: int = 64) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Change the w1 / w2 interleave block of a packed SwiGLU weight (and bias)."""
+    w1, w2 = unpack_swiglu(w, block_from)
+    b1 = b2 = None
+    if b is not None:
+        b1, b2 = unpack_swiglu(b, block_from)
+    return pack_swiglu(w1, w2, b1, b2, block_to)
+
+
 def fold_batchnorm_conv1x1(conv_w: torch.Tensor, conv_b: Optional[torch.Tensor], bn_w: torch.Tensor,
                            bn_b: torch.Tensor, bn_mean: torch.Tensor, bn_var: torch.Tensor, eps: float
                            ) -> Tuple[torch.Tensor, torch.Tensor]:

@@ -5,6 +5,7 @@ attention tensors, int32 row maps). Shapes are validated in the C++ bindings.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional, Sequence, Tuple
 
 import torch
@@ -16,6 +17,10 @@ AUX_NONE, AUX_SET, AUX_ADD, AUX_OUT_MINUS = range(4)
 
 # Number of native kernel launches issued through this module (read by the benchmark).
 LAUNCHES = [0]
+# NVFP4 tile width of the qkv GEMM: 0 = 256 when the widths allow (one accumulator; measured
+# 18.7 ms per ViT-7B step against 20.2 ms at 128), 128 = always 128 (two accumulators). The other
+# NVFP4 GEMMs run 128-wide tiles (SwiGLU 20.4 vs 24.0 ms, residual fc2 12.6 vs 13.3 ms).
+FP4_BN = [int(os.environ.get("APPCORR_FP4_BN", "0"))]
 
 
 def _count(n: int = 1) -> None:
@@ -46,8 +51,8 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
     or both NVFP4. e4m3 operands carry fp32 scales a_scale [M] (per row) and b_scale [N] (per
     output channel) that the epilogue applies to the fp32 accumulator before bias / activation.
     NVFP4 operands are uint8 [rows, K/2] (packed e2m1) and pass (row scale [rows] fp32, block
-    scales uint8) pairs as a_scale / b_scale (see quant_rows_nvfp4); their tile width is 256 when
-    N allows it (always for SwiGLU, whose packing block is then the usual 128), else 128.
+    scales uint8) pairs as a_scale / b_scale (see quant_rows_nvfp4); their default tile width is
+    128, so a SwiGLU weight is packed in 64-row blocks (bn=256 takes the usual 128-row packing).
     rs = (slot_ptrs, rows_per_rank, rank, slot_rows, ld): reduce-scatter epilogue; row m goes to
     rank (out_rows[m] or m) // rows_per_rank, slot row rank * slot_rows + m (`out` unused)."""
     fp8 = a.dtype == torch.float8_e4m3fn
@@ -56,7 +61,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
         a_scale, a_sf = a_scale
         b_scale, b_sf = b_scale
         if bn is None:
-            bn = 256 if (epi == EPI_SWIGLU or w.shape[0] % 256 == 0) else 128
+            bn = 128
     if bn is None:
         bn = 256 if epi == EPI_SWIGLU else _pick_bn(w.shape[0], a.shape[0])
         if fp8 and bn == 64:
@@ -88,7 +93,7 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
         a_scale, a_sf = a_scale
         b_scale, b_sf = b_scale
         if bn is None:
-            bn = 256 if dim % 256 == 0 and (kv_dim or dim) % 256 == 0 else 128
+            bn = 256 if dim % 256 == 0 and (kv_dim or dim) % 256 == 0 and FP4_BN[0] != 128 else 128
     if bn is None:  # widest tile that divides the q and the k / v widths (tiles never straddle)
         bn = next((t for t in (256, 128, 64) if dim % t == 0 and (kv_dim or dim) % t == 0), 128)
     sin, cos = rope if rope is not None else (None, None)

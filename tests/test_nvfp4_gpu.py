@@ -71,7 +71,7 @@ def test_layernorm_nvfp4(D, rms):
 
 
 @pytest.mark.parametrize("M,N,Kd,bn", [(1, 128, 256, None), (300, 512, 1024, None), (1029, 1024, 4096, None),
-                                       (1029, 1024, 4096, 128), (2500, 256, 768, None), (200, 384, 18944, None)])
+                                       (1029, 1024, 4096, 256), (2500, 256, 768, 256), (200, 384, 18944, None)])
 def test_gemm_nvfp4_bias(M, N, Kd, bn):
     K = _k()
     torch.manual_seed(2)
@@ -84,7 +84,8 @@ def test_gemm_nvfp4_bias(M, N, Kd, bn):
     _close(out, ref)
 
 
-def test_gemm_nvfp4_swiglu_resid_qkv():
+@pytest.mark.parametrize("block,bn", [(64, None), (128, 256)])
+def test_gemm_nvfp4_swiglu_resid_qkv(block, bn):
     K = _k()
     from appcorr_b200.models.weights import pack_swiglu, unpack_swiglu
 
@@ -94,11 +95,11 @@ def test_gemm_nvfp4_swiglu_resid_qkv():
     ad = K.nvfp4_dequantize(a4, a_sf, a_s)
     w1, w2 = _rand(Hd, D, scale=D ** -0.5), _rand(Hd, D, scale=D ** -0.5)
     b1, b2 = _rand(Hd, scale=0.1), _rand(Hd, scale=0.1)
-    wp, bp = pack_swiglu(w1, w2, b1, b2)
+    wp, bp = pack_swiglu(w1, w2, b1, b2, block)
     w4, (ws, wsf) = K.quantize_weight_nvfp4(wp)
     h = torch.empty(M, Hd, device=DEV, dtype=torch.bfloat16)
-    K.gemm(a4, w4, h, epi=K.EPI_SWIGLU, bias=bp, a_scale=(a_s, a_sf), b_scale=(ws, wsf))
-    w1d, w2d = unpack_swiglu(K.nvfp4_dequantize(w4, wsf, ws))
+    K.gemm(a4, w4, h, epi=K.EPI_SWIGLU, bias=bp, a_scale=(a_s, a_sf), b_scale=(ws, wsf), bn=bn)
+    w1d, w2d = unpack_swiglu(K.nvfp4_dequantize(w4, wsf, ws), block)
     x1 = ad @ w1d.T + b1.float()
     x2 = ad @ w2d.T + b2.float()
     _close(h, torch.nn.functional.silu(x1) * x2, rtol=3e-2, atol=3e-2)
@@ -108,7 +109,8 @@ def test_gemm_nvfp4_swiglu_resid_qkv():
     w34, (w3s, w3sf) = K.quantize_weight_nvfp4(w3)
     gamma, resid = _rand(D, scale=0.5), _rand(M, D)
     out = torch.empty(M, D, device=DEV, dtype=torch.bfloat16)
-    K.gemm(h4, w34, out, epi=K.EPI_RESID, gamma=gamma, resid=resid, a_scale=(h_s, h_sf), b_scale=(w3s, w3sf))
+    K.gemm(h4, w34, out, epi=K.EPI_RESID, gamma=gamma, resid=resid, a_scale=(h_s, h_sf), b_scale=(w3s, w3sf),
+           bn=bn)
     ref = resid.float() + (K.nvfp4_dequantize(h4, h_sf, h_s) @ K.nvfp4_dequantize(w34, w3sf, w3s).T) * gamma.float()
     _close(out, ref)
     # qkv split (no RoPE), 128-wide tiles
@@ -119,7 +121,7 @@ def test_gemm_nvfp4_swiglu_resid_qkv():
     k = torch.zeros_like(q)
     v = torch.zeros_like(q)
     K.qkv_gemm(a4, wq4, None, q, k, v, head_dim=Dh, seq_len=M, n_prefix=M, a_scale=(a_s, a_sf),
-               b_scale=(wqs, wqsf))
+               b_scale=(wqs, wqsf), bn=bn if bn else 128)
     ref = ad @ K.nvfp4_dequantize(wq4, wqsf, wqs).T
     _close(q, ref[:, : H * Dh])
     _close(k, ref[:, H * Dh: 2 * H * Dh])
