@@ -142,10 +142,17 @@ def main(argv=None) -> None:
         x = torch.randn(a.M, a.D, device=dev).to(torch.bfloat16)
         wt = torch.ones(a.D, device=dev, dtype=torch.bfloat16)
         bt = torch.zeros(a.D, device=dev, dtype=torch.bfloat16)
-        out = torch.empty_like(x)
-        fn = lambda: K.layernorm(x, wt, bt, 1e-5, out)  # noqa: E731
         flops = 0.0
-        res.update(M=a.M, D=a.D, bytes=2 * x.numel() * 2)
+        if a.fp4:  # NVFP4 output: packed rows + blocked block scales + row scales
+            out = torch.empty(a.M, a.D // 2, device=dev, dtype=torch.uint8)
+            sf = torch.zeros(K.nvfp4_sf_bytes(a.M, a.D), device=dev, dtype=torch.uint8)
+            sc = torch.empty(a.M, device=dev)
+            fn = lambda: K.layernorm(x, wt, bt, 1e-5, out, scale8=sc, sf=sf)  # noqa: E731
+            res.update(M=a.M, D=a.D, fp4=True, bytes=x.numel() * 2 + out.numel() + sf.numel() + sc.numel() * 4)
+        else:
+            out = torch.empty_like(x)
+            fn = lambda: K.layernorm(x, wt, bt, 1e-5, out)  # noqa: E731
+            res.update(M=a.M, D=a.D, bytes=2 * x.numel() * 2)
         ref = (lambda: torch.nn.functional.layer_norm(x, (a.D,), wt, bt, 1e-5)) if a.ref else None  # noqa: E731
     if a.once:
         fn()
