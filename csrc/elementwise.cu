@@ -192,34 +192,42 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_kernel(
   }
 }
 
-// Warp-per-row LayerNorm for D % 256 == 0, D <= 4096 (NV = D / 256 16-byte vectors per lane):
-// 8 rows per 256-thread CTA, shuffle-only reductions, the row kept as packed bf16 in registers.
-// Same arithmetic and outputs as layernorm_kernel (one CTA per row, block reductions), which it
-// replaces for these widths (that kernel was latency-bound at about 1.8 TB/s on 8k x 4096 rows).
-constexpr int kLnwRows = 8;
+// Warp-per-row LayerNorm for D % 256 == 0, D <= 4096, the row staged in shared memory: each warp
+// copies its row (D * 2 bytes) with 16-byte cp.async, then runs the statistics, normalisation and
+// output passes from shared memory. Registers stay low, so ~28 rows per SM are in flight (a
+// register-resident version held 254 registers and 8 rows per SM, latency-bound at 14 % DRAM
+// throughput). Same arithmetic and outputs as layernorm_kernel (one CTA per row, block reductions),
+// which stays for other widths.
+constexpr int kLnsRows = 4;  // rows (warps) per CTA
 
-template <int OUTK, int NV>
-__global__ void __launch_bounds__(kLnwRows * 32) layernorm_warp_kernel(
+__device__ __forceinline__ void ln_cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+template <int OUTK>
+__global__ void __launch_bounds__(kLnsRows * 32) layernorm_smem_kernel(
     const bf16* __restrict__ x, long ldx, const int* __restrict__ rows, const bf16* __restrict__ w,
     const bf16* __restrict__ b, float eps, bf16* __restrict__ out, long ldo, bf16* __restrict__ copy_out,
     long ldc, int D, int nrows, uint8_t* __restrict__ out8, float* __restrict__ scale8, int rms,
     uint8_t* __restrict__ sf) {
+  extern __shared__ uint4 lns_smem[];
   const int lane = threadIdx.x & 31;
-  const int r = blockIdx.x * kLnwRows + (threadIdx.x >> 5);
+  const int wid = threadIdx.x >> 5;
+  const int r = blockIdx.x * kLnsRows + wid;
   if (r >= nrows) return;
+  const int nvec = D >> 3;  // a multiple of 32
+  uint4* row = lns_smem + wid * nvec;
   const long src = rows ? rows[r] : r;
   const uint4* xr = reinterpret_cast<const uint4*>(x + src * ldx);
-  uint4 u[NV];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) u[i] = xr[lane + 32 * i];
-  if (copy_out) {
-#pragma unroll
-    for (int i = 0; i < NV; ++i) reinterpret_cast<uint4*>(copy_out + (long)r * ldc)[lane + 32 * i] = u[i];
-  }
+  for (int c = lane; c < nvec; c += 32) ln_cp_async16(smem_addr(row + c), xr + c);
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncwarp();
   float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const uint32_t* p = &u[i].x;
+#pragma unroll 4
+  for (int c = lane; c < nvec; c += 32) {
+    const uint4 u = row[c];
+    if (copy_out) reinterpret_cast<uint4*>(copy_out + (long)r * ldc)[c] = u;
+    const uint32_t* p = &u.x;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 f = unpack_bf16x2(p[j]);
@@ -228,9 +236,10 @@ __global__ void __launch_bounds__(kLnwRows * 32) layernorm_warp_kernel(
   }
   const float mean = rms ? 0.f : warp_sum(s) / D;
   float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const uint32_t* p = &u[i].x;
+#pragma unroll 4
+  for (int c = lane; c < nvec; c += 32) {
+    const uint4 u = row[c];
+    const uint32_t* p = &u.x;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 f = unpack_bf16x2(p[j]);
@@ -241,12 +250,12 @@ __global__ void __launch_bounds__(kLnwRows * 32) layernorm_warp_kernel(
   const uint4* wv = reinterpret_cast<const uint4*>(w);
   const uint4* bv = reinterpret_cast<const uint4*>(b);
   float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = lane + 32 * i;
+#pragma unroll 4
+  for (int c = lane; c < nvec; c += 32) {
+    uint4 u = row[c];
     const uint4 wu = __ldg(wv + c);
     const uint4 bu = b ? __ldg(bv + c) : make_uint4(0u, 0u, 0u, 0u);
-    uint32_t* p = &u[i].x;
+    uint32_t* p = &u.x;
     const uint32_t* wp = &wu.x;
     const uint32_t* bp = &bu.x;
 #pragma unroll
@@ -257,38 +266,34 @@ __global__ void __launch_bounds__(kLnwRows * 32) layernorm_warp_kernel(
       amax = fmaxf(amax, fmaxf(fabsf(y0), fabsf(y1)));
       p[j] = pack_bf16x2(y0, y1);
     }
+    if constexpr (OUTK == 0) reinterpret_cast<uint4*>(out + (long)r * ldo)[c] = u;
+    else row[c] = u;  // normalised row back in place (this lane reads it again below)
   }
-  if constexpr (OUTK == 0) {
-#pragma unroll
-    for (int i = 0; i < NV; ++i) reinterpret_cast<uint4*>(out + (long)r * ldo)[lane + 32 * i] = u[i];
-  } else if constexpr (OUTK == 1) {
+  if constexpr (OUTK == 1) {
     amax = warp_max(amax);
     const float sc = fmaxf(amax, 1e-12f) / kE4m3Max;
     const float inv = 1.f / sc;
     if (lane == 0) scale8[r] = sc;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      float v[8];
-      const uint32_t* p = &u[i].x;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack_bf16x2(p[j]);
-        v[2 * j] = f.x * inv;
-        v[2 * j + 1] = f.y * inv;
-      }
-      reinterpret_cast<uint2*>(out8 + (long)r * ldo)[lane + 32 * i] =
-          make_uint2(pack_e4m3x4(v[0], v[1], v[2], v[3]), pack_e4m3x4(v[4], v[5], v[6], v[7]));
+#pragma unroll 4
+    for (int c = lane; c < nvec; c += 32) {
+      const uint4 u = row[c];
+      const float2 a0 = unpack_bf16x2(u.x), a1 = unpack_bf16x2(u.y), a2 = unpack_bf16x2(u.z), a3 = unpack_bf16x2(u.w);
+      reinterpret_cast<uint2*>(out8 + (long)r * ldo)[c] =
+          make_uint2(pack_e4m3x4(a0.x * inv, a0.y * inv, a1.x * inv, a1.y * inv),
+                     pack_e4m3x4(a2.x * inv, a2.y * inv, a3.x * inv, a3.y * inv));
     }
-  } else {
+  } else if constexpr (OUTK == 2) {
     amax = warp_max(amax);
     const float rs = fmaxf(amax, 1e-12f) / kNvfp4RowDiv;
     const float inv_rs = 1.f / rs;
     if (lane == 0) scale8[r] = rs;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = lane + 32 * i;
+    // vector c = lane + 32 i: 16-element blocks pair lanes (l, l ^ 1); the four block scales of a
+    // 64-element tile (lanes c..c+7) go out as one 4-byte store
+#pragma unroll 2
+    for (int c = lane; c < nvec; c += 32) {
+      const uint4 u = row[c];
       float v[8];
-      const uint32_t* p = &u[i].x;
+      const uint32_t* p = &u.x;
       float bm = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -301,7 +306,6 @@ __global__ void __launch_bounds__(kLnwRows * 32) layernorm_warp_kernel(
       float mul;
       const uint32_t sb = nvfp4_block_scale(bm, inv_rs, rs, mul);
       reinterpret_cast<uint32_t*>(out8 + (long)r * ldo)[c] = pack_e2m1x8(v, mul);
-      // the four block scales of a 64-element tile (lanes c..c+7) as one 4-byte store
       const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 2);
       const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 4);
       const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 6);
@@ -316,19 +320,11 @@ static bool launch_layernorm_warp(int D, int nrows, cudaStream_t st, const bf16*
                                   const bf16* w, const bf16* b, float eps, bf16* out, long ldo, bf16* cp, long ldc,
                                   uint8_t* out8, float* scale8, int rms, uint8_t* sf) {
   if (D % 256 != 0 || D > 4096) return false;
-  const int grid = (nrows + kLnwRows - 1) / kLnwRows;
-#define APPCORR_LNW(NV)                                                                                    \
-  case NV:                                                                                                 \
-    layernorm_warp_kernel<OUTK, NV><<<grid, kLnwRows * 32, 0, st>>>(x, ldx, rp, w, b, eps, out, ldo, cp, ldc, \
-                                                                    D, nrows, out8, scale8, rms, sf);      \
-    return true;
-  switch (D / 256) {
-    APPCORR_LNW(1) APPCORR_LNW(2) APPCORR_LNW(3) APPCORR_LNW(4) APPCORR_LNW(5) APPCORR_LNW(6) APPCORR_LNW(7)
-    APPCORR_LNW(8) APPCORR_LNW(9) APPCORR_LNW(10) APPCORR_LNW(11) APPCORR_LNW(12) APPCORR_LNW(13)
-    APPCORR_LNW(14) APPCORR_LNW(15) APPCORR_LNW(16)
-    default: return false;
-  }
-#undef APPCORR_LNW
+  const int grid = (nrows + kLnsRows - 1) / kLnsRows;
+  const size_t smem = static_cast<size_t>(kLnsRows) * D * 2;  // <= 32 KB: no opt-in needed
+  layernorm_smem_kernel<OUTK><<<grid, kLnsRows * 32, smem, st>>>(x, ldx, rp, w, b, eps, out, ldo, cp, ldc, D, nrows,
+                                                                  out8, scale8, rms, sf);
+  return true;
 }
 
 // bf16 rows -> e4m3 rows + one fp32 scale per row (amax / 448). One CTA per row, K <= 8192.
