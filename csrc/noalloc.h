@@ -16,8 +16,14 @@
 //    larger problems are refused with APPCORR_NOALLOC_ERR_TOO_LARGE and nothing is launched.
 //    Every GPU that loads the library keeps this 4 MiB array until the process exits.
 //  * (N + head_dim) fp32 values must fit the kernel's shared memory (N up to about 50k tokens).
-//  * The first call on a device looks up the array's device address with that device current;
-//    make that first call before any stream capture.
+//  * q and k must be 4-byte aligned with an even row stride `ld`, and out 4-byte aligned; other
+//    pointers are refused with APPCORR_NOALLOC_ERR_BAD_ARG before anything is launched.
+//  * The first call on a device looks up the array's device address with that device current.
+//    With lazy module loading the driver also loads the library's device code, the 4 MiB array
+//    included, on that first call. So make the first call per device at start-up: outside any
+//    allocator or memory-pool callback and before any stream capture. Later calls allocate nothing.
+//  * A CUDA error already pending on the calling thread when the function is entered is not
+//    cleared; the call returns APPCORR_NOALLOC_ERR_CUDA without launching.
 //  * All calls share the one array, which keeps the last call's contents (every element a call
 //    reads is first written by the same call, so nothing needs clearing). Calls that overlap on
 //    the GPU (different streams, or different host threads on one device) race on the array;

@@ -3,6 +3,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <cstdio>
 #include <mutex>
 
@@ -27,7 +28,6 @@ constexpr int kProbThreads = 256;   // matches the kernel's launch bounds
 constexpr int kMaxSmem = 200 * 1024;
 std::mutex g_mu;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
-bool g_smem_ready[kMaxDevices] = {false};
 thread_local char g_err[256] = "";
 
 int fail(int code, const char* msg) {
@@ -45,6 +45,12 @@ extern "C" __attribute__((visibility("default"))) int appcorr_cls_attn_pscore_no
   if (q == nullptr || k == nullptr || out == nullptr || B <= 0 || N <= 0 || H <= 0 || head_dim <= 0 ||
       head_dim % 64 != 0 || ld < (long)H * head_dim)
     return fail(APPCORR_NOALLOC_ERR_BAD_ARG, "appcorr_cls_attn_pscore_noalloc: invalid argument");
+  // The kernel reads q and k two bf16 values at a time: both pointers 4-byte aligned and an even
+  // row stride, or the loads would be misaligned on the device.
+  if ((reinterpret_cast<uintptr_t>(q) & 3) != 0 || (reinterpret_cast<uintptr_t>(k) & 3) != 0 || (ld & 1) != 0 ||
+      (reinterpret_cast<uintptr_t>(out) & 3) != 0)
+    return fail(APPCORR_NOALLOC_ERR_BAD_ARG,
+                "appcorr_cls_attn_pscore_noalloc: q/k/out must be 4-byte aligned and ld even");
   if ((long)B * H * N > APPCORR_NOALLOC_PSCORE_MAX_ELEMS)
     return fail(APPCORR_NOALLOC_ERR_TOO_LARGE,
                 "appcorr_cls_attn_pscore_noalloc: B*H*N exceeds the scratch array of 1<<20 fp32 values");
@@ -64,21 +70,25 @@ extern "C" __attribute__((visibility("default"))) int appcorr_cls_attn_pscore_no
         return fail(APPCORR_NOALLOC_ERR_CUDA, "appcorr_cls_attn_pscore_noalloc: cudaGetSymbolAddress failed");
       g_scratch_ptr[dev] = static_cast<float*>(p);
     }
-    if (!g_smem_ready[dev]) {
-      if (cudaFuncSetAttribute(appcorr::cls_attn_probs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kMaxSmem) != cudaSuccess)
-        return fail(APPCORR_NOALLOC_ERR_CUDA, "appcorr_cls_attn_pscore_noalloc: cudaFuncSetAttribute failed");
-      g_smem_ready[dev] = true;
-    }
     scratch = g_scratch_ptr[dev];
   }
+  // The regular op sets this kernel's shared-memory limit to its own size, so the limit is set on
+  // every call that needs more than the default 48 KB (no allocation involved).
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(appcorr::cls_attn_probs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return fail(APPCORR_NOALLOC_ERR_CUDA, "appcorr_cls_attn_pscore_noalloc: cudaFuncSetAttribute failed");
+  // Launch errors are read with cudaPeekAtLastError: an error left by earlier, unrelated work is
+  // not cleared here, and it is reported as such rather than as this call's launch failure.
+  if (cudaPeekAtLastError() != cudaSuccess)
+    return fail(APPCORR_NOALLOC_ERR_CUDA, "appcorr_cls_attn_pscore_noalloc: a CUDA error was pending before this call");
   appcorr::cls_attn_probs_kernel<<<dim3(B, H), kProbThreads, smem, stream>>>(
       static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), ld, N, H, head_dim, scale, scratch);
-  if (cudaGetLastError() != cudaSuccess)
+  if (cudaPeekAtLastError() != cudaSuccess)
     return fail(APPCORR_NOALLOC_ERR_CUDA, "appcorr_cls_attn_pscore_noalloc: probability kernel launch failed");
   const long total = (long)B * N;
   appcorr::head_mean_kernel<<<(int)((total + 255) / 256), 256, 0, stream>>>(scratch, B, H, N, out);
-  if (cudaGetLastError() != cudaSuccess)
+  if (cudaPeekAtLastError() != cudaSuccess)
     return fail(APPCORR_NOALLOC_ERR_CUDA, "appcorr_cls_attn_pscore_noalloc: head-mean kernel launch failed");
   g_err[0] = '\0';
   return APPCORR_NOALLOC_OK;

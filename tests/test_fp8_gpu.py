@@ -65,6 +65,23 @@ def test_layernorm_e4m3(D):
     torch.testing.assert_close(s, ref.abs().amax(1) / 448.0, rtol=1e-2, atol=0)
 
 
+@pytest.mark.parametrize("D", [384, 1024, 4096])
+def test_layernorm_e4m3_gather_copy_out(D):
+    """The shared-memory LayerNorm with a row gather and the raw-row copy, e4m3 output."""
+    K = _k()
+    torch.manual_seed(11)
+    x = _rand(60, D, scale=2.0)
+    w, b = _rand(D), _rand(D, scale=0.1)
+    rows = torch.tensor([5, 0, 59, 5, 31, 2, 44], device=DEV, dtype=torch.int32)
+    q = torch.empty(7, D, device=DEV, dtype=torch.float8_e4m3fn)
+    s = torch.empty(7, device=DEV, dtype=torch.float32)
+    cp = torch.empty(7, D, device=DEV, dtype=torch.bfloat16)
+    K.layernorm(x, w, b, 1e-6, q, rows=rows, copy_out=cp, scale8=s)
+    ref = torch.nn.functional.layer_norm(x.float()[rows.long()], (D,), w.float(), b.float(), 1e-6)
+    _close(_deq(q, s), ref, rtol=7e-2, atol=0)
+    assert torch.equal(cp, x[rows.long()])
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 256, 128), (300, 512, 1024), (1029, 1024, 4096), (255, 384, 256),
                                    (2500, 256, 768)])
 def test_gemm_e4m3_bias(M, N, K):

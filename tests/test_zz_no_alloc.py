@@ -56,3 +56,41 @@ def test_noalloc_rejects_oversized_problem():
     rc = fn(q.data_ptr(), q.data_ptr(), 64 * 64, 64, 512, 64, 64, 0.125, out.data_ptr(), None)
     assert rc == 1
     assert b"exceeds" in err()
+
+
+def test_noalloc_large_smem_after_regular_op():
+    """A regular call that sets the kernel's shared-memory limit to ~60 KB, then an entry-point call
+    that needs ~160 KB: the entry point raises the limit itself on every call that needs it."""
+    from appcorr_b200.ops import kernels as K
+
+    fn, err = _entry()
+    torch.manual_seed(1)
+    H, Dh = 8, 64
+    q = torch.randn(15000, H * Dh, device="cuda").to(torch.bfloat16)
+    ref = torch.empty(1, 15000, device="cuda")
+    K.cls_attn_pscore(q, q, B=1, N=15000, H=H, Dh=Dh, scratch=torch.empty(1, H, 15000, device="cuda"), out=ref)
+    N = 40000
+    q = torch.randn(N, H * Dh, device="cuda").to(torch.bfloat16)
+    k = torch.randn(N, H * Dh, device="cuda").to(torch.bfloat16)
+    ref = torch.empty(1, N, device="cuda")
+    K.cls_attn_pscore(q, k, B=1, N=N, H=H, Dh=Dh, scratch=torch.empty(1, H, N, device="cuda"), out=ref,
+                      scale=Dh ** -0.5)
+    for _ in range(2):
+        out = torch.full((1, N), float("nan"), device="cuda")
+        rc = fn(q.data_ptr(), k.data_ptr(), q.stride(0), 1, N, H, Dh, Dh ** -0.5, out.data_ptr(),
+                torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, err()
+        torch.cuda.synchronize()
+        assert torch.allclose(out, ref, rtol=1e-3, atol=1e-6)
+
+
+def test_noalloc_rejects_misaligned_operands():
+    """Checked on the host: nothing is launched for a refused call."""
+    fn, err = _entry()
+    q = torch.zeros(8, 128, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(8, device="cuda")
+    base = q.data_ptr()
+    assert fn(base + 2, base, 128, 1, 8, 2, 64, 0.125, out.data_ptr(), None) == 2   # q 2-byte aligned
+    assert b"aligned" in err()
+    assert fn(base, base + 2, 128, 1, 8, 2, 64, 0.125, out.data_ptr(), None) == 2   # k 2-byte aligned
+    assert fn(base, base, 129, 1, 8, 2, 64, 0.125, out.data_ptr(), None) == 2       # odd row stride
