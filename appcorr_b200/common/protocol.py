@@ -7,6 +7,8 @@ AppCorr option normaliser implements the same aliases and validation rules
 """
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass, field
 from enum import Enum, auto
 from typing import Any, Dict, List, Optional, Tuple
@@ -218,7 +220,7 @@ _INPUT_PROFILES: Dict[str, Dict[str, Any]] = {
         "vggt_resolution": 512,
         "vggt_patch_size": 16,
         "vggt_resize_mode": "balanced",
-        "vggt_weights_path": "~/cjpark/weights/vggt/vggt_omega_1b_512.pt",
+        "vggt_weights_path": None,  # None: random init (no checkpoint shipped)
         "autocast_dtype": "bfloat16",
     },
 }
@@ -303,7 +305,7 @@ class ExperimentConfig:
         return {
             "model": sk.get("lowres_sr_model", "realesrgan_x4plus"),
             "dtype": sk.get("lowres_sr_dtype", "fp16"),
-            "weights_dir": sk.get("lowres_sr_weights_dir", "~/cjpark/weights/realesrgan"),
+            "weights_dir": sk.get("lowres_sr_weights_dir", os.environ.get("APPCORR_SR_WEIGHTS_DIR")),
             "tile": sk.get("lowres_sr_tile", 0),
             "tile_pad": sk.get("lowres_sr_tile_pad", 10),
             "pre_pad": sk.get("lowres_sr_pre_pad", 0),

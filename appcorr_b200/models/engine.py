@@ -213,6 +213,22 @@ class Session:
     extra: Dict[str, torch.Tensor] = field(default_factory=dict)
 
 
+def _score_kind(server_pscore: str) -> str:
+    """Family of a server_pscore name: "cls", "patch", "pseudo" or "none" (no attention-derived
+    score: none / disabled, and random, which is drawn at correction time)."""
+    k = str(server_pscore)
+    if k in ("none", "disabled", "random"):
+        return "none"
+    if k in ("cls_attn_prob", "cls_attn_prob_layermean"):
+        return "cls"
+    if k in ("patch_attn_prob", "patch_attn_prob_layermean", "patch_attn_prune"):
+        return "patch"
+    if k in ("patch_pseudo_attn_prob", "patch_pseudo_attn_prob_layermean", "pseudo_patch_attn_prob",
+             "pseudo_patch_attn_prob_layermean"):
+        return "pseudo"
+    raise ValueError(f"unknown server_pscore {server_pscore!r}")
+
+
 PRECISIONS = ("bf16", "fp8", "nvfp4")
 _Q8_NAMES = ("qkv", "proj", "fc1", "fc2")
 # nvfp4 precision: these GEMMs take NVFP4 operands; attn.proj stays e4m3 (the reference's
@@ -436,8 +452,7 @@ class ViTEngine:
             nw = sess.extra["n_windows"]
             K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B * nw, Tq=N // nw, Tk=N // nw, H=H, Dh=Dh)
         else:
-            self._attention_with_score(sess, l, H, server_pscore not in ("none", "disabled") and c.n_prefix > 0,
-                                       sess.pscore[l])
+            self._attention_with_score(sess, l, H, server_pscore, sess.pscore[l])
         # x_out = x + ls1 * proj(o); bos[l] = ls1 * proj(o)
         a, sa = self._act(sess, sess.o, "proj")
         w, ws = self._w(lw, "proj")
@@ -451,23 +466,48 @@ class ViTEngine:
         K.gemm(a, w, x_out, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_out,
                aux=sess.bos[l], aux_mode=K.AUX_ADD, a_scale=sa, b_scale=ws)
 
-    def _attention_with_score(self, sess: Session, l: int, H: int, score: bool, score_out: torch.Tensor) -> None:
-        """Full attention of layer l; with `score`, the CLS softmax row (server patch score)
-        comes out of the same attention pass and is averaged over the heads into score_out."""
+    def _attention_with_score(self, sess: Session, l: int, H: int, kind: str, score_out: torch.Tensor) -> None:
+        """Full attention of layer l over H (local) heads, plus the server patch score `kind`
+        averaged over those heads into score_out [B, N] (reference attention.py:241-274):
+          cls_attn_prob*    the CLS softmax row, written by the same attention pass
+          patch_attn_prob*  column means of the probabilities: the attention pass also writes the
+                            row LSE, then one tcgen05 Q K^T pass sums exp(s - lse) per key
+          patch_pseudo*     softmax row of one pseudo query per (image, head)
+          none / disabled / random: no score from the attention (random draws at correction)."""
         B, N, Dh = sess.B, sess.N, self.cfg.head_dim
-        fused = score and K.ATTENTION_IMPL[0].startswith("tcgen05")
-        if score and not fused:
-            K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out)
-        K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh,
-                    cls_probs=sess.ps_scratch if fused else None)
-        if fused:
-            K.head_mean(sess.ps_scratch, B, H, N, score_out)
+        kind = _score_kind(kind)
+        if kind == "cls" and self.cfg.n_prefix == 0:
+            kind = "none"  # no CLS token to score with
+        if kind == "cls":
+            fused = K.ATTENTION_IMPL[0].startswith("tcgen05")
+            if not fused:
+                K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out)
+            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh,
+                        cls_probs=sess.ps_scratch if fused else None)
+            if fused:
+                K.head_mean(sess.ps_scratch, B, H, N, score_out)
+            return
+        if kind == "patch":
+            lse = sess.extra.get("lse")
+            if lse is None:
+                lse = sess.extra["lse"] = torch.empty(B, H, N, device=self.device, dtype=torch.float32)
+            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, lse=lse, impl="tcgen05")
+            K.attn_colsum_pscore(sess.q, sess.kc[l], lse, B=B, N=N, H=H, Dh=Dh, probs=sess.ps_scratch, out=score_out)
+            return
+        if kind == "pseudo":
+            pq = sess.extra.get("pseudo_q")
+            if pq is None:
+                pq = sess.extra["pseudo_q"] = torch.empty(B, H * Dh, device=self.device, dtype=BF16)
+            K.pseudo_query(sess.q, B=B, N=N, npre=self.cfg.n_prefix, H=H, Dh=Dh, out=pq)
+            K.query_attn_pscore(pq, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out)
+        K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh)
 
     def approx(self, sess: Session, start: int, end: int, server_pscore: str = "cls_attn_prob") -> torch.Tensor:
         """Approximate pass over layers [start, end) on the running features."""
         if start == 0:
             sess.x.copy_(sess.x_in)
             sess.extra.pop("layermean", None)  # a new request's approximate pass
+            sess.extra.pop("random_score", None)
         self._set_pass(sess, "approx")
         for l in range(start, end):
             self.approx_layer(sess, l, sess.x, sess.x, server_pscore)
@@ -494,7 +534,12 @@ class ViTEngine:
     # -------------------------------------------------------------- correction pass
     def plan(self, sess: Session, l: int, pre: torch.Tensor, cand: torch.Tensor, k: int, opts: Dict,
              mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None,
-             server: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+             server: Optional[torch.Tensor] = None, thres: Optional[float] = None,
+             dynamic: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Packed plan of layer l (block.py:360-560). Top-k: the k best candidates. Threshold
+        (`thres`): candidates scoring >= thres, at most k of them (the cap), padded with the last
+        kept one. dynamic: threshold without a cap; the plan is built at the full width, then one
+        host read of the largest kept count sizes it (the reference's builder syncs likewise)."""
         B = sess.B
         T = pre.shape[1] + k
         upd = sess.upd.view(-1)[: B * T].view(B, T)
@@ -502,9 +547,26 @@ class ViTEngine:
         if server is None:
             server = sess.pscore[l]
         sess.extra["plan_id"] = sess.extra.get("plan_id", 0) + 1
+        counts = None
+        if dynamic:
+            counts = sess.extra.get("plan_counts")
+            if counts is None:
+                counts = sess.extra["plan_counts"] = torch.zeros(B, device=self.device, dtype=torch.int32)
         K.correction_plan(server, pre, cand, k, upd, rows, mobile=mobile, ws=float(opts.get("server_pscore_weight", 1.0)),
                           wm=float(opts.get("mobile_pscore_weight", 0.0)), fusion=opts.get("pscore_fusion", "add"),
-                          valid=valid, stats=sess.plan_stats)
+                          valid=valid, stats=sess.plan_stats, thres=thres, counts=counts)
+        if dynamic:
+            kmax = min(int(counts.max().item()), k)
+            T2 = pre.shape[1] + kmax
+            u2 = sess.extra.get("upd_dyn")
+            if u2 is None or u2.numel() < sess.upd.numel():
+                u2 = sess.extra["upd_dyn"] = torch.empty_like(sess.upd)
+                sess.extra["rows_dyn"] = torch.empty_like(sess.rows)
+            upd2 = u2.view(-1)[: B * T2].view(B, T2)
+            upd2.copy_(upd[:, :T2])
+            rows2 = sess.extra["rows_dyn"][: B * T2]
+            rows2.view(B, T2).copy_(rows.view(B, T)[:, :T2])
+            return upd2, rows2
         return upd, rows
 
     def _window_bounds(self, sess: Session, upd: torch.Tensor):
@@ -554,34 +616,60 @@ class ViTEngine:
         pre: int32 [B, n_prefix] prefix token indices; cand: int32 [B, P_g] candidate patch tokens
         (the residual group that just arrived). Keeps k = int(P_g * token_keep_ratio) per image.
         """
-        st = self._correct_begin(sess, start, cand, opts)
+        st = self._correct_begin(sess, start, cand, opts, pre)
         if server is not None:  # caller-provided per-token score [B, N], one plan for every layer
             st["shared"] = server
         for l in range(start, end):
             self._correct_step(sess, l, st, pre, cand, opts, mobile, valid)
         return sess.x
 
-    def _correct_begin(self, sess: Session, start: int, cand: torch.Tensor, opts: Dict) -> Dict:
+    def _correct_begin(self, sess: Session, start: int, cand: torch.Tensor, opts: Dict,
+                       pre: Optional[torch.Tensor] = None) -> Dict:
         P_g = cand.shape[1]
         ratio = float(opts.get("token_keep_ratio", 0.2))
-        if opts.get("token_keep_thres") is not None:
-            raise NotImplementedError("threshold selection on the sm_100a engine uses token_keep_cap (sync-free)")
+        thres = opts.get("token_keep_thres")
+        cap = int(opts.get("token_keep_cap", 0) or 0)
         kind = str(opts.get("server_pscore", "cls_attn_prob"))
         if start == 0:
+            if opts.get("token_prune_enabled") and pre is not None:
+                # prune state of this correction segment from the drift between the running
+                # features and the fresh tokens (vision_transformer.py:453-489); like the
+                # reference, the correction itself does not consume it
+                dind = torch.cat([pre, cand], dim=1).to(torch.int32).contiguous()
+                sess.extra["prune_state"] = K.token_prune(
+                    sess.x, sess.x_in, sess.N, dind, pre.shape[1], float(opts.get("token_prune_threshold", 0.0)),
+                    int(opts.get("token_prune_min_keep", 1)))
             sess.x.copy_(sess.x_in)
         self._set_pass(sess, "correct")
         shared = None
-        if kind in LAYERMEAN_SERVER_PSCORES:
+        _score_kind(kind)  # unknown names raise
+        if kind == "random":  # one random score per request, shared by every layer
+            shared = sess.extra.get("random_score")
+            if shared is None:
+                # a generator of the engine's own, consumed in the same order on every
+                # tensor-parallel rank, so all ranks draw the same scores
+                if getattr(self, "_rand_gen", None) is None:
+                    self._rand_gen = torch.Generator(device=self.device)
+                    self._rand_gen.manual_seed(0)
+                shared = sess.extra["random_score"] = torch.rand(sess.B, sess.N, device=self.device,
+                                                                 generator=self._rand_gen)
+        elif kind in LAYERMEAN_SERVER_PSCORES:
             shared = sess.extra.get("layermean")
             if shared is None:  # mean over the approximate pass's layers, computed once per request
                 shared = sess.pscore[: max(sess.approx_done, 1)].mean(0)
                 sess.extra["layermean"] = shared
-        return {"k": min(int(P_g * ratio), P_g), "shared": shared, "upd": None, "rows": None}
+        if thres is not None:  # threshold selection: width = the cap, or dynamic (one host read)
+            k = min(cap, P_g) if cap > 0 else P_g
+            return {"k": k, "shared": shared, "upd": None, "rows": None, "thres": float(thres),
+                    "dynamic": cap <= 0}
+        return {"k": min(int(P_g * ratio), P_g), "shared": shared, "upd": None, "rows": None, "thres": None,
+                "dynamic": False}
 
     def _correct_step(self, sess: Session, l: int, st: Dict, pre, cand, opts, mobile, valid) -> None:
         if st["upd"] is None or st["shared"] is None:
             st["upd"], st["rows"] = self.plan(sess, l, pre, cand, st["k"], opts, mobile=mobile, valid=valid,
-                                              server=st["shared"])
+                                              server=st["shared"], thres=st.get("thres"),
+                                              dynamic=st.get("dynamic", False))
         self.correct_layer(sess, l, sess.x, st["upd"], st["rows"])
         self._tap(sess, l)
 

@@ -328,6 +328,37 @@ def cls_attn_pscore(q: torch.Tensor, k: torch.Tensor, *, B: int, N: int, H: int,
     return out
 
 
+def query_attn_pscore(qb: torch.Tensor, k: torch.Tensor, *, B: int, N: int, H: int, Dh: int,
+                      scratch: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None) -> torch.Tensor:
+    """Softmax over keys of ONE query per image, averaged over heads: qb bf16 [B, H*Dh]
+    (e.g. the pseudo queries), k [B*N, H*Dh] rows -> out fp32 [B, N]."""
+    if scale is None:
+        scale = Dh ** -0.5
+    _count(2)
+    lib().cls_attn_pscore(qb, k, B, N, H, Dh, float(scale), scratch, out, qb.stride(0))
+    return out
+
+
+def pseudo_query(q: torch.Tensor, *, B: int, N: int, npre: int, H: int, Dh: int, out: torch.Tensor) -> torch.Tensor:
+    """Pseudo query per (image, head) (reference attention.py:261-268): the mean of the patch
+    queries q[b*N + npre : (b+1)*N] rescaled to their mean norm -> out bf16 [B, H*Dh]."""
+    _count()
+    lib().pseudo_query(q, B, N, npre, H, Dh, out)
+    return out
+
+
+def attn_colsum_pscore(q: torch.Tensor, k: torch.Tensor, lse: torch.Tensor, *, B: int, N: int, H: int, Dh: int,
+                       probs: torch.Tensor, out: Optional[torch.Tensor], scale: Optional[float] = None) -> torch.Tensor:
+    """Column means of the attention probabilities (tcgen05): probs[b, h, j] = mean_i
+    exp(q_i . k_j * scale - lse[b, h, i]); out[b, j] = mean_h probs[b, h, j] (patch_attn_prob,
+    reference attention.py:258-260). lse: fp32 [B, H, N] from `attention(..., lse=...)`."""
+    if scale is None:
+        scale = Dh ** -0.5
+    _count(1 if out is None else 2)
+    lib().attn_colsum_pscore(q, k, lse, B, N, H, Dh, float(scale), probs, out, err_word(q.device))
+    return probs
+
+
 def head_mean(probs: torch.Tensor, B: int, H: int, N: int, out: torch.Tensor) -> torch.Tensor:
     """out[b, j] = mean over heads of probs[b, h, j]."""
     _count()
@@ -341,10 +372,33 @@ FUSION = {"add": 0, "multiply": 1, "geo_mean": 2}
 def correction_plan(server: torch.Tensor, pre: torch.Tensor, cand: torch.Tensor, k: int, upd: torch.Tensor,
                     rows: torch.Tensor, *, mobile: Optional[torch.Tensor] = None, ws: float = 1.0,
                     wm: float = 0.0, fusion: str = "add", valid: Optional[torch.Tensor] = None,
-                    stats: Optional[torch.Tensor] = None) -> None:
+                    stats: Optional[torch.Tensor] = None, thres: Optional[float] = None,
+                    counts: Optional[torch.Tensor] = None) -> None:
+    """Packed correction plan per image, on the device with no host synchronisation.
+
+    Top-k (thres None): the k highest combined scores, in ascending candidate order after the
+    prefix tokens. Threshold: candidates scoring >= thres; the first k of them (k is the cap) in
+    candidate order, short rows padded with their last kept candidate; counts[b] (int32)
+    receives the number of candidates that passed the threshold."""
     _count()
     lib().correction_plan(server, pre, cand, mobile, float(ws), float(wm), FUSION.get(fusion, 0), valid, int(k),
-                          upd, rows, stats)
+                          upd, rows, stats, None if thres is None else float(thres), counts)
+
+
+def token_prune(x: torch.Tensor, x_ref: torch.Tensor, N: int, dindice: torch.Tensor, npre: int, threshold: float,
+                min_keep: int):
+    """Token-prune select + compact (reference triton_kernels/token_prune.py:9-89): per image,
+    score = mean |x - x_ref| over channels of the tokens dindice[b] (rows b*N + dindice); keep
+    the prefix, the patches scoring >= threshold, or the min_keep best patches when fewer pass.
+    Returns (dindice_sel [B, M], query_pos [B, M], valid [B, M] bool, kept_count [B])."""
+    B, M = dindice.shape
+    dsel = torch.empty(B, M, device=x.device, dtype=torch.int32)
+    qpos = torch.empty_like(dsel)
+    valid = torch.empty(B, M, device=x.device, dtype=torch.bool)
+    count = torch.empty(B, device=x.device, dtype=torch.int32)
+    _count()
+    lib().token_prune(x, x_ref, N, dindice, npre, float(threshold), int(min_keep), dsel, qpos, valid, count)
+    return dsel, qpos, valid, count
 
 
 def pyrup_add(src: torch.Tensor, res: Optional[torch.Tensor], out: torch.Tensor) -> torch.Tensor:

@@ -33,8 +33,10 @@ class SymTensor:
 
 @dataclass
 class BarrierChannel:
+    """Flags of one barrier: slots [0, 8) written by the ranks, slot 8 the local epoch counter
+    (kept on the device, so barriers can be captured into CUDA graphs and replayed)."""
+
     flags: SymTensor
-    epoch: int = 0
 
 
 class TPComm:
@@ -52,7 +54,7 @@ class TPComm:
 
     def channel(self) -> "BarrierChannel":
         """An independent barrier (own flags and epoch), for work issued on its own stream."""
-        return BarrierChannel(self.empty((MAX_RANKS,), torch.int32))
+        return BarrierChannel(self.empty((2 * MAX_RANKS,), torch.int32))
 
     # ------------------------------------------------------------------ buffers
     def empty(self, shape: Sequence[int], dtype: torch.dtype) -> SymTensor:
@@ -97,9 +99,8 @@ class TPComm:
         if self.world == 1:
             return
         ch = ch or self._default
-        ch.epoch = (ch.epoch + 1) & 0x7FFFFFFF
         _count()
-        lib().tp_barrier(ch.flags.ptrs, self.rank, ch.epoch, self.err)
+        lib().tp_barrier(ch.flags.ptrs, self.rank, self.err)
 
     def sp_row(self, M: int, D: int, rows_per_rank: int, *, tok=None, src: Optional[Tuple[List[int], List[int]]] = None,
                bias=None, gamma=None, resid=None, resid_tok: bool = True, resid2=None,

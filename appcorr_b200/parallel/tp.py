@@ -32,7 +32,7 @@ from typing import Dict, Optional
 import torch
 
 from ..models.dinov3.vit import ViTConfig
-from ..models.engine import BF16, EngineWeights, LayerW, Session, ViTEngine, random_weights
+from ..models.engine import BF16, EngineWeights, LayerW, Session, ViTEngine, _score_kind, random_weights
 from ..models.weights import SWIGLU_BLOCK, pack_swiglu, unpack_swiglu
 from ..ops import kernels as K
 from ..utils.tracing import PhaseTimer
@@ -246,9 +246,9 @@ class ViTEngineTP(ViTEngine):
         with tm("a.qkv"):
             K.qkv_gemm(a, w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
                        rope=sess.rope, n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
-        score = server_pscore not in ("none", "disabled")
+        score = _score_kind(server_pscore) != "none"
         with tm("a.attn"):
-            self._attention_with_score(sess, l, self.local_heads, score, e["sym_ps"].local)
+            self._attention_with_score(sess, l, self.local_heads, server_pscore, e["sym_ps"].local)
         with tm("a.quant"):
             a, sa = self._act(sess, sess.o, "proj")
         w, ws = self._w(lw, "proj")
@@ -308,6 +308,7 @@ class ViTEngineTP(ViTEngine):
         if start == 0:
             sess.x.copy_(sess.x_in)
             sess.extra.pop("layermean", None)
+            sess.extra.pop("random_score", None)
         self._set_pass(sess, "approx")
         sess.extra["approx_end"] = end
         if start < end:
@@ -325,6 +326,7 @@ class ViTEngineTP(ViTEngine):
         else:  # micro-batches interleaved layer by layer on their own streams
             if start == 0:
                 sess.extra.pop("layermean", None)
+                sess.extra.pop("random_score", None)
             streams = self._fork(len(subs))
             for sub, st in zip(subs, streams):
                 with torch.cuda.stream(st):
@@ -341,6 +343,10 @@ class ViTEngineTP(ViTEngine):
 
     def correct(self, sess: Session, start: int, end: int, pre: torch.Tensor, cand: torch.Tensor, opts: Dict,
                 mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if opts.get("token_prune_enabled"):
+            # the prune scores read every token row of the running features, which are split by
+            # rows across the ranks here
+            raise NotImplementedError("token_prune_enabled is supported by the one-GPU engine only")
         subs = sess.extra.get("subs")
         if subs is None:
             return super().correct(sess, start, end, pre, cand, opts, mobile=mobile, valid=valid)
@@ -353,7 +359,7 @@ class ViTEngineTP(ViTEngine):
         states = []
         for i, (sub, st) in enumerate(zip(subs, streams)):
             with torch.cuda.stream(st):
-                states.append(self._correct_begin(sub, start, part(cand, i), opts))
+                states.append(self._correct_begin(sub, start, part(cand, i), opts, part(pre, i)))
         for l in range(start, end):
             for i, (sub, st) in enumerate(zip(subs, streams)):
                 with torch.cuda.stream(st):

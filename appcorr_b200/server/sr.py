@@ -45,7 +45,7 @@ class LowResSR:
         p = PRESETS.get(name, PRESETS["realesrgan_x4plus"])
         self.scale = p["scale"]
         net = RRDBNet(**p)
-        path = os.path.join(os.path.expanduser(str(cfg.get("weights_dir", ""))), f"{name}.pth")
+        path = os.path.join(os.path.expanduser(str(cfg.get("weights_dir") or "")), f"{name}.pth")
         if os.path.exists(path):
             net.load_state_dict(convert_realesrgan_state(torch.load(path, map_location="cpu", weights_only=True)))
         else:

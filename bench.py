@@ -37,7 +37,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
 BASELINE_METRIC = "corrected-result p50/p99 latency & images/s, ViT-7B TP at 1/2/4/8 B200"
-# BASELINE.md publishes no images/s figure for this config, so vs_baseline is null.
+# The reference publishes no images/s figure for this config, so vs_baseline is null.
 BASELINE_VALUE = None
 
 
@@ -53,7 +53,7 @@ def parse_args():
     ap.add_argument("--arch", default="vit7b16")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-graph", action="store_true",
-                    help="1 GPU: time the device step eagerly instead of replaying its CUDA graph")
+                    help="time the device step eagerly instead of replaying its CUDA graph")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--precision", default="nvfp4", choices=["bf16", "fp8", "nvfp4"],
                     help="GEMM operand precision of the approx and correct passes (ours; the reference arm "
@@ -235,10 +235,10 @@ def run_mine(args, rank, world):
     torch.cuda.synchronize()
     step_fn = device_step
     graphed = False
-    if world == 1 and not args.no_graph:
+    if not args.no_graph:
         # the whole step (pyramid decode, approx, plan, correct, head) has no host synchronisation,
-        # so it is captured once and replayed; multi-GPU steps stay eager (their barrier epochs
-        # are host counters)
+        # so it is captured once and replayed; tensor-parallel barriers keep their epochs on the
+        # device, so a replay on every rank takes fresh epochs
         graph = torch.cuda.CUDAGraph()
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())

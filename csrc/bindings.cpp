@@ -191,4 +191,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_msda_ops(m);
   register_conv_ops(m);
   register_attention_sm100_ops(m);
+  register_pscore_sm100_ops(m);
+  register_token_prune_ops(m);
 }

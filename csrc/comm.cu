@@ -6,9 +6,10 @@
 // kernel can load and store another GPU's buffer directly; no library collective is involved.
 //
 //   ipc_alloc / ipc_open / ipc_close / ipc_free   symmetric buffer management
-//   tp_barrier          every rank stores `epoch` into slot [my_rank] of every peer's flag array,
-//                       then waits (bounded, ~1 s) until its own slots reach `epoch`; release /
-//                       acquire at system scope make the preceding writes visible
+//   tp_barrier          every rank advances its device-side epoch counter, stores the epoch into
+//                       slot [my_rank] of every peer's flag array, then waits (bounded, ~1 s)
+//                       until its own slots reach it; release / acquire at system scope make the
+//                       preceding writes visible. Graph-capturable: no host-side state.
 //   tp_mean_f32         small fp32 all-reduce (mean) of per-rank vectors (patch scores)
 // The reduce-scatter and all-gather of the layer activations are fused into the GEMM epilogue
 // (csrc/gemm_sm100.cu, rs_out) and into the owner-side row kernel (csrc/tp_sp.cu).
@@ -71,15 +72,24 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// flags: per rank an array of kMaxRanks uint32 slots (slot s written by rank s).
-__global__ void tp_barrier_kernel(PeerPtrs flags, int rank, int world, uint32_t epoch, int* err) {
+// flags: per rank an array of kFlagWords uint32: slots [0, kMaxRanks) are written by the ranks
+// (slot s by rank s); slot kMaxRanks is this rank's own epoch counter. The epoch lives in device
+// memory, so a captured barrier (CUDA graph) takes a fresh epoch on every replay. Barriers of one
+// channel run in stream order on every rank, so the counters of all ranks stay equal.
+constexpr int kFlagWords = 16;
+__global__ void tp_barrier_kernel(PeerPtrs flags, int rank, int world, int* err) {
   const int t = threadIdx.x;
+  __shared__ uint32_t s_epoch;
+  uint32_t* counter = reinterpret_cast<uint32_t*>(flags.p[rank]) + kMaxRanks;
+  if (t == 0) s_epoch = (*counter + 1u) & 0x7FFFFFFFu;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
   __threadfence_system();
   if (t < world) st_release_sys(reinterpret_cast<uint32_t*>(flags.p[t]) + rank, epoch);
   if (t < world) {
     const uint32_t* mine = reinterpret_cast<const uint32_t*>(flags.p[rank]) + t;
     const uint64_t t0 = global_timer_ns();
-    while (static_cast<int32_t>(ld_acquire_sys(mine) - epoch) < 0) {
+    while (static_cast<int32_t>((ld_acquire_sys(mine) - epoch) << 1) < 0) {
       if (global_timer_ns() - t0 > kWaitBudgetNs) {
         record_error(err, kErrTimeoutPeer);
         break;
@@ -87,15 +97,16 @@ __global__ void tp_barrier_kernel(PeerPtrs flags, int rank, int world, uint32_t 
     }
   }
   __syncthreads();
+  if (t == 0) *counter = epoch;
 }
 
-void tp_barrier_op(std::vector<int64_t> flag_ptrs, int64_t rank, int64_t epoch, const at::Tensor& err) {
+void tp_barrier_op(std::vector<int64_t> flag_ptrs, int64_t rank, const at::Tensor& err) {
   const int world = static_cast<int>(flag_ptrs.size());
   TORCH_CHECK(world >= 1 && world <= kMaxRanks, "tp_barrier: 1..8 ranks");
   PeerPtrs f{};
   for (int i = 0; i < world; ++i) f.p[i] = reinterpret_cast<void*>(flag_ptrs[i]);
   tp_barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(f, static_cast<int>(rank), world,
-                                                                    static_cast<uint32_t>(epoch), err.data_ptr<int>());
+                                                                    err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

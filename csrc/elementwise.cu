@@ -771,18 +771,19 @@ void scatter_rows_op(const at::Tensor& src, const at::Tensor& rows, at::Tensor& 
 }
 
 // ------------------------------------------------------------------------------ CLS attention pscore
-// grid (B, H). q: [B*N, H*Dh] rows (only row b*N of each image is read), k: [B*N, H*Dh].
-// probs: fp32 [B, H, N] = softmax over keys of the CLS query. A second pass averages over heads.
+// grid (B, H). q: image b's query row at q + b * q_bstride (row b*N of [B*N, H*Dh] rows for the
+// CLS query: q_bstride = N * ld; a [B, H*Dh] pseudo-query buffer: q_bstride = H*Dh), k: [B*N, H*Dh].
+// probs: fp32 [B, H, N] = softmax over keys of that query. A second pass averages over heads.
 constexpr int kPsThreads = 256;
 
 __global__ void __launch_bounds__(kPsThreads) cls_attn_probs_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                                    long ld, int N, int H, int Dh, float scale,
-                                                                    float* __restrict__ probs) {
+                                                                    long ld, long q_bstride, int N, int H, int Dh,
+                                                                    float scale, float* __restrict__ probs) {
   extern __shared__ float s_buf[];  // [N] logits, then [Dh] query
   __shared__ float red[kPsThreads / 32];
   const int b = blockIdx.x, h = blockIdx.y;
   float* qs = s_buf + N;
-  const bf16* qrow = q + (long)b * N * ld + (long)h * Dh;
+  const bf16* qrow = q + (long)b * q_bstride + (long)h * Dh;
   for (int d = threadIdx.x; d < Dh; d += kPsThreads) qs[d] = __bfloat162float(qrow[d]);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -826,9 +827,16 @@ __global__ void head_mean_kernel(const float* __restrict__ probs, int B, int H, 
 }
 
 void cls_attn_pscore_op(const at::Tensor& q, const at::Tensor& k, int64_t B, int64_t N, int64_t H, int64_t Dh,
-                        double scale, at::Tensor& scratch, at::Tensor& out) {
+                        double scale, at::Tensor& scratch, at::Tensor& out, int64_t q_bstride) {
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16, "cls_attn_pscore: bf16");
-  TORCH_CHECK(q.stride(0) == k.stride(0), "cls_attn_pscore: q and k share a row stride");
+  // q_bstride < 0: the CLS row of [B*N, H*Dh] q rows sharing k's row stride
+  if (q_bstride < 0) {
+    TORCH_CHECK(q.stride(0) == k.stride(0), "cls_attn_pscore: q and k share a row stride");
+    q_bstride = N * q.stride(0);
+  } else {
+    TORCH_CHECK(q.is_contiguous() && q.numel() >= (B - 1) * q_bstride + H * Dh, "cls_attn_pscore: query buffer too small");
+  }
+  TORCH_CHECK(k.stride(0) % 2 == 0 && q_bstride % 2 == 0, "cls_attn_pscore: even row strides");
   TORCH_CHECK(scratch.scalar_type() == at::kFloat && scratch.numel() >= B * H * N, "cls_attn_pscore: scratch fp32 [B,H,N]");
   TORCH_CHECK(out.scalar_type() == at::kFloat && out.numel() == B * N && out.is_contiguous(), "cls_attn_pscore: out fp32 [B,N]");
   TORCH_CHECK(Dh % 64 == 0, "cls_attn_pscore: Dh multiple of 64");
@@ -839,7 +847,7 @@ void cls_attn_pscore_op(const at::Tensor& q, const at::Tensor& k, int64_t B, int
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(cls_attn_probs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   cls_attn_probs_kernel<<<dim3(B, H), kPsThreads, smem, st>>>(
-      reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()), q.stride(0),
+      reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()), k.stride(0), q_bstride,
       static_cast<int>(N), static_cast<int>(H), static_cast<int>(Dh), static_cast<float>(scale), scratch.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   head_mean_kernel<<<static_cast<int>(std::max<long>(1, (B * N + 255) / 256)), 256, 0, st>>>(
@@ -867,7 +875,8 @@ __device__ __forceinline__ uint32_t f32_order_key(float f) {
 __global__ void __launch_bounds__(kPlanThreads) correction_plan_kernel(
     const float* __restrict__ server, int N, const int* __restrict__ pre, int npre, const int* __restrict__ cand, int P,
     const float* __restrict__ mobile, float ws, float wm, int fusion, const uint8_t* __restrict__ valid, int k,
-    int* __restrict__ upd, int* __restrict__ rows, float* __restrict__ stats) {
+    int* __restrict__ upd, int* __restrict__ rows, float* __restrict__ stats, int use_thres, float thres,
+    int* __restrict__ counts) {
   extern __shared__ uint32_t sm[];
   uint32_t* keys = sm;                                  // [P]
   float* sc = reinterpret_cast<float*>(sm + P);         // [P]
@@ -894,6 +903,12 @@ __global__ void __launch_bounds__(kPlanThreads) correction_plan_kernel(
     if (isfinite(s)) full += s;
   }
   full = block_sum<kPlanThreads>(full, red);
+  if (use_thres) {
+    // Threshold selection (block.py:373-375): keep every candidate scoring >= thres; the plan
+    // holds the first k of them in candidate order (k = the cap) and is padded below.
+    for (int i = threadIdx.x; i < P; i += kPlanThreads) flag[i] = sc[i] >= thres ? 1 : 0;
+    __syncthreads();
+  } else {
   // Radix select the k-th largest key, 8 bits per pass, most significant first.
   if (threadIdx.x == 0) { s_prefix = 0; s_remaining = k; }
   __syncthreads();
@@ -935,6 +950,7 @@ __global__ void __launch_bounds__(kPlanThreads) correction_plan_kernel(
     }
   }
   __syncthreads();
+  }
   // Block-wide exclusive scan over flags in chunks of kPlanThreads, emitting kept candidates in order.
   float kept = 0.f;
   int base = 0;
@@ -958,12 +974,26 @@ __global__ void __launch_bounds__(kPlanThreads) correction_plan_kernel(
     if (f) {
       const int pos = base + woff + incl - 1;
       const int tok = cand[(long)b * P + i];
-      upd[(long)b * T + npre + pos] = tok;
-      rows[(long)b * T + npre + pos] = b * N + tok;
+      if (pos < k) {  // top-k: always; threshold: the first k (the cap) kept candidates
+        upd[(long)b * T + npre + pos] = tok;
+        rows[(long)b * T + npre + pos] = b * N + tok;
+      }
       if (isfinite(sc[i])) kept += sc[i];
     }
     base += tot;
     __syncthreads();
+  }
+  if (use_thres) {
+    // Pad the unused tail with the row's last kept candidate (the first candidate if none was
+    // kept), as the sync-free threshold builder does (block.py:495-560): a duplicated row is
+    // corrected twice with identical results, so the padding changes nothing.
+    const int nk = min(base, k);
+    const int fill = nk > 0 ? upd[(long)b * T + npre + nk - 1] : (P > 0 ? cand[(long)b * P] : 0);
+    for (int pos = nk + threadIdx.x; pos < k; pos += kPlanThreads) {
+      upd[(long)b * T + npre + pos] = fill;
+      rows[(long)b * T + npre + pos] = b * N + fill;
+    }
+    if (threadIdx.x == 0 && counts != nullptr) counts[b] = base;
   }
   for (int i = threadIdx.x; i < npre; i += kPlanThreads) {
     const int tok = pre[(long)b * npre + i];
@@ -980,7 +1010,8 @@ __global__ void __launch_bounds__(kPlanThreads) correction_plan_kernel(
 void correction_plan_op(const at::Tensor& server, const at::Tensor& pre, const at::Tensor& cand,
                         c10::optional<at::Tensor> mobile, double ws, double wm, int64_t fusion,
                         c10::optional<at::Tensor> valid, int64_t k, at::Tensor& upd, at::Tensor& rows,
-                        c10::optional<at::Tensor> stats) {
+                        c10::optional<at::Tensor> stats, c10::optional<double> thres,
+                        c10::optional<at::Tensor> counts) {
   TORCH_CHECK(server.scalar_type() == at::kFloat && server.dim() == 2 && server.is_contiguous(), "plan: server fp32 [B,N]");
   const int B = static_cast<int>(server.size(0)), N = static_cast<int>(server.size(1));
   TORCH_CHECK(cand.scalar_type() == at::kInt && cand.dim() == 2 && cand.size(0) == B && cand.is_contiguous(), "plan: cand int32 [B,P]");
@@ -1004,6 +1035,11 @@ void correction_plan_op(const at::Tensor& server, const at::Tensor& pre, const a
     TORCH_CHECK(stats->scalar_type() == at::kFloat && stats->numel() >= 2L * B, "plan: stats fp32 [B,2]");
     sp = stats->data_ptr<float>();
   }
+  int* cp = nullptr;
+  if (counts.has_value()) {
+    TORCH_CHECK(counts->scalar_type() == at::kInt && counts->numel() >= B, "plan: counts int32 [B]");
+    cp = counts->data_ptr<int>();
+  }
   const size_t smem = 3 * sizeof(uint32_t) * P;
   TORCH_CHECK(smem <= 190 * 1024, "plan: too many candidates");
   c10::cuda::CUDAGuard g(server.device());
@@ -1011,7 +1047,8 @@ void correction_plan_op(const at::Tensor& server, const at::Tensor& pre, const a
     cudaFuncSetAttribute(correction_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   correction_plan_kernel<<<B, kPlanThreads, smem, at::cuda::getCurrentCUDAStream()>>>(
       server.data_ptr<float>(), N, pre.data_ptr<int>(), npre, cand.data_ptr<int>(), P, mp, static_cast<float>(ws),
-      static_cast<float>(wm), static_cast<int>(fusion), vp, static_cast<int>(k), upd.data_ptr<int>(), rows.data_ptr<int>(), sp);
+      static_cast<float>(wm), static_cast<int>(fusion), vp, static_cast<int>(k), upd.data_ptr<int>(), rows.data_ptr<int>(), sp,
+      thres.has_value() ? 1 : 0, thres.has_value() ? static_cast<float>(*thres) : 0.f, cp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1177,10 +1214,11 @@ void register_elementwise_ops(pybind11::module_& m) {
   m.def("set_prefix", &set_prefix_op);
   m.def("gather_rows", &gather_rows_op);
   m.def("scatter_rows", &scatter_rows_op);
-  m.def("cls_attn_pscore", &cls_attn_pscore_op);
+  m.def("cls_attn_pscore", &cls_attn_pscore_op, py::arg("q"), py::arg("k"), py::arg("B"), py::arg("N"), py::arg("H"),
+        py::arg("Dh"), py::arg("scale"), py::arg("scratch"), py::arg("out"), py::arg("q_bstride") = -1);
   m.def("correction_plan", &correction_plan_op, py::arg("server"), py::arg("pre"), py::arg("cand"), py::arg("mobile"),
         py::arg("ws"), py::arg("wm"), py::arg("fusion"), py::arg("valid"), py::arg("k"), py::arg("upd"), py::arg("rows"),
-        py::arg("stats") = py::none());
+        py::arg("stats") = py::none(), py::arg("thres") = py::none(), py::arg("counts") = py::none());
   m.def("pyrup_add", &pyrup_add_op);
   m.def("upsample_argmax", &upsample_argmax_op);
   m.def("mean_rows", &mean_rows_op);

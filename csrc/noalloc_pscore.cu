@@ -12,8 +12,8 @@
 namespace appcorr {
 // The two kernels of the regular `cls_attn_pscore` op (csrc/elementwise.cu); this entry point
 // launches them unchanged and only supplies a different probability buffer.
-__global__ void cls_attn_probs_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k, long ld, int N, int H, int Dh,
-                                      float scale, float* probs);
+__global__ void cls_attn_probs_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k, long ld, long q_bstride, int N,
+                                      int H, int Dh, float scale, float* probs);
 __global__ void head_mean_kernel(const float* probs, int B, int H, int N, float* out);
 }  // namespace appcorr
 
@@ -83,7 +83,7 @@ extern "C" __attribute__((visibility("default"))) int appcorr_cls_attn_pscore_no
   if (cudaPeekAtLastError() != cudaSuccess)
     return fail(APPCORR_NOALLOC_ERR_CUDA, "appcorr_cls_attn_pscore_noalloc: a CUDA error was pending before this call");
   appcorr::cls_attn_probs_kernel<<<dim3(B, H), kProbThreads, smem, stream>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), ld, N, H, head_dim, scale, scratch);
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), ld, (long)N * ld, N, H, head_dim, scale, scratch);
   if (cudaPeekAtLastError() != cudaSuccess)
     return fail(APPCORR_NOALLOC_ERR_CUDA, "appcorr_cls_attn_pscore_noalloc: probability kernel launch failed");
   const long total = (long)B * N;

@@ -12,4 +12,6 @@ void register_sp_ops(pybind11::module_& m);
 void register_msda_ops(pybind11::module_& m);
 void register_conv_ops(pybind11::module_& m);
 void register_attention_sm100_ops(pybind11::module_& m);
+void register_pscore_sm100_ops(pybind11::module_& m);
+void register_token_prune_ops(pybind11::module_& m);
 }  // namespace appcorr

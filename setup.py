@@ -2,8 +2,8 @@
 
     python setup.py build_ext --inplace
 
-produces appcorr_b200/_C*.so (CUDA kernels + pybind11 bindings) and
-appcorr_b200/_runtime*.so (host-side C++ runtime: codec, ring, scheduler helpers).
+produces appcorr_b200/_C*.so (CUDA kernels + pybind11 bindings) and, from csrc/runtime/,
+appcorr_b200/_runtime*.so (host-side C++ runtime).
 """
 import glob
 import os
