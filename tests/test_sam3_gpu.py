@@ -125,3 +125,54 @@ def np_isfinite(a):
     import numpy as np
 
     return bool(np.isfinite(a).all())
+
+
+def test_vggt_interleaved_walk_recovers_full_inference():
+    """The VGGTInterleaved schedule on the 48-stage axis (here the tiny tower's 6 stages): approx
+    [0, 3) on the base frames, a round that corrects [0, 3) and approximates [3, 6), then a final
+    correction of [0, 6). With every token kept, the corrected result equals full inference on the
+    final frames; a round whose patches cover one frame corrects only that frame's tokens."""
+    from appcorr_b200.common.protocol import ExperimentConfig, Patch, Task
+    from appcorr_b200.server.model import get_model_executor
+
+    cfg = ExperimentConfig(exp_id="t", model_name="vggt", batch_size=3, image_shape=(128, 128, 3),
+                           input_profile_kwargs={"vggt_arch": "vggt_tiny"},
+                           appcorr_kwargs={"token_keep_ratio": 1.0}, patch_size=(16, 16))
+    ex = get_model_executor("vggt", DEV)
+    ex.load_model("vggt", cfg)
+    g = torch.Generator().manual_seed(0)
+    base = torch.randint(0, 256, (3, 128, 128, 3), dtype=torch.uint8, generator=g)
+    final = torch.randint(0, 256, (3, 128, 128, 3), dtype=torch.uint8, generator=g)
+    t0 = Task(task_id=0, request_id=0, payload=[], instructions=[])
+    ctx = {}
+    ex.preprocess(base, t0, ctx, cfg)
+    ex.prepare_tokens(t0, ctx, cfg)
+    ex.approx_forward({"layers": (0, 3)}, ctx, cfg)
+    # round 1: patches of frame 1 only
+    p1 = [Patch(image_idx=1, spatial_idx=i, data=b"", res_level=0, group_id=1) for i in range(64)]
+    t1 = Task(task_id=1, request_id=0, payload=p1, instructions=[])
+    ex.preprocess(final, t1, ctx, cfg)
+    ex.prepare_tokens(t1, ctx, cfg)
+    arrived = ctx["vggt_arrived"]
+    assert arrived.shape[1] == 64 and int(arrived.min()) == 64 and int(arrived.max()) == 127
+    ex.correct_forward({"layers": (0, 3)}, ctx, cfg)
+    ex.approx_forward({"layers": (3, 6)}, ctx, cfg)
+    # final round: every token
+    t2 = Task(task_id=2, request_id=0, payload=[], instructions=[])
+    ex.preprocess(final, t2, ctx, cfg)
+    ex.prepare_tokens(t2, ctx, cfg)
+    ex.correct_forward({"layers": (0, 6)}, ctx, cfg)
+    ex.head_inference(t2, ctx, cfg)
+    got = ex.get_final_results(t2, ctx, cfg)[0]
+    ctx2 = {}
+    ex2 = get_model_executor("vggt", DEV)
+    ex2.load_model("vggt", cfg)
+    ex2.preprocess(final, t2, ctx2, cfg)
+    ex2.prepare_tokens(t2, ctx2, cfg)
+    ex2.full_inference(t2, ctx2, cfg)
+    ref = ex2.get_final_results(t2, ctx2, cfg)[0]
+    import numpy as np
+
+    for key in ("depth", "pose_enc"):
+        a, b = got[key].astype(np.float64), ref[key].astype(np.float64)
+        assert np.linalg.norm(a - b) / np.linalg.norm(b) < 2e-2, key
