@@ -120,6 +120,16 @@ class TPComm:
                      (ag.local.stride(0) if ag is not None else 0), ag_scale.ptrs if mode else [],
                      ag_sf.ptrs if mode == 2 else [])
 
+    def push_rows(self, src: int, dst: List[int], tok: Optional[torch.Tensor], M: int, D: int,
+                  rows_per_rank: int) -> None:
+        """Copy every packed bf16 row i of `src` [M, D] whose owner (tok[i] // rows_per_rank, or
+        i // rows_per_rank) is another rank into row i of that owner's `dst[owner]`
+        (coalesced peer stores; the sending half of a reduce-scatter)."""
+        if self.world == 1:
+            return
+        _count()
+        lib().sp_push_rows(int(src), [int(p) for p in dst], tok, int(M), int(D), int(rows_per_rank), self.rank)
+
     def mean_f32(self, src: SymTensor, dst: torch.Tensor) -> None:
         _count()
         lib().tp_mean_f32(src.ptrs, dst)

@@ -90,9 +90,11 @@ class ViTEngineTP(ViTEngine):
         # kernel) or "push" (GEMM epilogue stores partial rows into the owner's slots)
         # "ce": contiguous row blocks (approximate pass) travel by copy-engine peer copies into the
         # owners' slots, packed correction rows are pulled
+        # "pushk": the GEMM writes locally, then a row kernel pushes every row owned by a peer
+        # into the owner's slot with coalesced peer stores; owners reduce from local memory
         self.rs_mode = os.environ.get("APPCORR_TP_RS", "pull")
-        if self.rs_mode not in ("pull", "push", "ce"):
-            raise ValueError("APPCORR_TP_RS must be 'pull', 'push' or 'ce'")
+        if self.rs_mode not in ("pull", "push", "ce", "pushk"):
+            raise ValueError("APPCORR_TP_RS must be 'pull', 'push', 'pushk' or 'ce'")
 
     @classmethod
     def from_full(cls, full: EngineWeights, comm: TPComm, precision="bf16") -> "ViTEngineTP":
@@ -162,7 +164,8 @@ class ViTEngineTP(ViTEngine):
         sess.extra.update({
             "R": R, "chan": comm.channel(), "sym_xg": xg, "sym_xg8": xg8, "sym_xg4": xg4,
             "sym_xg_scale": comm.empty((M,), torch.float32),
-            "sym_part": (comm.empty((self.world, M, D), BF16) if self.rs_mode == "push" else comm.empty((M, D), BF16)),
+            "sym_part": (comm.empty((self.world, M, D), BF16) if self.rs_mode in ("push", "pushk")
+                         else comm.empty((M, D), BF16)),
             "sym_slot": comm.empty((self.world, M, D), BF16) if self.rs_mode == "ce" else None,
             "sym_ps": comm.empty((B, sess.N), torch.float32),
             "sym_feat": comm.empty((B * sess.P, D), BF16)})
@@ -199,6 +202,13 @@ class ViTEngineTP(ViTEngine):
         if self.rs_mode == "push":  # partial rows stored into their owners' slots by the epilogue
             K.gemm(a, w, None, out_rows=rows_out, a_scale=a_scale, b_scale=b_scale,
                    rs=(e["sym_part"].ptrs, e["R"], self.rank, n, self.cfg.embed_dim))
+        elif self.rs_mode == "pushk":  # local GEMM into my slot, then a push of the peers' rows
+            D = self.cfg.embed_dim
+            part = e["sym_part"]
+            mine = part.local.view(-1)[self.rank * n * D:(self.rank + 1) * n * D].view(n, D)
+            K.gemm(a, w, mine, a_scale=a_scale, b_scale=b_scale)
+            self.comm.push_rows(part.view_ptrs(self.rank * n * D)[self.rank], part.view_ptrs(self.rank * n * D),
+                                rows_out, n, D, e["R"])
         else:
             K.gemm(a, w, e["sym_part"].local[:n], a_scale=a_scale, b_scale=b_scale)
 
@@ -225,7 +235,7 @@ class ViTEngineTP(ViTEngine):
         """Where the owner finds row i of every rank's partial product (pointers, row offsets)."""
         e = sess.extra
         part = e["sym_part"]
-        if self.rs_mode == "push":
+        if self.rs_mode in ("push", "pushk"):
             return [part.ptrs[self.rank]] * self.world, [s * n for s in range(self.world)]
         if self.rs_mode == "ce" and contiguous:
             ptrs = [e["sym_slot"].ptrs[self.rank]] * self.world

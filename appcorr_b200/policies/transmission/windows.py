@@ -87,8 +87,52 @@ def _assign_with_crop_cover(strategy, items, num_groups, config=None, rng=None):
     return assign_groups(strategy, items, num_groups, config, rng)
 
 
-class NYUAppCorrProgressiveLaplacianPolicy(ProgressiveLPyramidPolicy):
-    pass
+class FixedModelGridMixin:
+    """NYU depther transmission on the depther's fixed model grid (reference
+    nyu_appcorr_progressive.py:15-84): input-shape preservation is always off, so every pyramid
+    level is cut on config.image_shape / 2**level, and whatever a decode produces is resized to
+    config.image_shape (area interpolation when shrinking, bilinear when enlarging)."""
+
+    @staticmethod
+    def preserve_shape(config: ExperimentConfig) -> bool:
+        return False
+
+    @staticmethod
+    def model_hw(config: ExperimentConfig):
+        return int(config.image_shape[0]), int(config.image_shape[1])
+
+    @staticmethod
+    def to_model_grid(image: np.ndarray, h: int, w: int) -> np.ndarray:
+        import cv2
+
+        image = np.ascontiguousarray(image)
+        if image.shape[:2] == (h, w):
+            return image
+        interp = cv2.INTER_LINEAR if (h > image.shape[0] or w > image.shape[1]) else cv2.INTER_AREA
+        return np.ascontiguousarray(cv2.resize(image, (w, h), interpolation=interp))
+
+    def fit_decoded(self, decoded, config: ExperimentConfig):
+        h, w = self.model_hw(config)
+        if isinstance(decoded, list):
+            out = []
+            for item in decoded:
+                if isinstance(item, dict) and item.get("image") is not None:
+                    item = dict(item)
+                    item["image"] = self.to_model_grid(item["image"], h, w)
+                elif isinstance(item, np.ndarray):
+                    item = self.to_model_grid(item, h, w)
+                out.append(item)
+            return out
+        if isinstance(decoded, np.ndarray) and decoded.ndim == 4 and decoded.shape[1:3] != (h, w):
+            return np.stack([self.to_model_grid(im, h, w) for im in decoded])
+        return decoded
+
+    def decode(self, patches, config: ExperimentConfig, canvas=None):
+        return self.fit_decoded(super().decode(patches, config, canvas=canvas), config)
+
+
+class NYUAppCorrProgressiveLaplacianPolicy(FixedModelGridMixin, ProgressiveLPyramidPolicy):
+    """Progressive Laplacian NYU transmission decoded onto the fixed model grid."""
 
 
 class VGGTLaplacianPolicy(ProgressiveLPyramidPolicy):

@@ -91,7 +91,7 @@ class WorkerModule(multiprocessing.Process):
     # ------------------------------------------------------------------ decoder thread
     def _pyramid_on_gpu(self) -> bool:
         return (self.device.type == "cuda" and hasattr(self.policy, "decode_pyramid")
-                and not bool(self.config.transmission_kwargs.get("preserve_input_shape", False))
+                and not self.policy.preserve_shape(self.config)
                 and type(self.policy).__name__ in {"LaplacianPyramidPolicy", "ProgressiveLPyramidPolicy",
                                                    "NYUAppCorrLaplacianPolicy", "NYUAppCorrProgressiveLaplacianPolicy",
                                                    "COCOWindowProgressiveLaplacianPolicy"})

@@ -409,7 +409,58 @@ void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------------------ row push
+// Reduce-scatter, sending half: after a row-parallel GEMM wrote this rank's partial rows into its
+// own slot `rank` of the symmetric slot buffer [world, M, D], every row owned by another rank is
+// copied into slot `rank` of the owner's buffer (fully coalesced 16-byte peer stores, one row per
+// CTA; remote stores are posted writes, so NVLink carries them without a read round trip). Rows
+// are visited in an order rotated by the rank so that all peers' links are loaded at once. After
+// a barrier each owner reduces its rows from local memory (sp_row with the slot sources).
+struct PushArgs {
+  const uint4* src;         // this rank's slot (packed rows, D/8 vectors each)
+  uint4* dst[kSpMaxRanks];  // every rank's slot `rank` (same packed row index)
+  const int* tok;           // packed row -> token row (nullptr: identity)
+  int M, nvec, rows_per_rank, rank, world;
+};
+
+__global__ void __launch_bounds__(kSpThreads) sp_push_rows_kernel(PushArgs a) {
+  for (int j = blockIdx.x; j < a.M; j += gridDim.x) {
+    const int i = (j + a.rank * (a.M / max(a.world, 1))) % a.M;  // rotated start per rank
+    const int tok = a.tok ? a.tok[i] : i;
+    if (tok < 0) continue;
+    const int owner = tok / a.rows_per_rank;
+    if (owner == a.rank || owner >= a.world) continue;
+    const uint4* s = a.src + (long)i * a.nvec;
+    uint4* d = a.dst[owner] + (long)i * a.nvec;
+    for (int c = threadIdx.x; c < a.nvec; c += kSpThreads) d[c] = s[c];
+  }
+}
+
+void sp_push_rows_op(int64_t src, std::vector<int64_t> dst, c10::optional<at::Tensor> tok, int64_t M, int64_t D,
+                     int64_t rows_per_rank, int64_t rank) {
+  const int world = static_cast<int>(dst.size());
+  TORCH_CHECK(world >= 1 && world <= kSpMaxRanks && D % 8 == 0, "sp_push_rows: 1..8 ranks, D % 8 == 0");
+  TORCH_CHECK((src & 15) == 0, "sp_push_rows: 16-byte aligned source");
+  PushArgs a{};
+  a.src = reinterpret_cast<const uint4*>(src);
+  for (int r = 0; r < world; ++r) {
+    TORCH_CHECK((dst[r] & 15) == 0, "sp_push_rows: 16-byte aligned destinations");
+    a.dst[r] = reinterpret_cast<uint4*>(dst[r]);
+  }
+  a.tok = sp_opt<const int>(tok);
+  a.M = static_cast<int>(M);
+  a.nvec = static_cast<int>(D / 8);
+  a.rows_per_rank = static_cast<int>(rows_per_rank);
+  a.rank = static_cast<int>(rank);
+  a.world = world;
+  if (M == 0 || world == 1) return;
+  const int grid = static_cast<int>(std::min<int64_t>(M, 4 * num_sms()));
+  sp_push_rows_kernel<<<grid, kSpThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void register_sp_ops(pybind11::module_& m) {
+  m.def("sp_push_rows", &sp_push_rows_op);
   namespace py = pybind11;
   m.def("sp_row", &sp_row_op, py::arg("M"), py::arg("tok"), py::arg("rows_per_rank"), py::arg("rank"),
         py::arg("world"), py::arg("D"), py::arg("src"), py::arg("src_off"), py::arg("bias"), py::arg("gamma"),

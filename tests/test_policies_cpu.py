@@ -299,3 +299,32 @@ def test_vggt_boundaries():
     assert b[-1] == 48 and b[0] < b[1] < b[2]
     cfg.scheduler_kwargs["layer_split"] = "uniform"
     assert VGGTInterleavedPolicy.boundaries(48, 3, cfg) == [16, 32, 48]
+
+
+def test_nyu_policies_decode_on_fixed_model_grid():
+    """NYU AppCorr transmission (reference nyu_appcorr_progressive.py): shape preservation is
+    forced off and every decode lands on config.image_shape, whatever the input image size."""
+    import numpy as np
+
+    from appcorr_b200.common.protocol import ExperimentConfig
+    from appcorr_b200.policies import get_transmission
+
+    cfg = ExperimentConfig(exp_id="t", model_name="dinov3_depther", batch_size=2, image_shape=(64, 96, 3),
+                           transmission_kwargs={"preserve_input_shape": True, "pyramid_levels": [1, 0],
+                                                "num_groups": 1, "grouping_strategy": "grid"})
+    rng = np.random.default_rng(0)
+    imgs = rng.integers(0, 256, (2, 64, 96, 3), dtype=np.uint8)
+    for name in ("NYUAppCorrLaplacian", "NYUAppCorrProgressiveLaplacian"):
+        pol = get_transmission(name)
+        groups = list(pol.encode(imgs, cfg))
+        out = pol.decode([p for g in groups for p in g], cfg)
+        out = np.stack([o["image"] if isinstance(o, dict) else o for o in out]) if isinstance(out, list) else out
+        assert out.shape == (2, 64, 96, 3), name
+        assert np.abs(out.astype(int) - imgs.astype(int)).max() <= 1, name   # lossless pyramid
+    # raw: a differently sized image is resized onto the model grid
+    big = rng.integers(0, 256, (2, 128, 192, 3), dtype=np.uint8)
+    pol = get_transmission("NYUAppCorrRaw")
+    (group,) = list(pol.encode(big, cfg))
+    assert len(group) == 2 and group[0].target_shape == (128, 192)
+    out = pol.decode(group, cfg)
+    assert out.shape == (2, 64, 96, 3)

@@ -76,8 +76,8 @@ def _worker(rank, world, port, q, precision="bf16", rs_mode="pull", microbatch=2
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("precision,rs_mode,microbatch", [("bf16", "pull", 2), ("bf16", "pull", 1), ("bf16", "push", 2),
-                                                          ("bf16", "ce", 1), ("fp8", "pull", 2),
-                                                          ("nvfp4", "pull", 2)])
+                                                          ("bf16", "ce", 1), ("bf16", "pushk", 2), ("fp8", "pull", 2),
+                                                          ("nvfp4", "pull", 2), ("nvfp4", "pushk", 2)])
 def test_tp2_matches_single_gpu(precision, rs_mode, microbatch):
     import torch.multiprocessing as mp
 
