@@ -77,9 +77,10 @@ class DINOv3BackboneMixin:
             from ...parallel.comm import TPComm
             from ...parallel.tp import ViTEngineTP
 
-            if not dist.is_initialized() or dist.get_world_size() != tp:
+            grp = getattr(self, "tp_group", None)  # set by the serving group after a re-form
+            if not dist.is_initialized() or dist.get_world_size(grp) != tp:
                 raise RuntimeError(f"tp_size={tp} needs a torch.distributed group of {tp} ranks, one per GPU")
-            self.comm = TPComm(device=self.device)
+            self.comm = TPComm(group=grp, device=self.device)
             if path is not None:
                 m = build_vit(self.arch)
                 m.load_state_dict(torch.load(path, map_location="cpu", mmap=True, weights_only=True), strict=True)

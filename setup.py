@@ -36,13 +36,18 @@ ext_modules = [
     ),
 ]
 if runtime_sources:
+    # host-only runtime: plain pybind11, no torch libraries (importable without torch)
+    import pybind11
+    from setuptools import Extension
+
     ext_modules.append(
-        CppExtension(
+        Extension(
             name="appcorr_b200._runtime",
             sources=runtime_sources,
-            include_dirs=[os.path.join(ROOT, "csrc", "runtime")],
-            extra_compile_args={"cxx": CXX_FLAGS + ["-fopenmp"]},
-            extra_link_args=["-fopenmp", "-lz"],
+            include_dirs=[os.path.join(ROOT, "csrc", "runtime"), pybind11.get_include()],
+            language="c++",
+            extra_compile_args=CXX_FLAGS + ["-fvisibility=hidden"],
+            extra_link_args=["-lrt"],
         )
     )
 
