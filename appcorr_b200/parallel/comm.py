@@ -106,7 +106,7 @@ class TPComm:
                bias=None, gamma=None, resid=None, resid_tok: bool = True, resid2=None,
                out=None, out_tok: bool = True, aux=None, aux_mode: int = 0, x=None, copy_out=None,
                ln_w=None, ln_b=None, eps: float = 1e-6, rms: bool = False, ag: Optional[SymTensor] = None,
-               ag_scale: Optional[SymTensor] = None, ag_sf: Optional[SymTensor] = None) -> None:
+               ag_scale: Optional[SymTensor] = None, ag_sf: Optional[SymTensor] = None, ag_push: bool = False) -> None:
         """Owner-side row kernel of the sequence-parallel layout (csrc/tp_sp.cu): finish the
         reduce-scatter of the partial rows `src` = (base pointers, row offsets), one per rank (or
         load x[tok]) on the rows this rank owns, then LayerNorm and all-gather the normalised
@@ -114,11 +114,20 @@ class TPComm:
         row scales and blocked block scales -- when ag_sf is given too)."""
         _count()
         mode = 0 if ag_scale is None else (2 if ag_sf is not None else 1)
+        # ag_push (contiguous rows only): the row kernel writes the gathered rows locally and a
+        # bulk push with coalesced 16-byte peer stores sends them to the other ranks
+        push = ag_push and tok is None and ag is not None and ln_w is not None and self.world > 1
         lib().sp_row(M, tok, rows_per_rank, self.rank, self.world, D, list(src[0]) if src else [],
                      list(src[1]) if src else [], bias, gamma, resid, resid_tok, resid2, out, out_tok, aux, aux_mode, x, copy_out,
                      ln_w, ln_b, float(eps), rms, mode, ag.ptrs if ag is not None else [],
                      (ag.local.stride(0) if ag is not None else 0), ag_scale.ptrs if mode else [],
-                     ag_sf.ptrs if mode == 2 else [])
+                     ag_sf.ptrs if mode == 2 else [], push)
+        if push:
+            r0, r1 = min(M, self.rank * rows_per_rank), min(M, (self.rank + 1) * rows_per_rank)
+            _count()
+            lib().sp_push_ag(ag.ptrs, ag.local.stride(0) * ag.local.element_size(), r0, r1,
+                             ag_scale.ptrs if mode else [], ag_sf.ptrs if mode == 2 else [],
+                             D // 64 if mode == 2 else 0, self.rank)
 
     def push_rows(self, src: int, dst: List[int], tok: Optional[torch.Tensor], M: int, D: int,
                   rows_per_rank: int) -> None:

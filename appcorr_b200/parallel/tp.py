@@ -92,6 +92,7 @@ class ViTEngineTP(ViTEngine):
         # owners' slots, packed correction rows are pulled
         # "pushk": the GEMM writes locally, then a row kernel pushes every row owned by a peer
         # into the owner's slot with coalesced peer stores; owners reduce from local memory
+        self.ag_push = os.environ.get("APPCORR_TP_AG", "push") == "push"
         self.rs_mode = os.environ.get("APPCORR_TP_RS", "pull")
         if self.rs_mode not in ("pull", "push", "ce", "pushk"):
             raise ValueError("APPCORR_TP_RS must be 'pull', 'push', 'pushk' or 'ce'")
@@ -190,11 +191,12 @@ class ViTEngineTP(ViTEngine):
 
     def _ag(self, sess: Session) -> Dict:
         e = sess.extra
+        push = self.ag_push  # contiguous rows: local gather stores + one bulk peer push
         if self._fp4:
-            return {"ag": e["sym_xg4"], "ag_scale": e["sym_xg_scale"], "ag_sf": e["sym_xg_sf"]}
+            return {"ag": e["sym_xg4"], "ag_scale": e["sym_xg_scale"], "ag_sf": e["sym_xg_sf"], "ag_push": push}
         if self._fp8:
-            return {"ag": e["sym_xg8"], "ag_scale": e["sym_xg_scale"]}
-        return {"ag": e["sym_xg"]}
+            return {"ag": e["sym_xg8"], "ag_scale": e["sym_xg_scale"], "ag_push": push}
+        return {"ag": e["sym_xg"], "ag_push": push}
 
     def _row_gemm(self, sess: Session, a, w, rows_out, a_scale, b_scale, n: int) -> None:
         """Row-parallel GEMM producing this rank's partial product of n (packed) rows."""

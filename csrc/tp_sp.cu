@@ -78,6 +78,7 @@ struct SpArgs {
   long ld_ag;               // elements (bf16 / e4m3) or bytes (NVFP4)
   float* ag_scale[kSpMaxRanks];
   uint8_t* ag_sf[kSpMaxRanks];  // NVFP4 block scales (blocked layout, K = D)
+  int ag_self;              // 1: write only this rank's gather buffers (a bulk push follows)
 };
 
 __device__ __forceinline__ void sp_unpack8(const uint4& u, float (&v)[8]) {
@@ -242,7 +243,7 @@ __device__ __forceinline__ void sp_row_one(const SpArgs& a, int i, float* red) {
     amax = sp_block_reduce<true>(amax, red);
     const float rs = fmaxf(amax, 1e-12f) / kNvfp4RowDiv;
     const float inv_rs = 1.f / rs;
-    if (threadIdx.x < W) a.ag_scale[threadIdx.x][i] = rs;
+    if (threadIdx.x < W && (!a.ag_self || threadIdx.x == a.rank)) a.ag_scale[threadIdx.x][i] = rs;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int c = threadIdx.x + k * kSpThreads;
@@ -264,6 +265,7 @@ __device__ __forceinline__ void sp_row_one(const SpArgs& a, int i, float* red) {
       const long so = nvfp4_sf_offset(i, c >> 1, a.D >> 6);
 #pragma unroll
       for (int r = 0; r < W; ++r) {
+        if (a.ag_self && r != a.rank) continue;
         reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(a.ag[r]) + (long)i * a.ld_ag)[c] = pk;
         if ((c & 7) == 0) *reinterpret_cast<uint32_t*>(a.ag_sf[r] + so) = sw;
       }
@@ -272,7 +274,7 @@ __device__ __forceinline__ void sp_row_one(const SpArgs& a, int i, float* red) {
     amax = sp_block_reduce<true>(amax, red);
     const float sc = fmaxf(amax, 1e-12f) / 448.f;
     const float inv = 1.f / sc;
-    if (threadIdx.x < W) a.ag_scale[threadIdx.x][i] = sc;
+    if (threadIdx.x < W && (!a.ag_self || threadIdx.x == a.rank)) a.ag_scale[threadIdx.x][i] = sc;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int c = threadIdx.x + k * kSpThreads;
@@ -283,7 +285,8 @@ __device__ __forceinline__ void sp_row_one(const SpArgs& a, int i, float* red) {
                                   sp_e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv));
 #pragma unroll
       for (int r = 0; r < W; ++r)
-        reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(a.ag[r]) + (long)i * a.ld_ag)[c] = pk;
+        if (!a.ag_self || r == a.rank)
+          reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(a.ag[r]) + (long)i * a.ld_ag)[c] = pk;
     }
   } else {
 #pragma unroll
@@ -292,7 +295,8 @@ __device__ __forceinline__ void sp_row_one(const SpArgs& a, int i, float* red) {
       if (c >= nvec) continue;
 #pragma unroll
       for (int r = 0; r < W; ++r)
-        reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.ag[r]) + (long)i * a.ld_ag)[c] = vb[k];
+        if (!a.ag_self || r == a.rank)
+          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.ag[r]) + (long)i * a.ld_ag)[c] = vb[k];
     }
   }
 }
@@ -317,7 +321,7 @@ void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, 
                c10::optional<at::Tensor> aux, int64_t aux_mode, c10::optional<at::Tensor> x,
                c10::optional<at::Tensor> copy_out, c10::optional<at::Tensor> ln_w, c10::optional<at::Tensor> ln_b,
                double eps, bool rms, int64_t fp8, std::vector<int64_t> ag, int64_t ld_ag, std::vector<int64_t> ag_scale,
-               std::vector<int64_t> ag_sf) {
+               std::vector<int64_t> ag_sf, bool ag_self) {
   TORCH_CHECK(D % 8 == 0 && D <= kSpThreads * kSpMaxVec * 8, "sp_row: D % 8 == 0 and D <= 8192");
   TORCH_CHECK(world >= 1 && world <= kSpMaxRanks, "sp_row: 1..8 ranks");
   SpArgs a{};
@@ -363,6 +367,7 @@ void sp_row_op(int64_t M, c10::optional<at::Tensor> tok, int64_t rows_per_rank, 
   a.rms = rms ? 1 : 0;
   TORCH_CHECK(fp8 >= 0 && fp8 <= 2, "sp_row: gather format 0 (bf16), 1 (e4m3) or 2 (nvfp4)");
   a.fp8 = static_cast<int>(fp8);
+  a.ag_self = ag_self ? 1 : 0;
   if (a.ln_w) {
     TORCH_CHECK(static_cast<int64_t>(ag.size()) == world, "sp_row: one gather buffer per rank");
     for (int r = 0; r < world; ++r) a.ag[r] = reinterpret_cast<void*>(ag[r]);
@@ -459,15 +464,113 @@ void sp_push_rows_op(int64_t src, std::vector<int64_t> dst, c10::optional<at::Te
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------------------ all-gather push
+// All-gather, sending half, for the contiguous row block [r0, r1) of this rank: the row kernel
+// wrote the gathered operand of these rows into this rank's own gather buffers only (local
+// stores); this kernel copies them into every peer's buffers at the same offsets with 16-byte
+// peer stores: the packed rows (one contiguous byte range), the fp32 row scales, and for NVFP4
+// the block scales. In the blocked scale layout a 16-byte chunk holds one k-group of rows
+// {c, c+32, c+64, c+96} of a 128-row tile; chunks whose four rows are all this rank's go out
+// whole, chunks shared with a neighbour's rows word by word.
+struct AgPushArgs {
+  const uint8_t* rows_src;   // local gather buffer
+  uint8_t* rows_dst[kSpMaxRanks];
+  long rows_lo, rows_bytes;  // byte range of the rows (16-byte aligned)
+  const float* rs_src;       // local row scales (nullptr: none)
+  float* rs_dst[kSpMaxRanks];
+  int r0, r1;
+  const uint8_t* sf_src;     // local block scales (nullptr: none)
+  uint8_t* sf_dst[kSpMaxRanks];
+  int sf_kt;                 // 64-element groups per row (D / 64)
+  int t0, t1;                // 128-row tiles touched by [r0, r1)
+  int rank, world;
+};
+
+__global__ void __launch_bounds__(kSpThreads) sp_push_ag_kernel(AgPushArgs a) {
+  const long nrow16 = a.rows_bytes >> 4;
+  const long nsf16 = a.sf_src ? (long)(a.t1 - a.t0 + 1) * a.sf_kt * 32 : 0;  // 16-byte chunks
+  const long nrs = a.rs_src ? (a.r1 - a.r0) : 0;
+  const long per_peer = nrow16 + nsf16 + nrs;
+  const long total = per_peer * (a.world - 1);
+  for (long w = blockIdx.x * (long)blockDim.x + threadIdx.x; w < total; w += (long)gridDim.x * blockDim.x) {
+    const int pk = static_cast<int>(w / per_peer);
+    const int peer = (a.rank + 1 + pk) % a.world;  // rotated so every link is busy
+    long j = w - (long)pk * per_peer;
+    if (j < nrow16) {
+      const long off = a.rows_lo + (j << 4);
+      *reinterpret_cast<uint4*>(a.rows_dst[peer] + off) = *reinterpret_cast<const uint4*>(a.rows_src + off);
+      continue;
+    }
+    j -= nrow16;
+    if (j < nsf16) {
+      const long base = (long)a.t0 * a.sf_kt * 512;
+      const long off = base + (j << 4);
+      const int tile = a.t0 + static_cast<int>(j / ((long)a.sf_kt * 32));
+      const int c = static_cast<int>(j & 31);
+      const int row0 = tile * 128 + c;
+      if (row0 >= a.r0 && row0 + 96 < a.r1) {
+        *reinterpret_cast<uint4*>(a.sf_dst[peer] + off) = *reinterpret_cast<const uint4*>(a.sf_src + off);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int row = row0 + 32 * q;
+          if (row >= a.r0 && row < a.r1)
+            *reinterpret_cast<uint32_t*>(a.sf_dst[peer] + off + 4 * q) =
+                *reinterpret_cast<const uint32_t*>(a.sf_src + off + 4 * q);
+        }
+      }
+      continue;
+    }
+    j -= nsf16;
+    a.rs_dst[peer][a.r0 + j] = a.rs_src[a.r0 + j];
+  }
+}
+
+void sp_push_ag_op(std::vector<int64_t> rows, int64_t row_bytes, int64_t r0, int64_t r1, std::vector<int64_t> rs,
+                   std::vector<int64_t> sf, int64_t sf_kt, int64_t rank) {
+  const int world = static_cast<int>(rows.size());
+  TORCH_CHECK(world >= 1 && world <= kSpMaxRanks, "sp_push_ag: 1..8 ranks");
+  TORCH_CHECK(row_bytes % 16 == 0, "sp_push_ag: row bytes a multiple of 16");
+  if (world == 1 || r1 <= r0) return;
+  AgPushArgs a{};
+  a.rows_src = reinterpret_cast<const uint8_t*>(rows[rank]);
+  for (int r = 0; r < world; ++r) a.rows_dst[r] = reinterpret_cast<uint8_t*>(rows[r]);
+  a.rows_lo = r0 * row_bytes;
+  a.rows_bytes = (r1 - r0) * row_bytes;
+  a.r0 = static_cast<int>(r0);
+  a.r1 = static_cast<int>(r1);
+  if (!rs.empty()) {
+    TORCH_CHECK(static_cast<int>(rs.size()) == world, "sp_push_ag: one row-scale buffer per rank");
+    a.rs_src = reinterpret_cast<const float*>(rs[rank]);
+    for (int r = 0; r < world; ++r) a.rs_dst[r] = reinterpret_cast<float*>(rs[r]);
+  }
+  if (!sf.empty()) {
+    TORCH_CHECK(static_cast<int>(sf.size()) == world && sf_kt > 0, "sp_push_ag: one block-scale buffer per rank");
+    a.sf_src = reinterpret_cast<const uint8_t*>(sf[rank]);
+    for (int r = 0; r < world; ++r) a.sf_dst[r] = reinterpret_cast<uint8_t*>(sf[r]);
+    a.sf_kt = static_cast<int>(sf_kt);
+    a.t0 = static_cast<int>(r0 / 128);
+    a.t1 = static_cast<int>((r1 - 1) / 128);
+  }
+  a.rank = static_cast<int>(rank);
+  a.world = world;
+  const long per_peer = (a.rows_bytes >> 4) + (a.sf_src ? (long)(a.t1 - a.t0 + 1) * a.sf_kt * 32 : 0) + (a.rs_src ? r1 - r0 : 0);
+  const long total = per_peer * (world - 1);
+  const int grid = static_cast<int>(std::min<long>((total + kSpThreads - 1) / kSpThreads, 4L * num_sms()));
+  sp_push_ag_kernel<<<grid, kSpThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void register_sp_ops(pybind11::module_& m) {
   m.def("sp_push_rows", &sp_push_rows_op);
+  m.def("sp_push_ag", &sp_push_ag_op);
   namespace py = pybind11;
   m.def("sp_row", &sp_row_op, py::arg("M"), py::arg("tok"), py::arg("rows_per_rank"), py::arg("rank"),
         py::arg("world"), py::arg("D"), py::arg("src"), py::arg("src_off"), py::arg("bias"), py::arg("gamma"),
         py::arg("resid"), py::arg("resid_tok"), py::arg("resid2"), py::arg("out"), py::arg("out_tok"),
         py::arg("aux"), py::arg("aux_mode"), py::arg("x"), py::arg("copy_out"), py::arg("ln_w"), py::arg("ln_b"),
         py::arg("eps"), py::arg("rms"), py::arg("fp8"), py::arg("ag"), py::arg("ld_ag"), py::arg("ag_scale"),
-        py::arg("ag_sf") = std::vector<int64_t>{});
+        py::arg("ag_sf") = std::vector<int64_t>{}, py::arg("ag_self") = false);
 }
 
 }  // namespace appcorr
