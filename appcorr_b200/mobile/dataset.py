@@ -1,10 +1,22 @@
-"""Request sources for the mobile client (reference offload/mobile/dataset.py:8-849).
+"""Request sources and task metrics for the mobile client (reference offload/mobile/dataset.py:8-849,
+co3d_loader.py:38-171).
 
-No network access is assumed: `synthetic` generates deterministic images of the configured shape
-(pixels ~ clipped N(128, 60^2), as the benchmark configurations specify) with random labels;
-`image_folder` reads `<root>/<class>/<file>` images with class-index labels (the ImageNet
-validation layout). Task metrics: classification top-1/top-5, segmentation mIoU / pixel
-accuracy, depth abs_rel / delta1.
+Loaders (`get_dataset_loader(name, root, batch_size, image_shape, ...)`), all reading local files
+in the datasets' standard layouts (no network, no fiftyone / HF datasets / pycocotools):
+  imagenet-1k        <root>/<class>/<image>                      top-1 / top-5 accuracy
+  coco2017           <root>/annotations/instances_val2017.json,  COCO box mAP (own evaluator:
+                     <root>/val2017/<file>                       IoU 0.50:0.95, 101-point AP)
+  ade20k             <root>/images/validation/*.jpg,             mIoU / aAcc / dice / fscore from
+                     <root>/annotations/validation/*.png         intersect-and-union areas
+  nyu_depth          <root>/nyu_test.txt: "rgb depth_png [focal]" abs_rel, sq_rel, rmse, rmse_log,
+                                                                 delta 1.25^k after least-squares
+                                                                 scale/shift alignment, Eigen crop
+  co3d / co3dv2      <root>/<category>/frame_annotations.jgz    median-aligned depth abs_rel,
+                                                                 relative rotation error / RRA@15
+  synthetic          deterministic images of the configured shape (pixels ~ clipped N(128, 60^2))
+                     with random labels; also used when `root` does not exist
+Loaders iterate as (images, labels); those with metrics expose evaluate_batch(preds, labels) and
+get_summary().
 """
 from __future__ import annotations
 
@@ -78,6 +90,19 @@ class ImageFolderLoader:
 def get_dataset_loader(name: str, data_root: Optional[str], batch_size: int, image_shape, **kwargs):
     if name == "synthetic" or data_root is None or not os.path.isdir(os.path.expanduser(str(data_root))):
         return SyntheticLoader(batch_size, image_shape, **kwargs)
+    from . import datasets as D
+
+    n = str(name).lower()
+    if n in ("imagenet-1k", "imagenet", "image_folder"):
+        return D.ImageNetLoader(data_root, batch_size, image_shape, **kwargs)
+    if n == "coco2017":
+        return D.COCO2017Loader(data_root, batch_size, image_shape, **kwargs)
+    if n in ("ade20k", "scene_parse_150"):
+        return D.ADE20KLoader(data_root, batch_size, image_shape, **kwargs)
+    if n == "nyu_depth":
+        return D.NYUDepthLoader(data_root, batch_size, image_shape, **kwargs)
+    if n in ("co3d", "co3dv2"):
+        return D.CO3DSequenceLoader(data_root, batch_size, image_shape, **kwargs)
     return ImageFolderLoader(data_root, batch_size, image_shape, **kwargs)
 
 

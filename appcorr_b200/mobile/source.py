@@ -119,7 +119,12 @@ class SourceModule(multiprocessing.Process):
                 r = self.execute_request(policy, imgs, labels, offset)
                 n = len(labels)
                 preds = r["result"].output[:n]
-                if preds and isinstance(preds[0], dict) and "topk" in preds[0]:
+                if hasattr(loader, "evaluate_batch"):  # dataset loaders with task metrics
+                    try:
+                        loader.evaluate_batch(preds, labels)
+                    except Exception as exc:  # a malformed prediction must not end the run
+                        print(f"!!! [Source] evaluate_batch: {exc}", flush=True)
+                elif preds and isinstance(preds[0], dict) and "topk" in preds[0]:
                     correct1 += topk_correct(preds, labels, 1)
                     correct5 += topk_correct(preds, labels, 5)
                 seen += n
@@ -154,6 +159,8 @@ class SourceModule(multiprocessing.Process):
         if correct1 or correct5:
             summary["top1"] = correct1 / max(seen, 1)
             summary["top5"] = correct5 / max(seen, 1)
+        if hasattr(loader, "get_summary"):
+            summary["metrics"] = loader.get_summary()
         with open(os.path.join(log_dir, "summary.json"), "w") as f:
             json.dump(summary, f, indent=2, default=float)
         print(f"[Source] done: {json.dumps(summary['latency_ms'])} ms, logs in {log_dir}", flush=True)
