@@ -229,7 +229,10 @@ def _score_kind(server_pscore: str) -> str:
     raise ValueError(f"unknown server_pscore {server_pscore!r}")
 
 
-PRECISIONS = ("bf16", "fp8", "nvfp4")
+PRECISIONS = ("bf16", "fp8", "nvfp4", "auto")
+# "auto": e4m3 operands for a pass whose GEMMs have at least this many rows, bf16 below
+# (reference dinov3_precision.py:479-488, config fp8_auto_min_rows)
+AUTO_MIN_ROWS = 3072
 _Q8_NAMES = ("qkv", "proj", "fc1", "fc2")
 # nvfp4 precision: these GEMMs take NVFP4 operands; attn.proj stays e4m3 (the reference's
 # FastFP4 path keeps proj in FP8 by default, offload/server/model/fp4_fast_linear.py)
@@ -277,7 +280,8 @@ class ViTEngine:
             if v not in PRECISIONS:
                 raise ValueError(f"engine precision must be one of {PRECISIONS}, got {v!r}")
         self.precision = dict(precision)
-        low = set(self.precision.values()) - {"bf16"}
+        self.auto_min_rows = AUTO_MIN_ROWS
+        low = {("fp8" if v == "auto" else v) for v in self.precision.values()} - {"bf16"}
         for lw in self.w.layers:
             if low and lw.q8 is None:
                 quantize_layer_e4m3(lw)
@@ -348,9 +352,18 @@ class ViTEngine:
             e["a4_scale"] = torch.empty(M, device=self.device, dtype=torch.float32)
             e["a4_sf"] = torch.zeros(K.nvfp4_sf_bytes(M, width), device=self.device, dtype=torch.uint8)
 
-    def _set_pass(self, sess: Session, which: str) -> None:
-        self._fp4 = self.precision[which] == "nvfp4"
-        self._fp8 = self.precision[which] in ("fp8", "nvfp4")
+    def effective_precision(self, which: str, rows: int) -> str:
+        """Operand precision of a pass whose GEMMs have `rows` rows ("auto" resolves by rows)."""
+        p = self.precision[which]
+        if p == "auto":
+            return "fp8" if rows >= self.auto_min_rows else "bf16"
+        return p
+
+    def _set_pass(self, sess: Session, which: str, rows: Optional[int] = None) -> None:
+        p = self.effective_precision(which, sess.x.shape[0] if rows is None else rows)
+        sess.extra["pass_precision"] = (which, p)
+        self._fp4 = p == "nvfp4"
+        self._fp8 = p in ("fp8", "nvfp4")
         if self._fp8:
             self._ensure_fp8_scratch(sess)
 
@@ -640,7 +653,9 @@ class ViTEngine:
                     sess.x, sess.x_in, sess.N, dind, pre.shape[1], float(opts.get("token_prune_threshold", 0.0)),
                     int(opts.get("token_prune_min_keep", 1)))
             sess.x.copy_(sess.x_in)
-        self._set_pass(sess, "correct")
+        k_rows = P_g if thres is not None and cap <= 0 else (min(cap, P_g) if thres is not None else
+                                                             min(int(P_g * ratio), P_g))
+        self._set_pass(sess, "correct", rows=sess.B * (self.cfg.n_prefix + k_rows))
         shared = None
         _score_kind(kind)  # unknown names raise
         if kind == "random":  # one random score per request, shared by every layer

@@ -48,10 +48,10 @@ class DINOv3BackboneMixin:
     # ------------------------------------------------------------------ loading
     @staticmethod
     def engine_precision(config: Any) -> Dict[str, str]:
-        """Config precision -> engine precision per pass. "auto" selects e4m3 (the reference
-        picks FP8 at >= 3072 rows, dinov3_precision.py:172-200, which every batched approx pass
-        of the served models reaches). "fp4" / "nvfp4" select the NVFP4 block-scaled GEMMs."""
-        m = {"bf16": "bf16", "fp8": "fp8", "auto": "fp8", "fp4": "nvfp4", "nvfp4": "nvfp4"}
+        """Config precision -> engine precision per pass. "auto" picks e4m3 for a pass whose GEMMs
+        have at least `fp8_auto_min_rows` rows and bf16 below (dinov3_precision.py:479-488).
+        "fp4" / "nvfp4" select the NVFP4 block-scaled GEMMs."""
+        m = {"bf16": "bf16", "fp8": "fp8", "auto": "auto", "fp4": "nvfp4", "nvfp4": "nvfp4"}
         ap = m.get(str(getattr(config, "precision", "bf16")).lower(), "bf16")
         cp = m.get(str(getattr(config, "correct_precision", "bf16")).lower(), "bf16")
         return {"approx": ap, "correct": cp}
@@ -66,6 +66,7 @@ class DINOv3BackboneMixin:
         tp = int(getattr(config, "tp_size", 1) or 1)
         prec = self.engine_precision(config)
         self.sr_engine = None
+        self._auto_min_rows = int(getattr(config, "fp8_auto_min_rows", 3072) or 3072)
         if self.device.type == "cuda" and hasattr(config, "lowres_sr_enabled") and config.lowres_sr_enabled():
             from ..sr import create_lowres_sr_engine
 
@@ -88,6 +89,7 @@ class DINOv3BackboneMixin:
             else:
                 self.engine = ViTEngineTP.random_tp(PRESETS[self.arch], self.comm, seed=seed, precision=prec)
             self.cfg = self.engine.cfg
+            self.engine.auto_min_rows = self._auto_min_rows
         elif self.device.type == "cuda":
             from ...models.engine import ViTEngine
 
@@ -99,6 +101,7 @@ class DINOv3BackboneMixin:
             else:
                 self.engine = ViTEngine.random(PRESETS[self.arch], self.device, seed=seed, precision=prec)
             self.cfg = self.engine.cfg
+            self.engine.auto_min_rows = self._auto_min_rows
         else:
             m = build_vit(self.arch)
             if path is not None:
@@ -197,7 +200,11 @@ class DINOv3BackboneMixin:
                                                           server_pscore_weight=opts["server_pscore_weight"])
             context["x"] = x
         context["approx_frontier"] = max(context.get("approx_frontier", 0), end)
-        return {"precision": self.engine.precision["approx"] if self.engine is not None else "fp32"}
+        if self.engine is None:
+            return {"precision": "fp32"}
+        sess = context["session"]
+        return {"precision": sess.extra.get("pass_precision", ("approx", self.engine.precision["approx"]))[1],
+                "rows": int(sess.x.shape[0])}
 
     def group_candidates(self, B: int, grid_hw: Tuple[int, int], group_id: int, config: Any,
                          device) -> Tuple[torch.Tensor, torch.Tensor]:

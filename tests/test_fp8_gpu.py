@@ -146,3 +146,34 @@ def test_qkv_e4m3_grouped_query():
     _close(q, ref[:, : Hq * Dh])
     _close(k, ref[:, Hq * Dh:(Hq + Hkv) * Dh])
     _close(v, ref[:, (Hq + Hkv) * Dh:])
+
+
+def test_auto_precision_picks_by_rows():
+    """precision "auto" (reference dinov3_precision.py:479-488): e4m3 operands for a pass with at
+    least fp8_auto_min_rows GEMM rows, bf16 below; results stay close to the bf16 engine."""
+    from appcorr_b200.models.dinov3.vit import ViTConfig
+    from appcorr_b200.models.engine import ViTEngine, random_weights
+
+    cfg = ViTConfig(embed_dim=256, depth=2, num_heads=4, layerscale_init=0.3)
+    dev = torch.device(DEV)
+    eng = ViTEngine(random_weights(cfg, dev, seed=1, std=0.05), dev, "auto")
+    ref = ViTEngine(random_weights(cfg, dev, seed=1, std=0.05), dev, "bf16")
+    B, H, W = 4, 128, 128                      # 4 x (64 + 5) = 276 approx rows
+    eng.auto_min_rows = 200                    # approx (276 rows) -> fp8; correction (4 x 21) -> bf16
+    img = torch.randint(0, 256, (B, H, W, 3), dtype=torch.uint8, device=DEV)
+    outs = []
+    for e in (eng, ref):
+        s = e.new_session(B, H, W)
+        e.prepare_tokens(s, img)
+        xa = e.approx(s, 0, 2).clone()
+        if e is eng:
+            assert s.extra["pass_precision"] == ("approx", "fp8")
+        pre = torch.arange(5, dtype=torch.int32, device=DEV).repeat(B, 1).contiguous()
+        cand = torch.arange(5, s.N, dtype=torch.int32, device=DEV).repeat(B, 1).contiguous()
+        xc = e.correct(s, 0, 2, pre, cand, {"token_keep_ratio": 0.25}).clone()
+        if e is eng:
+            assert s.extra["pass_precision"] == ("correct", "bf16")
+        outs.append((xa, xc))
+    torch.cuda.synchronize()
+    rel = ((outs[0][0].float() - outs[1][0].float()).norm() / outs[1][0].float().norm()).item()
+    assert 1e-4 < rel < 6e-2   # e4m3 noise on the approximate pass, not bit-identical to bf16
