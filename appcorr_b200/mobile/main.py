@@ -58,6 +58,7 @@ def main(argv=None):
     ap.add_argument("-nr", "--num-request", type=int, default=None)
     ap.add_argument("-nw", "--num-warmup", type=int, default=1)
     ap.add_argument("--set", dest="config_overrides", action="append", default=[], metavar="KEY=VALUE")
+    ap.add_argument("--log-root", type=str, default=None, help="directory for summary.json / events.jsonl runs")
     a = ap.parse_args(argv)
     if a.num_request is not None and a.num_request <= 0:
         ap.error("--num-request must be a positive integer")
@@ -70,7 +71,8 @@ def main(argv=None):
         apply_config_overrides(raw, a.config_overrides)
         data = raw.get("dataset_kwargs", {}).get("data_root")
     rc = run_mobile(a.ip, a.recv_port, a.send_port, data, a.config, a.num_request, a.num_warmup,
-                    reverse_connect=a.reverse_connect, listen_host=a.listen_host, config_overrides=a.config_overrides)
+                    reverse_connect=a.reverse_connect, listen_host=a.listen_host, config_overrides=a.config_overrides,
+                    log_root=a.log_root)
     raise SystemExit(rc or 0)
 
 
