@@ -7,8 +7,10 @@ DINOv3 block). The engine (models/engine.py) runs these blocks with LayerScale =
 the learned position embedding added to the patch tokens; the pooled output is
 LN_post(CLS) @ proj, L2-normalised, and class scores are 100 * cosine against the class text
 embeddings (`text_embeds` [C, E], an input: the text tower is not part of this build).
-Presets use 64-wide heads (ViT-B/16, ViT-L/14); the reference's bigG/14 (head dim 104) needs
-head padding in the engine and is refused with a clear error.
+ViT-B/16 and ViT-L/14 use 64-wide heads; bigG/14 (head dim 104, reference
+openclip_executor.py:40-262) runs with its heads zero-padded to 128 in the engine: the qkv
+weight gets zero rows and the proj weight zero columns per head, so the padded lanes carry zeros
+through attention, and the softmax keeps the 1 / sqrt(104) scale.
 """
 from __future__ import annotations
 
@@ -42,6 +44,8 @@ CLIP_PRESETS: Dict[str, CLIPVisionConfig] = {
     "clip_vitl14": CLIPVisionConfig(),
     "clip_vitbigg14": CLIPVisionConfig(width=1664, layers=48, heads=16, mlp_ratio=8192 / 1664, embed_dim=1280),
     "clip_tiny": CLIPVisionConfig(patch_size=16, width=256, layers=2, heads=4, embed_dim=128),
+    # bigG-shaped head width (104) on a small tower, for tests of the padded-head path
+    "clip_tiny_hd104": CLIPVisionConfig(patch_size=16, width=416, layers=2, heads=4, mlp_ratio=2.0, embed_dim=128),
 }
 
 
@@ -102,12 +106,39 @@ class CLIPVision(nn.Module):
         return F.normalize(self.ln_post(x[:, 0]) @ self.proj, dim=-1)
 
 
+def padded_head_dim(head_dim: int) -> int:
+    """Attention width the engine runs a head at: 64 or 128 (0: no padding needed)."""
+    if head_dim in (64, 128):
+        return 0
+    if head_dim < 64:
+        return 64
+    if head_dim < 128:
+        return 128
+    raise ValueError(f"head dim {head_dim} > 128 is not supported by the engine")
+
+
 def clip_vit_config(c: CLIPVisionConfig):
     from .dinov3.vit import ViTConfig
 
     return ViTConfig(img_size=c.image_size, patch_size=c.patch_size, embed_dim=c.width, depth=c.layers,
                      num_heads=c.heads, ffn_ratio=c.mlp_ratio, qkv_bias=True, layerscale_init=None,
-                     norm_layer="layernormbf16", ffn_layer="mlp", n_storage_tokens=0)
+                     norm_layer="layernormbf16", ffn_layer="mlp", n_storage_tokens=0,
+                     padded_head_dim=padded_head_dim(c.head_dim))
+
+
+def pad_heads(qkv_w, qkv_b, proj_w, heads: int, hd: int, hp: int):
+    """qkv [3*H*hd, D] -> [3*H*hp, D] and its bias, proj [D, H*hd] -> [D, H*hp], zero-filled."""
+    D = qkv_w.shape[1]
+    w = qkv_w.new_zeros(3, heads, hp, D)
+    w[:, :, :hd] = qkv_w.view(3, heads, hd, D)
+    b = None
+    if qkv_b is not None:
+        b = qkv_b.new_zeros(3, heads, hp)
+        b[:, :, :hd] = qkv_b.view(3, heads, hd)
+        b = b.reshape(-1)
+    p = proj_w.new_zeros(proj_w.shape[0], heads, hp)
+    p[:, :, :hd] = proj_w.view(proj_w.shape[0], heads, hd)
+    return w.reshape(3 * heads * hp, D), b, p.reshape(proj_w.shape[0], heads * hp)
 
 
 def clip_engine_weights(model: CLIPVision, device):
@@ -116,14 +147,18 @@ def clip_engine_weights(model: CLIPVision, device):
     from .engine import EngineWeights, LayerW
 
     c = model.c
-    if c.head_dim not in (64, 128):
-        raise ValueError(f"CLIP tower head dim {c.head_dim} is not supported by the engine (64 or 128)")
+    hp = padded_head_dim(c.head_dim)
     bf = lambda t: t.detach().to(device=device, dtype=torch.bfloat16).contiguous()  # noqa: E731
     ones = torch.ones(c.width, device=device, dtype=torch.bfloat16)
-    layers = [LayerW(norm1_w=bf(b.ln_1.weight), norm1_b=bf(b.ln_1.bias), qkv_w=bf(b.qkv.weight), qkv_b=bf(b.qkv.bias),
-                     proj_w=bf(b.proj.weight), proj_b=bf(b.proj.bias), ls1=ones, norm2_w=bf(b.ln_2.weight),
-                     norm2_b=bf(b.ln_2.bias), fc1_w=bf(b.fc1.weight), fc1_b=bf(b.fc1.bias), fc2_w=bf(b.fc2.weight),
-                     fc2_b=bf(b.fc2.bias), ls2=ones) for b in model.blocks]
+    layers = []
+    for b in model.blocks:
+        qkv_w, qkv_b, proj_w = b.qkv.weight.detach(), b.qkv.bias.detach(), b.proj.weight.detach()
+        if hp:
+            qkv_w, qkv_b, proj_w = pad_heads(qkv_w, qkv_b, proj_w, c.heads, c.head_dim, hp)
+        layers.append(LayerW(norm1_w=bf(b.ln_1.weight), norm1_b=bf(b.ln_1.bias), qkv_w=bf(qkv_w), qkv_b=bf(qkv_b),
+                             proj_w=bf(proj_w), proj_b=bf(b.proj.bias), ls1=ones, norm2_w=bf(b.ln_2.weight),
+                             norm2_b=bf(b.ln_2.bias), fc1_w=bf(b.fc1.weight), fc1_b=bf(b.fc1.bias),
+                             fc2_w=bf(b.fc2.weight), fc2_b=bf(b.fc2.bias), ls2=ones))
     pw = model.conv1.weight.detach()
     return EngineWeights(cfg=clip_vit_config(c), patch_w=bf(pw.reshape(pw.shape[0], -1)),
                          patch_b=torch.zeros(c.width, device=device, dtype=torch.bfloat16),

@@ -63,6 +63,10 @@ class ViTConfig:
     global_layers: Tuple[int, ...] = ()
     window_rope_everywhere: bool = False  # global layers also use window-local RoPE (multi-frame towers)
     cls_token: bool = True                # False: patch tokens only (SAM- / VGGT-style towers)
+    # engine only: attention heads zero-padded to this width (0: head_dim). Lets towers whose
+    # head dim is not 64 / 128 (CLIP bigG: 104) run the 64 / 128 attention kernels; the softmax
+    # scale stays 1 / sqrt(head_dim)
+    padded_head_dim: int = 0
 
     @property
     def head_dim(self) -> int:

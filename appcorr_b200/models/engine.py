@@ -269,8 +269,13 @@ class ViTEngine:
         self.w = weights
         self.cfg = weights.cfg
         self.device = torch.device(device) if device is not None else weights.patch_w.device
-        if self.cfg.head_dim not in (64, 128):
-            raise ValueError("the sm_100a engine supports head_dim 64 or 128")
+        # attention head width the kernels run at (padded heads: zero rows in qkv, zero columns in
+        # proj) and the softmax scale of the true head dim
+        self.Dh = self.cfg.padded_head_dim or self.cfg.head_dim
+        self.A = self.cfg.num_heads * self.Dh
+        self.attn_scale = self.cfg.head_dim ** -0.5
+        if self.Dh not in (64, 128):
+            raise ValueError("the sm_100a engine supports head_dim 64 or 128 (or padded to one of them)")
         kp = (3 * self.cfg.patch_size ** 2 + 15) // 16 * 16  # patch rows padded to 16 elements
         if self.w.patch_w.shape[1] != kp:
             self.w.patch_w = torch.nn.functional.pad(self.w.patch_w, (0, kp - self.w.patch_w.shape[1])).contiguous()
@@ -391,8 +396,8 @@ class ViTEngine:
             order = window_order(gh, gw, c.window_size, 1).to(device=dev, dtype=torch.int32)
         sess = Session(
             B=B, img_hw=(H, W), grid_hw=(gh, gw), N=N, P=P,
-            x_in=e(M, D), x=e(M, D), x_tmp=e(M, D), xn=e(M, D), q=e(M, D), o=e(M, D), h=e(M, Hd),
-            kc=e(L, M, D), vc=e(L, M, D), bos=e(L, M, D), pscore=torch.zeros(L, B, N, device=dev),
+            x_in=e(M, D), x=e(M, D), x_tmp=e(M, D), xn=e(M, D), q=e(M, self.A), o=e(M, self.A), h=e(M, Hd),
+            kc=e(L, M, self.A), vc=e(L, M, self.A), bos=e(L, M, D), pscore=torch.zeros(L, B, N, device=dev),
             ps_scratch=e(B, c.num_heads, N, dtype=torch.float32),
             cols=torch.zeros(B * P, self.w.patch_w.shape[1], device=dev, dtype=BF16),
             patch_rows=patch_rows.reshape(-1).to(torch.int32).contiguous(),
@@ -456,14 +461,15 @@ class ViTEngine:
 
     def approx_layer(self, sess: Session, l: int, x: torch.Tensor, x_out: torch.Tensor, server_pscore: str) -> None:
         c, lw = self.cfg, self.w.layers[l]
-        B, N, H, Dh = sess.B, sess.N, c.num_heads, c.head_dim
+        B, N, H, Dh = sess.B, sess.N, c.num_heads, self.Dh
         a, sa = self._norm(sess, x, lw.norm1_w, lw.norm1_b, sess.xn)
         w, ws = self._w(lw, "qkv")
         K.qkv_gemm(a, w, lw.qkv_b, sess.q, sess.kc[l], sess.vc[l], head_dim=Dh, seq_len=N,
                    rope=self._rope(sess, l), n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         if self._windowed(l):  # windows are contiguous token runs: a batched attention over windows
             nw = sess.extra["n_windows"]
-            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B * nw, Tq=N // nw, Tk=N // nw, H=H, Dh=Dh)
+            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B * nw, Tq=N // nw, Tk=N // nw, H=H, Dh=Dh,
+                        scale=self.attn_scale)
         else:
             self._attention_with_score(sess, l, H, server_pscore, sess.pscore[l])
         # x_out = x + ls1 * proj(o); bos[l] = ls1 * proj(o)
@@ -487,15 +493,16 @@ class ViTEngine:
                             row LSE, then one tcgen05 Q K^T pass sums exp(s - lse) per key
           patch_pseudo*     softmax row of one pseudo query per (image, head)
           none / disabled / random: no score from the attention (random draws at correction)."""
-        B, N, Dh = sess.B, sess.N, self.cfg.head_dim
+        B, N, Dh, sc = sess.B, sess.N, self.Dh, self.attn_scale
         kind = _score_kind(kind)
         if kind == "cls" and self.cfg.n_prefix == 0:
             kind = "none"  # no CLS token to score with
         if kind == "cls":
             fused = K.ATTENTION_IMPL[0].startswith("tcgen05")
             if not fused:
-                K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out)
-            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh,
+                K.cls_attn_pscore(sess.q, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out,
+                                  scale=sc)
+            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, scale=sc,
                         cls_probs=sess.ps_scratch if fused else None)
             if fused:
                 K.head_mean(sess.ps_scratch, B, H, N, score_out)
@@ -504,16 +511,19 @@ class ViTEngine:
             lse = sess.extra.get("lse")
             if lse is None:
                 lse = sess.extra["lse"] = torch.empty(B, H, N, device=self.device, dtype=torch.float32)
-            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, lse=lse, impl="tcgen05")
-            K.attn_colsum_pscore(sess.q, sess.kc[l], lse, B=B, N=N, H=H, Dh=Dh, probs=sess.ps_scratch, out=score_out)
+            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, lse=lse, impl="tcgen05",
+                        scale=sc)
+            K.attn_colsum_pscore(sess.q, sess.kc[l], lse, B=B, N=N, H=H, Dh=Dh, probs=sess.ps_scratch, out=score_out,
+                                 scale=sc)
             return
         if kind == "pseudo":
             pq = sess.extra.get("pseudo_q")
             if pq is None:
                 pq = sess.extra["pseudo_q"] = torch.empty(B, H * Dh, device=self.device, dtype=BF16)
             K.pseudo_query(sess.q, B=B, N=N, npre=self.cfg.n_prefix, H=H, Dh=Dh, out=pq)
-            K.query_attn_pscore(pq, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out)
-        K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh)
+            K.query_attn_pscore(pq, sess.kc[l], B=B, N=N, H=H, Dh=Dh, scratch=sess.ps_scratch, out=score_out,
+                                scale=sc)
+        K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, scale=sc)
 
     def approx(self, sess: Session, start: int, end: int, server_pscore: str = "cls_attn_prob") -> torch.Tensor:
         """Approximate pass over layers [start, end) on the running features."""
@@ -594,7 +604,7 @@ class ViTEngine:
 
     def correct_layer(self, sess: Session, l: int, x: torch.Tensor, upd: torch.Tensor, rows: torch.Tensor) -> None:
         c, lw = self.cfg, self.w.layers[l]
-        B, N, H, Dh = sess.B, sess.N, c.num_heads, c.head_dim
+        B, N, H, Dh = sess.B, sess.N, c.num_heads, self.Dh
         T = upd.shape[1]
         MT = B * T
         x_act, x_att = sess.x_act[:MT], sess.x_att[:MT]
@@ -607,9 +617,10 @@ class ViTEngine:
                    kv_rows=rows, rope=self._rope(sess, l), n_prefix=c.n_prefix, a_scale=sa, b_scale=ws)
         if self._windowed(l):  # each kept query attends its own window's keys
             lo, hi = self._window_bounds(sess, upd)
-            K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh, causal=True, q_pos=hi, q_lo=lo)
+            K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh, causal=True, q_pos=hi, q_lo=lo,
+                        scale=self.attn_scale)
         else:
-            K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh)
+            K.attention(q, sess.kc[l], sess.vc[l], o, B=B, Tq=T, Tk=N, H=H, Dh=Dh, scale=self.attn_scale)
         a, sa = self._act(sess, o, "proj")
         w, ws = self._w(lw, "proj")
         K.gemm(a, w, x_att, epi=K.EPI_RESID, bias=lw.proj_b, gamma=lw.ls1, resid=x_act, a_scale=sa, b_scale=ws)

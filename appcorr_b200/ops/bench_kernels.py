@@ -71,7 +71,7 @@ def main(argv=None) -> None:
             xs = torch.empty(a.M, device=dev)
             K.quant_rows_nvfp4(x, x4, xsf, xs)
             w4, (ws, wsf) = K.quantize_weight_nvfp4(w)
-            fn = lambda: K.gemm(x4, w4, out, epi=epi, a_scale=(xs, xsf), b_scale=(ws, wsf))  # noqa: E731
+            fn = lambda: K.gemm(x4, w4, out, epi=epi, bn=a.bn, a_scale=(xs, xsf), b_scale=(ws, wsf))  # noqa: E731
             ref = None
             if a.ref:
                 fa, fb = x4.view(torch.float4_e2m1fn_x2), w4.view(torch.float4_e2m1fn_x2)

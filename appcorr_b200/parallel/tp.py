@@ -77,6 +77,8 @@ class ViTEngineTP(ViTEngine):
 
     def __init__(self, weights: EngineWeights, comm: TPComm, device=None, precision="bf16"):
         super().__init__(weights, device, precision)
+        if self.cfg.padded_head_dim:
+            raise ValueError("tensor parallelism does not support padded attention heads")
         self.comm = comm
         self.world, self.rank = comm.world, comm.rank
         self.local_heads = self.cfg.num_heads // self.world

@@ -714,6 +714,220 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------------- 2-CTA NVFP4 variant
+// NVFP4 x NVFP4 on a CTA pair: one 256 x 256 output tile per cluster with
+// tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 (M = 256, N = 256, K = 64 per MMA),
+// four MMAs per 256-element K stage. Per CTA and stage: its 128 A rows (16 KB), its half of the
+// 256 B rows (16 KB) and block scales (SFA of its rows; SFB of all 256 B rows, or of its own half,
+// see SFB_HALF). Both CTAs stage their scales into their own TMEM (four scale warps each,
+// tcgen05.st); the follower's scale warps arrive on the leader's `sfull`. The leader issues the
+// MMAs once both CTAs' tiles landed (`full`, tx-counted across the pair) and both CTAs' scales are
+// in TMEM, then commits `empty` to both CTAs. TMEM per CTA: one 256-column accumulator (its 128
+// rows x 256 columns) + one scale slot per stage. Loads are plain per-CTA TMA (no multicast).
+// SFB_HALF = 0: every CTA's slot holds the scales of all 256 B rows (8 columns per 64-element
+// step); 1: each CTA's slot holds its own 128 B rows' scales (4 columns per step).
+__device__ __forceinline__ void umma_f4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t tmem_sfa, uint32_t tmem_sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+
+template <int STAGES, int EPI, int SFB_HALF>
+__global__ void __launch_bounds__(gemm_threads<2>(), 1)
+    gemm_f4_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       GemmShape shp, GemmEpilogue ep) {
+  constexpr int BN = 256;                          // output tile width (pair)
+  constexpr int BH = BN / 2;                       // B rows staged per CTA
+  constexpr uint32_t A_BYTES = kBM * 128;          // 128 rows x 256 e2m1
+  constexpr uint32_t B_BYTES = BH * 128;
+  constexpr uint32_t SFA_BYTES = kBM * 16;         // four 512-byte groups
+  constexpr uint32_t SFB_BYTES = (SFB_HALF ? BH : BN) * 16;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  constexpr uint32_t SFB_COLS = (SFB_HALF ? BH : BN) / 8;   // 4 per step per 128 rows
+  constexpr uint32_t SF_COLS = 16 + SFB_COLS;
+  constexpr uint32_t TMEM_COLS = 512;
+  static_assert(BN + STAGES * SF_COLS <= TMEM_COLS, "2-CTA NVFP4 TMEM budget");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+  constexpr uint32_t IDESC = idesc_nvf4_f32(2 * kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);  // leader: A/B of both CTAs
+  uint64_t* empty = full + STAGES;
+  uint64_t* sf_full = empty + STAGES;   // local: this CTA's scale bytes landed
+  uint64_t* sfull = sf_full + STAGES;   // leader: both CTAs' scales are in TMEM
+  uint64_t* tfull = sfull + STAGES;
+  uint64_t* tempty = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), 1);
+      mbar_init(smem_addr(&sf_full[s]), 1);
+      mbar_init(smem_addr(&sfull[s]), 8);   // 4 scale warps x 2 CTAs
+    }
+    mbar_init(smem_addr(tfull), 1);
+    mbar_init(smem_addr(tempty), 2 * kEpiWarps * 32);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_addr(tmem_slot), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (shp.M + 2 * kBM - 1) / (2 * kBM);
+  const int num_n = (shp.N + BN - 1) / BN;
+  const int KB = (shp.K + 255) / 256;
+  const int total = num_m * num_n;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = cluster_id; tile < total; tile += num_clusters) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) goto producer_done;
+          const uint32_t fb = mapa_shared(smem_addr(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx_cluster(fb, 2 * (A_BYTES + B_BYTES));
+          const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
+          tma_load_2d_pair(sa, &tmA, fb, kb * 128, mb * 2 * kBM + rank * kBM);
+          tma_load_2d_pair(sa + A_BYTES, &tmB, fb, kb * 128, nb * BN + rank * BH);
+          const uint32_t sfb = smem_addr(&sf_full[s]);
+          mbar_arrive_expect_tx(sfb, SFA_BYTES + SFB_BYTES);
+          const uint32_t sf = sa + A_BYTES + B_BYTES;
+          bulk_g2s(sf, ep.sfa + ((long)(mb * 2 + rank) * ep.sf_kt + kb * 4) * 512, SFA_BYTES, sfb);
+          if (SFB_HALF) {
+            bulk_g2s(sf + SFA_BYTES, ep.sfb + ((long)(nb * 2 + rank) * ep.sf_kt + kb * 4) * 512, 2048, sfb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              bulk_g2s(sf + SFA_BYTES + j * 2048, ep.sfb + ((long)(nb * 2 + j) * ep.sf_kt + kb * 4) * 512, 2048, sfb);
+          }
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+      }
+      for (int i = 0; i < STAGES; ++i) {
+        if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) break;
+        if (++s == STAGES) { s = 0; ph ^= 1; }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int t_local = 0;
+      for (int tile = cluster_id; tile < total; tile += num_clusters, ++t_local) {
+        if (!mbar_wait(smem_addr(tempty), (t_local & 1) ^ 1, shp.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
+          if (!mbar_wait(smem_addr(&sfull[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+          const uint32_t sf_col = tmem_base + BN + s * SF_COLS;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f4_pair(tmem_base, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
+                         sf_col + k * 4, sf_col + 16 + k * (SFB_COLS / 4), (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair_mask(smem_addr(&empty[s]), 0x3);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair_mask(smem_addr(tfull), 0x3);
+      }
+    }
+  } else if (warp >= 2 + kEpiWarps) {
+    // scale warps: stage s's A scales (4 groups of 4 columns) and B scales (SFB_COLS columns)
+    constexpr int NG = SF_COLS / 4;
+    const int q = warp & 3;
+    const uint32_t sfull_leader = mapa_shared(smem_addr(&sfull[0]), 0);
+    int s = 0;
+    uint32_t ph = 0;
+    for (int tile = cluster_id; tile < total; tile += num_clusters) {
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!mbar_wait(smem_addr(&sf_full[s]), ph, shp.err, kErrTimeoutEpilogue)) { ok = false; break; }
+        const uint8_t* sfs = smem + s * STAGE_BYTES + A_BYTES + B_BYTES;
+        uint32_t r[32], r2[16];
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          int off;
+          if (g < 4) {
+            off = g * 512;
+          } else if (SFB_HALF) {
+            off = SFA_BYTES + (g - 4) * 512;
+          } else {
+            const int gb = g - 4;   // step gb / 2, 128-row B tile gb % 2
+            off = SFA_BYTES + (gb % 2) * 2048 + (gb / 2) * 512;
+          }
+          const uint4 u = *reinterpret_cast<const uint4*>(sfs + off + lane * 16);
+          uint32_t* dst = g < 8 ? &r[4 * g] : &r2[4 * (g - 8)];
+          dst[0] = u.x;
+          dst[1] = u.y;
+          dst[2] = u.z;
+          dst[3] = u.w;
+        }
+        const uint32_t ta = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + BN + s * SF_COLS;
+        tmem_st32(ta, r);
+        if constexpr (NG == 12) tmem_st16(ta + 32, r2);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(sfull_leader + s * 8);
+        if (++s == STAGES) { s = 0; ph ^= 1; }
+      }
+      if (!ok) break;
+    }
+  } else {
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int t_local = 0;
+    const uint32_t tempty_leader = mapa_shared(smem_addr(tempty), 0);
+    for (int tile = cluster_id; tile < total; tile += num_clusters, ++t_local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      if (!mbar_wait(smem_addr(tfull), t_local & 1, shp.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+      run_epilogue<BN, EPI>(taddr, mb * 2 * kBM + rank * kBM + row_in_tile, nb * BN, shp, ep, (warp - 2) / 4,
+                            kEpiWarps / 4);
+      tc_fence_before();
+      mbar_arrive_cluster(tempty_leader);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------------------------ host side
 namespace {
 
@@ -837,6 +1051,39 @@ void launch_gemm_2sm(const at::Tensor& A, const at::Tensor& B, int M, int N, int
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, shp, ep));
 }
 
+template <int STAGES, int EPI, int SFB_HALF>
+void launch_gemm_f4_2sm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const GemmEpilogue& ep,
+                        int* err, int max_ctas, cudaStream_t stream) {
+  constexpr uint32_t STAGE_BYTES = kBM * 128 + 128 * 128 + kBM * 16 + (SFB_HALF ? 128 : 256) * 16;
+  constexpr size_t SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  auto kern = gemm_f4_2sm_kernel<STAGES, EPI, SFB_HALF>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM));
+    configured = true;
+  }
+  TORCH_CHECK(K % 256 == 0, "nvfp4 2-CTA gemm: K % 256 == 0");
+  CUtensorMap ta = make_tmap_u8_2d(A.data_ptr(), M, K / 2, A.stride(0), kBM, 128);
+  CUtensorMap tb = make_tmap_u8_2d(B.data_ptr(), B.size(0), K / 2, B.stride(0), 128, 128);
+  GemmShape shp{M, N, K, err};
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + 255) / 256);
+  int clusters = std::min(tiles, (max_ctas > 0 ? max_ctas : num_sms()) / 2);
+  if (clusters <= 0) return;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(gemm_threads<2>());
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, shp, ep));
+}
+
 // Dispatch on (epilogue, BN). STAGES chosen to fill ~192 KB of shared memory.
 void gemm_dispatch_fp8(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
                        const GemmEpilogue& ep, int* err, int max_ctas) {
@@ -869,12 +1116,15 @@ void gemm_dispatch_fp8(int epi, int bn, const at::Tensor& A, const at::Tensor& B
 void gemm_dispatch_fp4(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
                        const GemmEpilogue& ep, int* err, int max_ctas) {
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  TORCH_CHECK(bn == 128 || bn == 256, "nvfp4 gemm: BN 128 or 256");
+  TORCH_CHECK(bn == 128 || bn == 256 || bn == 512 || bn == 513, "nvfp4 gemm: BN 128, 256 or 512 / 513 (2-CTA)");
+  // bn 512: 2-CTA 256 x 256 tiles, every CTA holding all B scales; 513: each CTA its own half
   switch (epi) {
-#define APPCORR_GEMM4_CASE(E)                                                         \
-  case E:                                                                             \
-    if (bn == 256) launch_gemm<256, 4, E, 2>(A, B, M, N, K, ep, err, max_ctas, st);   \
-    else launch_gemm<128, 6, E, 2>(A, B, M, N, K, ep, err, max_ctas, st);             \
+#define APPCORR_GEMM4_CASE(E)                                                                  \
+  case E:                                                                                      \
+    if (bn == 512) launch_gemm_f4_2sm<5, E, 0>(A, B, M, N, K, ep, err, max_ctas, st);         \
+    else if (bn == 513) launch_gemm_f4_2sm<5, E, 1>(A, B, M, N, K, ep, err, max_ctas, st);    \
+    else if (bn == 256) launch_gemm<256, 4, E, 2>(A, B, M, N, K, ep, err, max_ctas, st);       \
+    else launch_gemm<128, 6, E, 2>(A, B, M, N, K, ep, err, max_ctas, st);                     \
     break;
     APPCORR_GEMM4_CASE(EPI_BF16)
     APPCORR_GEMM4_CASE(EPI_F32)

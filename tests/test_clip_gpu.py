@@ -7,11 +7,13 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def test_clip_engine_matches_module():
+@pytest.mark.parametrize("arch", ["clip_tiny", "clip_tiny_hd104"])
+def test_clip_engine_matches_module(arch):
+    """clip_tiny_hd104 has bigG's head width (104): heads run zero-padded to 128."""
     from appcorr_b200.models.clip import CLIP_MEAN, CLIP_PRESETS, CLIPVision, clip_engine_weights
     from appcorr_b200.models.engine import ViTEngine
 
-    c = CLIP_PRESETS["clip_tiny"]
+    c = CLIP_PRESETS[arch]
     m = CLIPVision(c).init_weights(0).to(DEV)
     eng = ViTEngine(clip_engine_weights(m, DEV), DEV)
     B = 2
