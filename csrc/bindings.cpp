@@ -135,7 +135,7 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
       TORCH_CHECK(N % 3 == 0, "qkv weight rows must be 3*dim");
       ep.dim = N / 3;
     }
-    const int tile_n = bn >= 512 ? 256 : static_cast<int>(bn);  // bn 512 / 513 = 2-CTA 256x256 tile
+    const int tile_n = bn == 512 ? 256 : (bn == 513 ? 128 : static_cast<int>(bn));  // 512 / 513: 2-CTA tiles
     TORCH_CHECK(ep.dim % tile_n == 0 && (ep.kv_dim == 0 || ep.kv_dim % tile_n == 0),
                 "qkv: q and kv widths must be multiples of the tile width");
     TORCH_CHECK(head_dim == 64 || head_dim == 128, "qkv: head_dim must be 64 or 128");

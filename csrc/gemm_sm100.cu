@@ -715,17 +715,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------------- 2-CTA NVFP4 variant
-// NVFP4 x NVFP4 on a CTA pair: one 256 x 256 output tile per cluster with
-// tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 (M = 256, N = 256, K = 64 per MMA),
+// NVFP4 x NVFP4 on a CTA pair: one 256 x BN output tile per cluster with
+// tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 (M = 256, N = BN, K = 64 per MMA),
 // four MMAs per 256-element K stage. Per CTA and stage: its 128 A rows (16 KB), its half of the
-// 256 B rows (16 KB) and block scales (SFA of its rows; SFB of all 256 B rows, or of its own half,
-// see SFB_HALF). Both CTAs stage their scales into their own TMEM (four scale warps each,
-// tcgen05.st); the follower's scale warps arrive on the leader's `sfull`. The leader issues the
-// MMAs once both CTAs' tiles landed (`full`, tx-counted across the pair) and both CTAs' scales are
-// in TMEM, then commits `empty` to both CTAs. TMEM per CTA: one 256-column accumulator (its 128
-// rows x 256 columns) + one scale slot per stage. Loads are plain per-CTA TMA (no multicast).
-// SFB_HALF = 0: every CTA's slot holds the scales of all 256 B rows (8 columns per 64-element
-// step); 1: each CTA's slot holds its own 128 B rows' scales (4 columns per step).
+// BN B rows and block scales (SFA of its own rows; SFB of all BN B rows: the pair's MMA reads the
+// B scales from each CTA's own TMEM). Both CTAs stage their scales into their own TMEM (four scale
+// warps each, tcgen05.st); the follower's scale warps arrive on the leader's `sfull`. The leader
+// issues the MMAs once both CTAs' tiles landed (`full`, tx-counted across the pair) and both CTAs'
+// scales are in TMEM, then commits `empty` to both CTAs. TMEM per CTA: BN = 128 keeps two
+// 128-column accumulators (the epilogue of tile t overlaps the main loop of tile t + 1), BN = 256
+// one. Cross-CTA arrivals that only publish tensor-memory state (scales written, accumulator
+// drained, both complete by tcgen05.wait) are relaxed: a release at cluster scope would make every
+// epilogue thread wait for its global stores. Loads are plain per-CTA TMA (no multicast).
 __device__ __forceinline__ void umma_f4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                              uint32_t tmem_sfa, uint32_t tmem_sfb, uint32_t accumulate) {
   asm volatile(
@@ -737,21 +738,25 @@ __device__ __forceinline__ void umma_f4_pair(uint32_t tmem_d, uint64_t adesc, ui
       : "memory");
 }
 
-template <int STAGES, int EPI, int SFB_HALF>
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(gemm_threads<2>(), 1)
     gemm_f4_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        GemmShape shp, GemmEpilogue ep) {
-  constexpr int BN = 256;                          // output tile width (pair)
   constexpr int BH = BN / 2;                       // B rows staged per CTA
+  constexpr int NACC = BN == 128 ? 2 : 1;
   constexpr uint32_t A_BYTES = kBM * 128;          // 128 rows x 256 e2m1
   constexpr uint32_t B_BYTES = BH * 128;
   constexpr uint32_t SFA_BYTES = kBM * 16;         // four 512-byte groups
-  constexpr uint32_t SFB_BYTES = (SFB_HALF ? BH : BN) * 16;
+  constexpr uint32_t SFB_BYTES = BN * 16;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
-  constexpr uint32_t SFB_COLS = (SFB_HALF ? BH : BN) / 8;   // 4 per step per 128 rows
+  constexpr uint32_t SFB_COLS = BN / 8;            // 4 per 64-element step per 128 B rows
   constexpr uint32_t SF_COLS = 16 + SFB_COLS;
   constexpr uint32_t TMEM_COLS = 512;
-  static_assert(BN + STAGES * SF_COLS <= TMEM_COLS, "2-CTA NVFP4 TMEM budget");
+  static_assert(NACC * BN + STAGES * SF_COLS <= TMEM_COLS, "2-CTA NVFP4 TMEM budget");
   static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
   constexpr uint32_t IDESC = idesc_nvf4_f32(2 * kBM, BN);
 
@@ -761,9 +766,9 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
   uint64_t* empty = full + STAGES;
   uint64_t* sf_full = empty + STAGES;   // local: this CTA's scale bytes landed
   uint64_t* sfull = sf_full + STAGES;   // leader: both CTAs' scales are in TMEM
-  uint64_t* tfull = sfull + STAGES;
-  uint64_t* tempty = tfull + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 1);
+  uint64_t* tfull = sfull + STAGES;     // 2
+  uint64_t* tempty = tfull + 2;         // 2 (leader)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -777,8 +782,10 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
       mbar_init(smem_addr(&sf_full[s]), 1);
       mbar_init(smem_addr(&sfull[s]), 8);   // 4 scale warps x 2 CTAs
     }
-    mbar_init(smem_addr(tfull), 1);
-    mbar_init(smem_addr(tempty), 2 * kEpiWarps * 32);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_addr(&tfull[a]), 1);
+      mbar_init(smem_addr(&tempty[a]), 2 * kEpiWarps);   // one arrival per epilogue warp of each CTA
+    }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -817,13 +824,10 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
           mbar_arrive_expect_tx(sfb, SFA_BYTES + SFB_BYTES);
           const uint32_t sf = sa + A_BYTES + B_BYTES;
           bulk_g2s(sf, ep.sfa + ((long)(mb * 2 + rank) * ep.sf_kt + kb * 4) * 512, SFA_BYTES, sfb);
-          if (SFB_HALF) {
-            bulk_g2s(sf + SFA_BYTES, ep.sfb + ((long)(nb * 2 + rank) * ep.sf_kt + kb * 4) * 512, 2048, sfb);
-          } else {
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
-              bulk_g2s(sf + SFA_BYTES + j * 2048, ep.sfb + ((long)(nb * 2 + j) * ep.sf_kt + kb * 4) * 512, 2048, sfb);
-          }
+          for (int j = 0; j < BN / 128; ++j)
+            bulk_g2s(sf + SFA_BYTES + j * 2048, ep.sfb + ((long)(nb * (BN / 128) + j) * ep.sf_kt + kb * 4) * 512,
+                     2048, sfb);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
       }
@@ -839,8 +843,11 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
       uint32_t ph = 0;
       int t_local = 0;
       for (int tile = cluster_id; tile < total; tile += num_clusters, ++t_local) {
-        if (!mbar_wait(smem_addr(tempty), (t_local & 1) ^ 1, shp.err, kErrTimeoutMma)) break;
+        const int acc = NACC == 2 ? (t_local & 1) : 0;
+        const uint32_t acc_ph = NACC == 2 ? ((t_local >> 1) & 1) : (t_local & 1);
+        if (!mbar_wait(smem_addr(&tempty[acc]), acc_ph ^ 1, shp.err, kErrTimeoutMma)) break;
         tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
@@ -848,16 +855,16 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
           tc_fence_after();
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
-          const uint32_t sf_col = tmem_base + BN + s * SF_COLS;
+          const uint32_t sf_col = tmem_base + NACC * BN + s * SF_COLS;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_f4_pair(tmem_base, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
+            umma_f4_pair(d_tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), IDESC,
                          sf_col + k * 4, sf_col + 16 + k * (SFB_COLS / 4), (kb | k) != 0 ? 1u : 0u);
           umma_commit_pair_mask(smem_addr(&empty[s]), 0x3);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
-        umma_commit_pair_mask(smem_addr(tfull), 0x3);
+        umma_commit_pair_mask(smem_addr(&tfull[acc]), 0x3);
       }
     }
   } else if (warp >= 2 + kEpiWarps) {
@@ -875,15 +882,8 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
         uint32_t r[32], r2[16];
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
-          int off;
-          if (g < 4) {
-            off = g * 512;
-          } else if (SFB_HALF) {
-            off = SFA_BYTES + (g - 4) * 512;
-          } else {
-            const int gb = g - 4;   // step gb / 2, 128-row B tile gb % 2
-            off = SFA_BYTES + (gb % 2) * 2048 + (gb / 2) * 512;
-          }
+          const int gb = g - 4;   // B: step gb / (BN / 128), 128-row B tile gb % (BN / 128)
+          const int off = g < 4 ? g * 512 : SFA_BYTES + (gb % (BN / 128)) * 2048 + (gb / (BN / 128)) * 512;
           const uint4 u = *reinterpret_cast<const uint4*>(sfs + off + lane * 16);
           uint32_t* dst = g < 8 ? &r[4 * g] : &r2[4 * (g - 8)];
           dst[0] = u.x;
@@ -891,13 +891,13 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
           dst[2] = u.z;
           dst[3] = u.w;
         }
-        const uint32_t ta = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + BN + s * SF_COLS;
+        const uint32_t ta = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + NACC * BN + s * SF_COLS;
         tmem_st32(ta, r);
         if constexpr (NG == 12) tmem_st16(ta + 32, r2);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(sfull_leader + s * 8);
+        if (lane == 0) mbar_arrive_cluster_relaxed(sfull_leader + s * 8);
         if (++s == STAGES) { s = 0; ph ^= 1; }
       }
       if (!ok) break;
@@ -906,17 +906,20 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
     int t_local = 0;
-    const uint32_t tempty_leader = mapa_shared(smem_addr(tempty), 0);
+    const uint32_t tempty_leader = mapa_shared(smem_addr(&tempty[0]), 0);
     for (int tile = cluster_id; tile < total; tile += num_clusters, ++t_local) {
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
-      if (!mbar_wait(smem_addr(tfull), t_local & 1, shp.err, kErrTimeoutEpilogue)) break;
+      const int acc = NACC == 2 ? (t_local & 1) : 0;
+      const uint32_t acc_ph = NACC == 2 ? ((t_local >> 1) & 1) : (t_local & 1);
+      if (!mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       run_epilogue<BN, EPI>(taddr, mb * 2 * kBM + rank * kBM + row_in_tile, nb * BN, shp, ep, (warp - 2) / 4,
                             kEpiWarps / 4);
       tc_fence_before();
-      mbar_arrive_cluster(tempty_leader);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster_relaxed(tempty_leader + acc * 8);
     }
   }
   tc_fence_before();
@@ -1051,12 +1054,12 @@ void launch_gemm_2sm(const at::Tensor& A, const at::Tensor& B, int M, int N, int
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, shp, ep));
 }
 
-template <int STAGES, int EPI, int SFB_HALF>
+template <int BN, int STAGES, int EPI>
 void launch_gemm_f4_2sm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const GemmEpilogue& ep,
                         int* err, int max_ctas, cudaStream_t stream) {
-  constexpr uint32_t STAGE_BYTES = kBM * 128 + 128 * 128 + kBM * 16 + (SFB_HALF ? 128 : 256) * 16;
+  constexpr uint32_t STAGE_BYTES = kBM * 128 + (BN / 2) * 128 + kBM * 16 + BN * 16;
   constexpr size_t SMEM = STAGES * STAGE_BYTES + 1024 + 256;
-  auto kern = gemm_f4_2sm_kernel<STAGES, EPI, SFB_HALF>;
+  auto kern = gemm_f4_2sm_kernel<BN, STAGES, EPI>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM));
@@ -1064,9 +1067,9 @@ void launch_gemm_f4_2sm(const at::Tensor& A, const at::Tensor& B, int M, int N, 
   }
   TORCH_CHECK(K % 256 == 0, "nvfp4 2-CTA gemm: K % 256 == 0");
   CUtensorMap ta = make_tmap_u8_2d(A.data_ptr(), M, K / 2, A.stride(0), kBM, 128);
-  CUtensorMap tb = make_tmap_u8_2d(B.data_ptr(), B.size(0), K / 2, B.stride(0), 128, 128);
+  CUtensorMap tb = make_tmap_u8_2d(B.data_ptr(), B.size(0), K / 2, B.stride(0), BN / 2, 128);
   GemmShape shp{M, N, K, err};
-  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + 255) / 256);
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + BN - 1) / BN);
   int clusters = std::min(tiles, (max_ctas > 0 ? max_ctas : num_sms()) / 2);
   if (clusters <= 0) return;
   cudaLaunchConfig_t cfg = {};
@@ -1116,13 +1119,13 @@ void gemm_dispatch_fp8(int epi, int bn, const at::Tensor& A, const at::Tensor& B
 void gemm_dispatch_fp4(int epi, int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K,
                        const GemmEpilogue& ep, int* err, int max_ctas) {
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  TORCH_CHECK(bn == 128 || bn == 256 || bn == 512 || bn == 513, "nvfp4 gemm: BN 128, 256 or 512 / 513 (2-CTA)");
-  // bn 512: 2-CTA 256 x 256 tiles, every CTA holding all B scales; 513: each CTA its own half
+  TORCH_CHECK(bn == 128 || bn == 256 || bn == 512 || bn == 513,
+              "nvfp4 gemm: BN 128, 256, 512 (2-CTA 256 x 256) or 513 (2-CTA 256 x 128)");
   switch (epi) {
 #define APPCORR_GEMM4_CASE(E)                                                                  \
   case E:                                                                                      \
-    if (bn == 512) launch_gemm_f4_2sm<5, E, 0>(A, B, M, N, K, ep, err, max_ctas, st);         \
-    else if (bn == 513) launch_gemm_f4_2sm<5, E, 1>(A, B, M, N, K, ep, err, max_ctas, st);    \
+    if (bn == 512) launch_gemm_f4_2sm<256, 5, E>(A, B, M, N, K, ep, err, max_ctas, st);       \
+    else if (bn == 513) launch_gemm_f4_2sm<128, 6, E>(A, B, M, N, K, ep, err, max_ctas, st);  \
     else if (bn == 256) launch_gemm<256, 4, E, 2>(A, B, M, N, K, ep, err, max_ctas, st);       \
     else launch_gemm<128, 6, E, 2>(A, B, M, N, K, ep, err, max_ctas, st);                     \
     break;

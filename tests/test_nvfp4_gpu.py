@@ -84,6 +84,24 @@ def test_gemm_nvfp4_bias(M, N, Kd, bn):
     _close(out, ref)
 
 
+@pytest.mark.parametrize("bn", [512, 513])
+@pytest.mark.parametrize("M,N,Kd", [(300, 512, 512), (1029, 1536, 1024)])
+def test_gemm_nvfp4_2cta_matches_one_cta(M, N, Kd, bn):
+    """The CTA-pair kernels (256 x 256 and 256 x 128 tiles, cta_group::2) produce the same bytes as
+    the one-CTA 128 x 128 kernel: identical fp32 accumulation order per output."""
+    K = _k()
+    torch.manual_seed(5)
+    a4, a_sf, a_s = _quant(_rand(M, Kd))
+    w4, (w_s, w_sf) = K.quantize_weight_nvfp4(_rand(N, Kd, scale=Kd ** -0.5))
+    bias = _rand(N, scale=0.1)
+    ref = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    out = torch.full((M, N), float("nan"), device=DEV, dtype=torch.bfloat16)
+    K.gemm(a4, w4, ref, bias=bias, a_scale=(a_s, a_sf), b_scale=(w_s, w_sf), bn=128)
+    K.gemm(a4, w4, out, bias=bias, a_scale=(a_s, a_sf), b_scale=(w_s, w_sf), bn=bn)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
 @pytest.mark.parametrize("block,bn", [(64, None), (128, 256)])
 def test_gemm_nvfp4_swiglu_resid_qkv(block, bn):
     K = _k()
