@@ -47,10 +47,10 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
-    ap.add_argument("--batch", type=int, default=8)
-    ap.add_argument("--res", type=int, default=512)
-    ap.add_argument("--keep", type=float, default=0.3)
-    ap.add_argument("--arch", default="vit7b16")
+    ap.add_argument("--batch", type=int, default=None, help="images per GPU (workload default)")
+    ap.add_argument("--res", type=int, default=None)
+    ap.add_argument("--keep", type=float, default=None)
+    ap.add_argument("--arch", default=None)
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-graph", action="store_true",
                     help="time the device step eagerly instead of replaying its CUDA graph")
@@ -58,15 +58,60 @@ def parse_args():
     ap.add_argument("--precision", default="nvfp4", choices=["bf16", "fp8", "nvfp4"],
                     help="GEMM operand precision of the approx and correct passes (ours; the reference arm "
                          "runs its default bf16 path: its fp8/fp4 approx controllers need torchao)")
-    ap.add_argument("--workload", default="vit7b_seg", choices=["vit7b_seg", "vlm"],
-                    help="vit7b_seg: the headline ViT-7B linear-head segmentation config; vlm: Qwen2.5-VL-7B-shaped "
-                         "prefill with KV rewrite (1 image 1024^2 + 128 text tokens, keep 0.25; ranks data-parallel)")
-    ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
+    ap.add_argument("--workload", default="vit7b_seg", choices=["vit7b_seg", "vitl_cls", "vitl_detr", "vlm", "cpu_loopback"],
+                    help="vit7b_seg: the headline ViT-7B linear-head segmentation config; vitl_cls: ViT-L/16 classifier, "
+                         "224^2, 64 images per GPU, 3-level pyramid, keep 0.25 (data-parallel); vitl_detr: ViT-L/16 + "
+                         "6-layer DETR decoder (300 queries, 80 classes), 1024^2, batch 4, keep 0.5, 3x3 windows + "
+                         "global source; vlm: Qwen2.5-VL-7B-shaped prefill with KV rewrite (1 image 1024^2 + 128 text "
+                         "tokens, keep 0.25); cpu_loopback: ViT-S/16 fp32 on the CPU over loopback TCP, 224^2, batch 4, "
+                         "2-level pyramid, keep 0.5 (p50 / p99 latency)")
+    ap.add_argument("--parallel", default=None, choices=["tp", "dp"],
                     help="N > 1: tensor-parallel over N GPUs (one request batch) or N data-parallel replicas")
-    return ap.parse_args()
+    a = ap.parse_args()
+    wl = WORKLOADS.get(a.workload, WORKLOADS["vit7b_seg"])
+    for k in ("batch", "res", "keep", "arch", "parallel"):
+        if getattr(a, k) is None:
+            setattr(a, k, wl[k])
+    return a
+
+
+# ----------------------------------------------------------------------------- workloads
+# the BASELINE configurations other than the headline (vit7b_seg): model, backbone, image side,
+# images per GPU, pyramid levels (coarse first), keep ratio, default parallelism
+WORKLOADS = {
+    "vit7b_seg": dict(model="dinov3_segmentor_linhead", arch="vit7b16", res=512, batch=8, levels=[1, 0], keep=0.3,
+                      parallel="tp", label="DINOv3 ViT-7B/16 + linear seg head (150 cls)",
+                      profile="dinov3_ade20k_linhead_official"),
+    "vitl_cls": dict(model="dinov3_classifier", arch="vitl16", res=224, batch=64, levels=[2, 1, 0], keep=0.25,
+                     parallel="dp", label="DINOv3 ViT-L/16 + linear classifier (1000 cls)", profile="fixed_image_shape",
+                     metric="images/s, ViT-L/16 data-parallel at 1/2/4/8 B200 (224^2, 3-level pyramid, keep 0.25)"),
+    "vitl_detr": dict(model="dinov3_detector", arch="vitl16", res=1024, batch=4, levels=[1, 0], keep=0.5,
+                      parallel="tp", label="DINOv3 ViT-L/16 (3x3 windows + global source) + 6-layer DETR, 300 q, 80 cls",
+                      profile="fixed_image_shape",
+                      metric="p50/p99 latency & images/s, ViT-L + DETR decoder, 1024^2 batch 4"),
+}
 
 
 # ----------------------------------------------------------------------------- data
+def synthetic_pyramid_levels(batch: int, res: int, levels, seed: int):
+    """Clipped N(128, 60^2) images -> (images, base uint8, [int16 residual of each finer level,
+    coarse first]) for a Laplacian pyramid over `levels` (e.g. [2, 1, 0])."""
+    sys.path.insert(0, ROOT)
+    from appcorr_b200.policies.transmission.pyramid import pyr_down, pyr_up
+
+    rng = np.random.default_rng(seed)
+    imgs = np.clip(rng.normal(128, 60, size=(batch, res, res, 3)), 0, 255).astype(np.uint8)
+    pyr = [imgs]
+    for _ in range(levels[0]):
+        pyr.append(np.stack([pyr_down(im) for im in pyr[-1]]))
+    base = pyr[levels[0]]
+    resid = []
+    for lvl in levels[1:]:  # residual of level lvl against the reconstruction from level lvl + 1
+        fine, coarse = pyr[lvl], pyr[lvl + 1]
+        resid.append(np.stack([f.astype(np.int16) - pyr_up(c).astype(np.int16) for f, c in zip(fine, coarse)]))
+    return imgs, base, resid
+
+
 def synthetic_pyramid(batch: int, res: int, seed: int):
     """Clipped N(128, 60^2) RGB images -> (images, base uint8, residual int16) on the host."""
     sys.path.insert(0, ROOT)
@@ -180,13 +225,17 @@ def make_config(args, world: int = 1):
     from appcorr_b200.common.protocol import ExperimentConfig
 
     tp = world if (world > 1 and args.parallel == "tp") else 1
+    wl = WORKLOADS[args.workload]
+    prof = {"backbone_arch": args.arch, "server_inference_mode": "whole"}
+    if args.workload == "vitl_detr":
+        prof.update({"num_queries": 300, "num_classes": 80, "decoder_layers": 6, "detector_windows": 3})
     return ExperimentConfig(
         tp_size=tp, precision=_cfg_precision(args), correct_precision=_cfg_precision(args),
-        exp_id="bench", model_name="dinov3_segmentor_linhead", batch_size=args.batch,
-        image_shape=(args.res, args.res, 3), input_profile_name="dinov3_ade20k_linhead_official",
-        input_profile_kwargs={"backbone_arch": args.arch, "server_inference_mode": "whole"},
+        exp_id="bench", model_name=wl["model"], batch_size=args.batch,
+        image_shape=(args.res, args.res, 3), input_profile_name=wl["profile"],
+        input_profile_kwargs=prof,
         scheduler_policy_name="GroupTrigger", transmission_policy_name="ProgressiveLaplacian",
-        transmission_kwargs={"pyramid_levels": [1, 0], "num_groups": 1, "grouping_strategy": "grid"},
+        transmission_kwargs={"pyramid_levels": wl["levels"], "num_groups": 1, "grouping_strategy": "grid"},
         appcorr_kwargs={"token_keep_ratio": args.keep, "server_pscore": "cls_attn_prob"})
 
 
@@ -206,20 +255,22 @@ def run_mine(args, rank, world):
     ex.load_model(cfg.model_name, cfg)
     L = ex.cfg.depth
     # tensor parallel: every rank serves the same request; data parallel: independent requests
-    imgs, base, resid = synthetic_pyramid(args.batch, args.res, seed=0 if tp else rank)
+    levels = WORKLOADS[args.workload]["levels"]
+    imgs, base, resid = synthetic_pyramid_levels(args.batch, args.res, levels, seed=0 if tp else rank)
     base_h = torch.from_numpy(base).pin_memory()
-    res_h = torch.from_numpy(resid).pin_memory()
+    res_hs = [torch.from_numpy(r).pin_memory() for r in resid]
+    res_h = res_hs if len(res_hs) > 1 else res_hs[0]
     task = Task(task_id=0, request_id=0, payload=[], instructions=[])
 
     # ---- device-resident variant for the kernel-time measurement
     base_d = base_h.to(dev)
-    res_d = res_h.to(dev)
+    res_d = [r.to(dev) for r in res_hs] if len(res_hs) > 1 else res_hs[0].to(dev)
 
     def device_step(ctx):
-        ex.preprocess(PyramidBatch(base_d, None), task, ctx, cfg)
+        ex.preprocess(PyramidBatch(base_d, None, levels=levels), task, ctx, cfg)
         ex.prepare_tokens(task, ctx, cfg)
         ex.approx_forward({"layers": (0, L)}, ctx, cfg)
-        ex.preprocess(PyramidBatch(base_d, res_d), task, ctx, cfg)
+        ex.preprocess(PyramidBatch(base_d, res_d, levels=levels), task, ctx, cfg)
         ex.prepare_tokens(task, ctx, cfg)
         ex.correct_forward({"layers": (0, L), "group_id": 1}, ctx, cfg)
         ex.head_inference(task, ctx, cfg)
@@ -287,15 +338,17 @@ def run_mine(args, rank, world):
     e2e = None
     if not args.no_e2e:
         n_e2e = args.e2e_steps or max(3, args.steps)
-        h2d = base_h.numel() * base_h.element_size() + res_h.numel() * res_h.element_size()
-        d2h = args.batch * args.res * args.res  # uint8 labels
+        h2d = base_h.numel() * base_h.element_size() + sum(r.numel() * r.element_size() for r in res_hs)
+        d2h = {"vit7b_seg": args.batch * args.res * args.res,          # uint8 labels
+               "vitl_cls": args.batch * 5 * (8 + 4),                   # top-5 (index, probability)
+               "vitl_detr": args.batch * 100 * (4 + 8 + 16)}[args.workload]  # 100 x (score, label, box)
         ctx2 = {}
 
         def e2e_step():
-            ex.preprocess(PyramidBatch(base_h, None), task, ctx2, cfg)
+            ex.preprocess(PyramidBatch(base_h, None, levels=levels), task, ctx2, cfg)
             ex.prepare_tokens(task, ctx2, cfg)
             ex.approx_forward({"layers": (0, L)}, ctx2, cfg)
-            ex.preprocess(PyramidBatch(base_h, res_h), task, ctx2, cfg)
+            ex.preprocess(PyramidBatch(base_h, res_h, levels=levels), task, ctx2, cfg)
             ex.prepare_tokens(task, ctx2, cfg)
             ex.correct_forward({"layers": (0, L), "group_id": 1}, ctx2, cfg)
             ex.head_inference(task, ctx2, cfg)
@@ -316,7 +369,9 @@ def run_mine(args, rank, world):
         e1.record()
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / n_e2e, world)
-        assert len(out) == args.batch and out[0]["mask"].shape == (args.res, args.res)
+        assert len(out) == args.batch
+        if args.workload == "vit7b_seg":
+            assert out[0]["mask"].shape == (args.res, args.res)
         lat.sort()
         e2e = {"value": round(args.batch * (1 if tp else world) * 1e3 / e2e_ms, 3), "unit": "images/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
@@ -429,6 +484,53 @@ def run_vlm(args, rank, world):
                        "parallelism": (f"tp{world}" if tp > 1 else f"dp{world}") if world > 1 else "single",
                        "llm_layers": c.depth},
             "gpu_launches": int(launches * args.steps), "clocks": clk, "e2e": e2e}))
+
+
+# ----------------------------------------------------------------------------- CPU loopback
+def run_cpu_loopback(args) -> None:
+    """the CPU fp32 server (ViT-S/16) and the mobile client over loopback TCP,
+    224^2 batch 4, 2-level pyramid, top 50% corrected by residual energy; the client's measured
+    request latencies (send of the first patch to the result) give p50 / p99."""
+    import socket
+    import tempfile
+
+    def port():
+        with socket.socket() as so:
+            so.bind(("127.0.0.1", 0))
+            return so.getsockname()[1]
+
+    sys.path.insert(0, ROOT)
+    from appcorr_b200.mobile.main import load_config, run_mobile
+
+    rp, sp = port(), port()
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", PYTHONPATH=ROOT)
+    srv = subprocess.Popen([sys.executable, "-m", "offload.server.main", "--recv-port", str(rp), "--send-port", str(sp),
+                            "--listen-host", "127.0.0.1", "--device", "cpu", "--group-port", str(port())],
+                           cwd=ROOT, env=env, stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+    try:
+        time.sleep(3)
+        cfg = load_config(os.path.join(ROOT, "offload/config/cpu_vits16_loopback_keep05.json"),
+                          [f"dataset_kwargs.num_batches={args.steps + 1}"])
+        with tempfile.TemporaryDirectory() as logs:
+            rc = run_mobile("127.0.0.1", rp, sp, None, None, num_request=args.steps, num_warmup=args.warmup,
+                            config=cfg, log_root=logs)
+            runs = os.listdir(logs)
+            summ = json.load(open(os.path.join(logs, runs[0], "summary.json"))) if runs else {}
+    finally:
+        srv.terminate()
+        try:
+            srv.wait(timeout=30)
+        except subprocess.TimeoutExpired:
+            srv.kill()
+    lat = summ.get("latency_ms", {})
+    print(json.dumps({"metric": "CPU fp32 end-to-end latency over loopback TCP (p50 ms), ViT-S/16 224^2 batch 4",
+                      "value": round(float(lat.get("p50", 0.0)), 3), "unit": "ms", "n_gpus": 0, "steps": args.steps,
+                      "warmup": args.warmup, "p50_ms": lat.get("p50"), "p99_ms": lat.get("p99"),
+                      "mean_ms": lat.get("mean"), "images_per_s": summ.get("images_per_s"),
+                      "higher_is_better": False, "scaling": "none", "vs_baseline": None, "dtype": "fp32",
+                      "data": "synthetic images, random-init weights", "rc": rc,
+                      "config": {"model": "DINOv3 ViT-S/16 + linear classifier", "global_batch": 4, "image": "224x224",
+                                 "pyramid_levels": [1, 0], "keep_ratio": 0.5, "transport": "loopback TCP"}}))
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -558,6 +660,10 @@ def main():
     if args.gpus != world_env and world_env == 1 and args.gpus > 1:
         print(json.dumps({"error": "for --gpus > 1 launch with torch.distributed.run"}))
         sys.exit(2)
+    if args.workload == "cpu_loopback":  # host-only: no device, no process group
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_cpu_loopback(args)
+        return
     rank, world, local = dist_setup(args.gpus)
     if args.workload == "vlm":
         if args.impl == "reference":
@@ -571,13 +677,24 @@ def main():
 
             dist.destroy_process_group()
         return
+    wl = WORKLOADS[args.workload]
+    metric = wl.get("metric", BASELINE_METRIC)
     parallelism = (f"{args.parallel}{world}" if world > 1 else "single")
     images_per_step = args.batch * (world if (world > 1 and args.parallel == "dp") else 1)
-    cfg_out = {"model": "DINOv3 ViT-7B/16 + linear seg head (150 cls)" if args.arch == "vit7b16" else args.arch,
+    cfg_out = {"model": wl["label"] if args.arch == wl["arch"] else args.arch, "workload": args.workload,
                "global_batch": images_per_step, "per_gpu_batch": args.batch, "seq_len": (args.res // 16) ** 2 + 5,
-               "image": f"{args.res}x{args.res}", "keep_ratio": args.keep, "pyramid_levels": [1, 0],
+               "image": f"{args.res}x{args.res}", "keep_ratio": args.keep, "pyramid_levels": wl["levels"],
                "parallelism": parallelism, "precision": args.precision if args.impl == "mine" else "bf16",
                "l2": "working set > L2 each step (13.4 GB bf16 weights + 8 GB K/V/increment caches)"}
+    if args.impl == "reference" and args.workload != "vit7b_seg":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm runs the headline workload "
+                              "(vit7b_seg); this workload has no reference run"}))
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     if args.impl == "reference":
         try:
             res, why = run_reference(args, rank, world)
@@ -610,7 +727,7 @@ def main():
     cfg_out["cuda_graph"] = graphed
     if rank == 0:
         value = images_per_step * 1e3 / ms
-        line = {"metric": BASELINE_METRIC, "value": round(value, 3), "unit": "images/s", "n_gpus": world,
+        line = {"metric": metric, "value": round(value, 3), "unit": "images/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
                 "p50_ms": round(per_step[len(per_step) // 2], 3),
                 "p99_ms": round(per_step[min(len(per_step) - 1, int(0.99 * len(per_step)))], 3),
@@ -623,6 +740,9 @@ def main():
                           "e4m3 attn.proj, fp32 accumulate, bf16 attention and residual stream"),
                 "data": "synthetic images (clipped N(128,60^2)), random-init weights",
                 "config": cfg_out, "gpu_launches": int(launches * args.steps), "clocks": clk, "e2e": e2e}
+        if args.workload != "vit7b_seg":
+            line["scaling"] = "weak" if args.parallel == "dp" or world == 1 else "strong"
+            line["dtype"] = args.precision
         print(json.dumps(line))
     if world > 1:
         import torch.distributed as dist
