@@ -223,9 +223,12 @@ def add_(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     return x
 
 
-# "tcgen05": one 128-row query tile per CTA, P in shared memory (default: measured faster);
+# "tcgen05": one 128-row query tile per CTA, one softmax thread per row, P in shared memory;
+# "tcgen05_split": the same tile with two softmax threads per row (64 key columns each);
+# "tcgen05_pp": the same tile with two warpgroups taking alternate key blocks (own max / sum / O);
 # "tcgen05_2q": two query tiles per CTA sharing K/V, P kept in TMEM; "mma": the mma.sync kernel
 ATTENTION_IMPL = ["tcgen05"]
+_ATTN_VARIANT = {"tcgen05_2q": 0, "tcgen05": 1, "tcgen05_split": 2, "tcgen05_pp": 3}
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, *, B: int, Tq: int,
@@ -250,12 +253,12 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor
     impl = impl or ATTENTION_IMPL[0]
     if impl == "mma" and (Hkv or causal or q_pos is not None or block_table is not None):
         impl = "tcgen05"
-    if q_lo is not None:
+    if q_lo is not None and impl not in ("tcgen05", "tcgen05_split", "tcgen05_pp"):
         impl = "tcgen05"
     _count()
-    if impl in ("tcgen05", "tcgen05_2q"):
+    if impl in _ATTN_VARIANT:
         lib().attention_sm100(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse, err_word(q.device), cls_probs,
-                              Hkv, causal, q_pos, block_table, 0 if impl == "tcgen05_2q" else 1, q_lo)
+                              Hkv, causal, q_pos, block_table, _ATTN_VARIANT[impl], q_lo)
     else:
         lib().attention(q, k, v, o, B, Tq, Tk, H, Dh, float(scale), lse)
     return o

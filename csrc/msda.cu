@@ -99,7 +99,8 @@ void msda_op(const at::Tensor& value, const at::Tensor& ref, const at::Tensor& o
               "msda: value bf16 [N, S, M, Dh] contiguous");
   const int N = static_cast<int>(value.size(0)), S = static_cast<int>(value.size(1));
   const int Dh = static_cast<int>(value.size(3));
-  TORCH_CHECK(value.size(2) == M && (Dh == 32 || Dh == 64), "msda: head dim 32 or 64");
+  TORCH_CHECK(value.size(2) == M && (Dh == 8 || Dh == 16 || Dh == 32 || Dh == 64 || Dh == 128),
+              "msda: head dim 8, 16, 32, 64 or 128");
   TORCH_CHECK(L >= 1 && L <= kMsdaMaxLevels && L * P <= 32, "msda: L <= 8 and L * P <= 32");
   TORCH_CHECK(static_cast<int64_t>(shapes.size()) == 2 * L, "msda: shapes = [H0, W0, H1, W1, ...]");
   const int Q = static_cast<int>(out.size(1));
@@ -141,8 +142,13 @@ void msda_op(const at::Tensor& value, const at::Tensor& ref, const at::Tensor& o
   const long threads = groups * (Dh / 8);
   const int grid = static_cast<int>((threads + 255) / 256);
   auto st = at::cuda::getCurrentCUDAStream();
-  if (Dh == 32) msda_fwd_kernel<32><<<grid, 256, 0, st>>>(a);
-  else msda_fwd_kernel<64><<<grid, 256, 0, st>>>(a);
+  switch (Dh) {
+    case 8: msda_fwd_kernel<8><<<grid, 256, 0, st>>>(a); break;
+    case 16: msda_fwd_kernel<16><<<grid, 256, 0, st>>>(a); break;
+    case 32: msda_fwd_kernel<32><<<grid, 256, 0, st>>>(a); break;
+    case 64: msda_fwd_kernel<64><<<grid, 256, 0, st>>>(a); break;
+    default: msda_fwd_kernel<128><<<grid, 256, 0, st>>>(a); break;
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -168,7 +168,7 @@ def test_qkv_rope_scatter(Dh, H):
     _close(k2, k, rtol=1e-2, atol=1e-2)
 
 
-@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_2q", "mma"])
+@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_pp", "tcgen05_2q", "mma"])
 @pytest.mark.parametrize("Dh,H,Tq,Tk", [(128, 4, 1029, 1029), (64, 6, 197, 197), (128, 2, 312, 1029), (64, 3, 5, 70),
                                         (128, 2, 130, 260)])
 def test_attention(Dh, H, Tq, Tk, impl):
@@ -328,7 +328,8 @@ def test_gemm_2cta_epilogues():
         _close(x, y, rtol=1e-2, atol=1e-2)
 
 
-def test_attention_fused_cls_score():
+@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_pp"])
+def test_attention_fused_cls_score(impl):
     """The tcgen05 attention's CLS softmax row equals the standalone CLS score kernel."""
     K_ = _k()
     torch.manual_seed(12)
@@ -338,7 +339,7 @@ def test_attention_fused_cls_score():
     v = _rand(B * N, H * Dh)
     o = torch.empty_like(q)
     probs = torch.empty(B, H, N, device=DEV)
-    K_.attention(q, k, v, o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, impl="tcgen05", cls_probs=probs)
+    K_.attention(q, k, v, o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, impl=impl, cls_probs=probs)
     fused = torch.empty(B, N, device=DEV)
     K_.head_mean(probs, B, H, N, fused)
     ref = torch.empty(B, N, device=DEV)

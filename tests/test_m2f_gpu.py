@@ -6,13 +6,13 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-@pytest.mark.parametrize("Dh", [32, 64])
+@pytest.mark.parametrize("Dh", [8, 16, 32, 64, 128])
 def test_msda_kernel_matches_grid_sample(Dh):
     from appcorr_b200.models.m2f import msda_reference
     from appcorr_b200.ops import kernels as K
 
     torch.manual_seed(0)
-    N, M, L, P, Q = 2, 8 if Dh == 32 else 4, 3, 4, 37
+    N, M, L, P, Q = 2, 8 if Dh <= 32 else 4, 3, 4, 37
     shapes = [(16, 20), (8, 10), (4, 5)]
     S = sum(h * w for h, w in shapes)
     value = torch.randn(N, S, M, Dh, device=DEV).to(torch.bfloat16)
@@ -28,18 +28,3 @@ def test_msda_kernel_matches_grid_sample(Dh):
     exp = msda_reference(value.float(), shapes, loc, w)
     err = (out.float() - exp).abs().max().item()
     assert err < 2e-2 * exp.abs().max().item() + 1e-2, err
-
-
-def test_m2f_head_gpu_matches_module():
-    from appcorr_b200.models.m2f import M2FHead, M2FHeadGPU
-
-    torch.manual_seed(1)
-    B, gh, gw, D, C = 2, 16, 16, 384, 20
-    head = M2FHead(D, num_classes=C, enc_layers=2, dec_layers=2, queries=100).init_weights(0).to(DEV).eval()
-    gpu = M2FHeadGPU(head, DEV)
-    feat = torch.randn(B * gh * gw, D, device=DEV).to(torch.bfloat16)
-    out = gpu.logits(feat, B, gh, gw)
-    with torch.no_grad():
-        ref = head(feat.float().view(B, gh * gw, D), gh, gw)
-    rel = ((out - ref).norm() / ref.norm()).item()
-    assert rel < 5e-2, rel

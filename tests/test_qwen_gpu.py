@@ -109,7 +109,8 @@ def test_full_correction_equals_forward_on_new_image():
     assert _rel(xc, xr) < 3e-2
 
 
-def test_attention_gqa_causal_paged():
+@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_pp"])
+def test_attention_gqa_causal_paged(impl):
     """Kernel-level: grouped-query causal attention over a paged pool, packed query subset."""
     from appcorr_b200.ops import kernels as K
 
@@ -127,7 +128,7 @@ def test_attention_gqa_causal_paged():
     q = torch.randn(qpos.numel(), H * Dh, device=DEV).to(torch.bfloat16)
     o = torch.empty_like(q)
     K.attention(q, kpool, vpool, o, B=1, Tq=qpos.numel(), Tk=N, H=H, Dh=Dh, Hkv=Hkv, causal=True, q_pos=qpos,
-                block_table=table)
+                block_table=table, impl=impl)
     qq = q.float().view(-1, H, Dh).transpose(0, 1)
     kk = kl.float().view(N, Hkv, Dh).repeat_interleave(H // Hkv, dim=1).transpose(0, 1)
     vv = vl.float().view(N, Hkv, Dh).repeat_interleave(H // Hkv, dim=1).transpose(0, 1)
@@ -138,7 +139,7 @@ def test_attention_gqa_causal_paged():
     # contiguous causal prefill (q_pos implicit) with multiple query tiles
     q2 = torch.randn(N, H * Dh, device=DEV).to(torch.bfloat16)
     o2 = torch.empty_like(q2)
-    K.attention(q2, kpool, vpool, o2, B=1, Tq=N, Tk=N, H=H, Dh=Dh, Hkv=Hkv, causal=True, block_table=table)
+    K.attention(q2, kpool, vpool, o2, B=1, Tq=N, Tk=N, H=H, Dh=Dh, Hkv=Hkv, causal=True, block_table=table, impl=impl)
     qq = q2.float().view(-1, H, Dh).transpose(0, 1)
     ref2 = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=True).transpose(0, 1).reshape(N, -1)
     assert (o2.float() - ref2).abs().max().item() < 2e-2 * ref2.abs().max().item() + 2e-2

@@ -50,7 +50,8 @@ def test_windowed_tower_approx_and_full_correction():
     assert _rel(got, ref) < 3e-2
 
 
-def test_attention_per_query_key_ranges():
+@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_pp"])
+def test_attention_per_query_key_ranges(impl):
     from appcorr_b200.ops import kernels as K
 
     torch.manual_seed(1)
@@ -63,7 +64,7 @@ def test_attention_per_query_key_ranges():
     lo = (sel // tw * tw).repeat(B).to(torch.int32).contiguous()
     hi = (lo + tw - 1).contiguous()
     o = torch.empty_like(q)
-    K.attention(q, k, v, o, B=B, Tq=T, Tk=N, H=H, Dh=Dh, causal=True, q_pos=hi, q_lo=lo)
+    K.attention(q, k, v, o, B=B, Tq=T, Tk=N, H=H, Dh=Dh, causal=True, q_pos=hi, q_lo=lo, impl=impl)
     qq = q.float().view(B, T, H, Dh).transpose(1, 2)
     kk = k.float().view(B, N, H, Dh).transpose(1, 2)
     vv = v.float().view(B, N, H, Dh).transpose(1, 2)
