@@ -511,7 +511,7 @@ class ViTEngine:
             lse = sess.extra.get("lse")
             if lse is None:
                 lse = sess.extra["lse"] = torch.empty(B, H, N, device=self.device, dtype=torch.float32)
-            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, lse=lse, impl="tcgen05",
+            K.attention(sess.q, sess.kc[l], sess.vc[l], sess.o, B=B, Tq=N, Tk=N, H=H, Dh=Dh, lse=lse,
                         scale=sc)
             K.attn_colsum_pscore(sess.q, sess.kc[l], lse, B=B, N=N, H=H, Dh=Dh, probs=sess.ps_scratch, out=score_out,
                                  scale=sc)

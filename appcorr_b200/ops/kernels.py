@@ -223,12 +223,12 @@ def add_(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     return x
 
 
-# "tcgen05": one 128-row query tile per CTA, one softmax thread per row, P in shared memory;
-# "tcgen05_split": the same tile with two softmax threads per row (64 key columns each);
-# "tcgen05_pp": the same tile with two warpgroups taking alternate key blocks (own max / sum / O);
+# "tcgen05_split" (default: measured fastest): one 128-row query tile per CTA, two softmax threads
+# per row (64 key columns each), P in TMEM, 3-stage K/V ring;
+# "tcgen05": the same tile with one softmax thread per row, P in shared memory;
 # "tcgen05_2q": two query tiles per CTA sharing K/V, P kept in TMEM; "mma": the mma.sync kernel
-ATTENTION_IMPL = ["tcgen05"]
-_ATTN_VARIANT = {"tcgen05_2q": 0, "tcgen05": 1, "tcgen05_split": 2, "tcgen05_pp": 3}
+ATTENTION_IMPL = ["tcgen05_split"]
+_ATTN_VARIANT = {"tcgen05_2q": 0, "tcgen05": 1, "tcgen05_split": 2}
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, *, B: int, Tq: int,
@@ -253,7 +253,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor
     impl = impl or ATTENTION_IMPL[0]
     if impl == "mma" and (Hkv or causal or q_pos is not None or block_table is not None):
         impl = "tcgen05"
-    if q_lo is not None and impl not in ("tcgen05", "tcgen05_split", "tcgen05_pp"):
+    if q_lo is not None and impl not in ("tcgen05", "tcgen05_split"):
         impl = "tcgen05"
     _count()
     if impl in _ATTN_VARIANT:

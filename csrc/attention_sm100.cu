@@ -723,333 +723,6 @@ __global__ void __launch_bounds__(kFaSThreads, 1)
   }
 }
 
-// ------------------------------------------------------------------------- ping-pong variant
-// One 128-row query tile per CTA, two softmax warpgroups that take alternate key blocks:
-// warps 2..5 the even blocks, warps 6..9 the odd ones. Each warpgroup keeps its own running max
-// and sum and its own O accumulator in TMEM (block j: S / P in buffer j & 1, PV into O[j & 1]),
-// exactly like two independent flash-attention passes over the two halves of the key set, so
-// their softmax chains run side by side with no per-block exchange; at the end the two partial
-// results are merged with the usual log-sum-exp rescaling (each warpgroup writes half of the
-// output columns). K/V: 3-stage TMA ring; P (bf16) is written back into its S columns and read
-// from TMEM as the A operand of PV; MMA issue order S_0, S_1, PV_0, S_2, PV_1, ... (MMAs of one
-// thread complete in issue order, so S_{j+2} may overwrite P_j once PV_j is issued).
-// TMEM: S0 [0, 128), S1 [128, 256), O0 [256, 256 + DH), O1 [256 + DH, 256 + 2 DH).
-constexpr int kFaPThreads = 320;
-
-template <int DH>
-__global__ void __launch_bounds__(kFaPThreads, 1)
-    fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, FaParams p) {
-  constexpr int NCH = DH / 64;
-  constexpr uint32_t CHUNK_BYTES = 128 * 128;
-  constexpr uint32_t Q_BYTES = NCH * CHUNK_BYTES;
-  constexpr uint32_t KV_BYTES = NCH * CHUNK_BYTES;
-  constexpr int NST = 3;
-  constexpr uint32_t IDESC_S = idesc_bf16_f32(kFaBM, kFaBN);
-  constexpr uint32_t IDESC_O = idesc_bf16_f32_b(kFaBM, DH, true);
-  constexpr uint32_t TMEM_COLS = 512;
-  constexpr uint32_t O_COL = 2 * kFaBN;
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + Q_BYTES;
-  uint8_t* sV = sK + NST * KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NST * KV_BYTES);
-  uint64_t* q_full = bars;           // 1
-  uint64_t* kv_full = bars + 1;      // NST
-  uint64_t* kv_empty = bars + 4;     // NST
-  uint64_t* s_full = bars + 7;       // 2 (per buffer = per warpgroup)
-  uint64_t* p_full = bars + 9;       // 2
-  uint64_t* p_empty = bars + 11;     // 2 (PV into O[w] completed)
-  uint64_t* o_full = bars + 13;      // 1
-  uint64_t* x_fin = bars + 14;       // [quadrant] final (max, sum) exchange
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
-  __shared__ int s_nkb, s_kb0;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qt * kFaBM;
-  const int kvh = h / (p.H / p.Hkv);
-
-  if (warp == 0 && lane == 0) {
-    mbar_init(smem_addr(q_full), 1);
-    for (int i = 0; i < NST; ++i) {
-      mbar_init(smem_addr(&kv_full[i]), 1);
-      mbar_init(smem_addr(&kv_empty[i]), 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_addr(&s_full[i]), 1);
-      mbar_init(smem_addr(&p_full[i]), kFaBM);
-      mbar_init(smem_addr(&p_empty[i]), 1);
-    }
-    mbar_init(smem_addr(o_full), 1);
-    for (int i = 0; i < 4; ++i) mbar_init(smem_addr(&x_fin[i]), 64);
-    fence_barrier_init();
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_addr(tmem_slot), TMEM_COLS);
-    tmem_relinquish();
-  }
-  if (warp == 2) {
-    int nk = (p.Tk + kFaBN - 1) / kFaBN;
-    if (p.causal) {
-      int mq = 0;
-      for (int r = lane; r < kFaBM; r += 32) {
-        const int qi = min(q0 + r, p.Tq - 1);
-        mq = max(mq, p.q_pos ? p.q_pos[(long)b * p.Tq + qi] : qi + p.Tk - p.Tq);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mq = max(mq, __shfl_xor_sync(0xffffffffu, mq, o));
-      nk = max(1, min(nk, mq / kFaBN + 1));
-    }
-    int kb0 = 0;
-    if (p.q_lo) {
-      int lo = 0x7FFFFFFF;
-      for (int r = lane; r < kFaBM; r += 32) lo = min(lo, p.q_lo[(long)b * p.Tq + min(q0 + r, p.Tq - 1)]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-      kb0 = min(max(lo, 0) / kFaBN, nk - 1);
-    }
-    if (lane == 0) {
-      s_nkb = nk - kb0;
-      s_kb0 = kb0;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const int nkb = s_nkb;
-  const int kb0 = s_kb0;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      const uint32_t qb = smem_addr(q_full);
-      mbar_arrive_expect_tx(qb, Q_BYTES);
-      for (int c = 0; c < NCH; ++c)
-        tma_load_2d(smem_addr(sQ + c * CHUNK_BYTES), &tmQ, qb, h * DH + c * 64, b * p.Tq + q0);
-      for (int j = 0; j < nkb; ++j) {
-        const int s = j % NST;
-        if (!mbar_wait(smem_addr(&kv_empty[s]), ((j / NST) & 1) ^ 1, p.err, kErrTimeoutProducer)) break;
-        const uint32_t fb = smem_addr(&kv_full[s]);
-        mbar_arrive_expect_tx(fb, 2 * KV_BYTES);
-        const int jb = kb0 + j;
-        const int row = p.block_table ? p.block_table[(long)b * p.max_blocks + jb] * kFaBN : b * p.Tk + jb * kFaBN;
-        for (int c = 0; c < NCH; ++c) {
-          tma_load_2d(smem_addr(sK + s * KV_BYTES + c * CHUNK_BYTES), &tmK, fb, kvh * DH + c * 64, row);
-          tma_load_2d(smem_addr(sV + s * KV_BYTES + c * CHUNK_BYTES), &tmV, fb, kvh * DH + c * 64, row);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      bool ok = mbar_wait(smem_addr(q_full), 0, p.err, kErrTimeoutMma);
-      const uint32_t qa = smem_addr(sQ);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % NST;
-        if (!mbar_wait(smem_addr(&kv_full[st]), (j / NST) & 1, p.err, kErrTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t ka = smem_addr(sK + st * KV_BYTES);
-#pragma unroll
-        for (int k = 0; k < DH / 16; ++k) {
-          const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
-          umma_f16(tmem + (j & 1) * kFaBN, sw128_kmajor_desc(qa + off), sw128_kmajor_desc(ka + off), IDESC_S, k > 0);
-        }
-        umma_commit(smem_addr(&s_full[j & 1]));
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      if (ok && nkb > 1) ok = issue_s(1);
-      for (int j = 0; ok && j < nkb; ++j) {
-        const int w = j & 1;
-        if (!mbar_wait(smem_addr(&p_full[w]), (j >> 1) & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t va = smem_addr(sV + (j % NST) * KV_BYTES);
-#pragma unroll
-        for (int k = 0; k < kFaBN / 16; ++k)
-          umma_f16_tmem_a(tmem + O_COL + w * DH, tmem + w * kFaBN + k * 8,
-                          sw128_mnmajor_desc(va + k * 2048, CHUNK_BYTES, 1024), IDESC_O, (j > 1 || k > 0) ? 1u : 0u);
-        umma_commit(smem_addr(&p_empty[w]));
-        umma_commit(smem_addr(&kv_empty[j % NST]));
-        if (j + 2 < nkb && !issue_s(j + 2)) { ok = false; break; }
-      }
-      if (ok) umma_commit(smem_addr(o_full));
-    }
-  } else {
-    const int qd = warp & 3;
-    const int w = (warp - 2) >> 2;          // warpgroup: key blocks j with j & 1 == w
-    const int row = qd * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
-    const uint32_t s_col = w * kFaBN;
-    const bool dead = q0 + qd * 32 >= p.Tq;
-    float m_run = -FLT_MAX, l_run = 0.f;
-    bool ok = true;
-    const bool cls_row = p.cls != nullptr && qt == 0 && row == 0;
-    const float sl2 = p.scale_log2;
-    int qpos = 0x7FFFFFFF;
-    if (p.causal) {
-      const int qi = min(q0 + row, p.Tq - 1);
-      qpos = p.q_pos ? p.q_pos[(long)b * p.Tq + qi] : qi + p.Tk - p.Tq;
-    }
-    const int qlo = p.q_lo ? p.q_lo[(long)b * p.Tq + min(q0 + row, p.Tq - 1)] : 0;
-    const int klim = min(p.Tk - 1, qpos);
-    for (int j = w; j < nkb; j += 2) {
-      const uint32_t ph = (j >> 1) & 1;
-      const bool first = j < 2;
-      if (!mbar_wait(smem_addr(&s_full[w]), ph, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
-      tc_fence_after();
-      if (dead) {
-        tc_fence_before();
-        mbar_arrive(smem_addr(&p_full[w]));
-        continue;
-      }
-      // pass 1: row max over the block, 64 scores at a time (S is read again in pass 2)
-      const int kbase = (kb0 + j) * kFaBN;
-      const int nvalid = klim - kbase + 1;  // keys of this block at or below the row's last key
-      const bool ragged = nvalid < kFaBN || kbase < qlo;
-      float mx8[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) mx8[u] = -FLT_MAX;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(tmem + lane_base + s_col + hh * 64, r0);
-        tmem_ld32(tmem + lane_base + s_col + hh * 64 + 32, r1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int t = 0; t < 64; ++t) {
-          const int kk = hh * 64 + t;
-          float v = __uint_as_float(t < 32 ? r0[t] : r1[t - 32]);
-          if (ragged && (kk >= nvalid || kbase + kk < qlo)) v = -FLT_MAX;
-          mx8[t & 7] = fmaxf(mx8[t & 7], v);
-          if (cls_row && kk < p.Tk - kbase) p.cls[((long)b * p.H + h) * p.Tk + kbase + kk] = v * sl2;
-        }
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      const bool grow = (mx - m_run) * sl2 > kRescaleThreshold;
-      const bool any_grow = __any_sync(0xffffffffu, grow) && !first;
-      float corr = 1.f;
-      if (grow || first) {
-        const float mnew = fmaxf(m_run, mx);
-        corr = first ? 0.f : ex2_approx((m_run - mnew) * sl2);
-        m_run = mnew;
-      }
-      if (any_grow) {  // rescale O[w] once this warpgroup's previous PV (block j - 2) completed
-        if (!mbar_wait(smem_addr(&p_empty[w]), ((j >> 1) - 1) & 1, p.err, kErrTimeoutEpilogue)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < DH / 32; ++c) {
-          uint32_t r[32];
-          const uint32_t oa = tmem + lane_base + O_COL + w * DH + c * 32;
-          tmem_ld32(oa, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * corr);
-          tmem_st32(oa, r);
-        }
-        tmem_wait_st();
-      }
-      l_run *= first ? 0.f : corr;
-      const float moff = m_run * sl2;
-      // pass 2: exponentials of each 64-key half; P_half -> 32 columns at s_col + 32 * half (the
-      // S columns it overwrites were read in this or the previous half)
-      float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r0[32], r1[32], pk[32];
-        tmem_ld32(tmem + lane_base + s_col + c * 64, r0);
-        tmem_ld32(tmem + lane_base + s_col + c * 64 + 32, r1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int k0 = c * 64 + 2 * t;
-          const float s0 = __uint_as_float(t < 16 ? r0[2 * t] : r1[2 * t - 32]);
-          const float s1 = __uint_as_float(t < 16 ? r0[2 * t + 1] : r1[2 * t - 31]);
-          float e0 = ex2_approx(fmaf(s0, sl2, -moff));
-          float e1 = ex2_approx(fmaf(s1, sl2, -moff));
-          if (ragged) {
-            if (k0 >= nvalid || kbase + k0 < qlo) e0 = 0.f;
-            if (k0 + 1 >= nvalid || kbase + k0 + 1 < qlo) e1 = 0.f;
-          }
-          ls8[(2 * t) & 7] += e0;
-          ls8[(2 * t + 1) & 7] += e1;
-          pk[t] = pack_bf16x2(e0, e1);
-        }
-        tmem_st32(tmem + lane_base + s_col + c * 32, pk);
-      }
-      l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(smem_addr(&p_full[w]));
-    }
-    if (ok && !dead) ok = mbar_wait(smem_addr(o_full), 0, p.err, kErrTimeoutEpilogue);
-    float2* xs = reinterpret_cast<float2*>(sQ);  // [warpgroup][row] (max, sum); every MMA is done
-    if (ok && !dead) {  // swap (max, sum) with the other warpgroup's thread of this row
-      xs[w * kFaBM + row] = make_float2(m_run, l_run);
-      const uint32_t xb = smem_addr(&x_fin[qd]);
-      mbar_arrive(xb);
-      ok = mbar_wait(xb, 0, p.err, kErrTimeoutEpilogue);
-    }
-    if (ok && !dead) {
-      tc_fence_after();
-      const float2 other = xs[(w ^ 1) * kFaBM + row];
-      const float m0 = w == 0 ? m_run : other.x, l0 = w == 0 ? l_run : other.y;
-      const float m1 = w == 0 ? other.x : m_run, l1 = w == 0 ? other.y : l_run;
-      const bool has1 = nkb > 1;  // O[1] holds nothing when there is a single key block
-      const float m = has1 ? fmaxf(m0, m1) : m0;
-      const float f0 = ex2_approx((m0 - m) * sl2);
-      const float f1 = has1 ? ex2_approx((m1 - m) * sl2) : 0.f;
-      const float l = l0 * f0 + l1 * f1;
-      const float inv = 1.f / l;
-      const float g0 = f0 * inv, g1 = f1 * inv;
-      const int qrow = q0 + row;
-      bf16* orow = p.o + ((long)b * p.Tq + qrow) * p.ldo + (long)h * DH + w * (DH / 2);
-#pragma unroll 1
-      for (int c = 0; c < DH / 64; ++c) {
-        uint32_t r0[32], r1[32];
-        const uint32_t col = O_COL + w * (DH / 2) + c * 32;
-        tmem_ld32(tmem + lane_base + col, r0);
-        if (has1) tmem_ld32(tmem + lane_base + col + DH, r1);
-        tmem_wait_ld();
-        float v[32];
-#pragma unroll
-        for (int t = 0; t < 32; ++t)
-          v[t] = __uint_as_float(r0[t]) * g0 + (has1 ? __uint_as_float(r1[t]) * g1 : 0.f);
-        if (qrow < p.Tq) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            dst[u] = make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
-                                pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
-        }
-      }
-      if (w == 0 && p.lse != nullptr && qrow < p.Tq)
-        p.lse[((long)b * p.H + h) * p.Tq + qrow] = (m * sl2 + log2f(l)) * 0.69314718055994531f;
-      if (p.cls != nullptr && qt == 0 && qd == 0 && w == 0) {  // both warpgroups' CLS logits are written
-        __syncwarp();
-        const float mm = __shfl_sync(0xffffffffu, m, 0) * sl2;
-        const float il = 1.f / __shfl_sync(0xffffffffu, l, 0);
-        float* src = p.cls + ((long)b * p.H + h) * p.Tk;
-        for (int t = lane; t < p.Tk; t += 32) src[t] = exp2f(src[t] - mm) * il;
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
-  }
-}
-
 // ------------------------------------------------------------------------------ two-tile variant
 // One CTA = two 128-row query tiles of one (batch, head) sharing every K / V tile; 10 warps:
 //   warp 0      TMA: both Q tiles once; K and V tiles of 128 keys into a 2-stage ring
@@ -1387,19 +1060,6 @@ void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tens
     p.lse = lse->data_ptr<float>();
   }
   auto st = at::cuda::getCurrentCUDAStream();
-  if (variant == 3) {  // one query tile per CTA, two warpgroups on alternate key blocks
-    dim3 grid((Tq + kFaBM - 1) / kFaBM, H, B);
-    const int smem = static_cast<int>(Dh / 64) * 16384 * 7 + 1024 + 256;  // Q + 3 K/V stages
-    if (Dh == 128) {
-      FA_CHECK_ATTR(cudaFuncSetAttribute(fa_fwd_pp_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      fa_fwd_pp_kernel<128><<<grid, kFaPThreads, smem, st>>>(tq, tk, tv, p);
-    } else {
-      FA_CHECK_ATTR(cudaFuncSetAttribute(fa_fwd_pp_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      fa_fwd_pp_kernel<64><<<grid, kFaPThreads, smem, st>>>(tq, tk, tv, p);
-    }
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-    return;
-  }
   if (variant == 2) {  // one query tile per CTA, two softmax threads per row
     dim3 grid((Tq + kFaBM - 1) / kFaBM, H, B);
     const int smem = static_cast<int>(Dh / 64) * 16384 * 7 + 1024 + 256;  // Q + 3 K/V stages

@@ -80,6 +80,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Same test, but the thread may be suspended (up to `hint_ns`) until the phase completes instead
+// of returning at once: a waiting warp then issues almost nothing while it waits.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete. Returns false (after recording
 // `code` in *err) if the budget runs out or another role of the same kernel already failed.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code,
@@ -88,8 +102,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   const uint64_t t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 32; ++i)  // at most 32 x 0.26 ms between the checks below
+      if (mbar_try_wait_hint(bar, parity, 0x40000u)) return true;
     if (error_raised(err)) return false;
     if (global_timer_ns() - t0 > budget_ns) {
       record_error(err, code);

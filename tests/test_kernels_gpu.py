@@ -168,7 +168,7 @@ def test_qkv_rope_scatter(Dh, H):
     _close(k2, k, rtol=1e-2, atol=1e-2)
 
 
-@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_pp", "tcgen05_2q", "mma"])
+@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_2q", "mma"])
 @pytest.mark.parametrize("Dh,H,Tq,Tk", [(128, 4, 1029, 1029), (64, 6, 197, 197), (128, 2, 312, 1029), (64, 3, 5, 70),
                                         (128, 2, 130, 260)])
 def test_attention(Dh, H, Tq, Tk, impl):
@@ -328,7 +328,7 @@ def test_gemm_2cta_epilogues():
         _close(x, y, rtol=1e-2, atol=1e-2)
 
 
-@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_pp"])
+@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split"])
 def test_attention_fused_cls_score(impl):
     """The tcgen05 attention's CLS softmax row equals the standalone CLS score kernel."""
     K_ = _k()

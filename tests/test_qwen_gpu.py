@@ -109,7 +109,7 @@ def test_full_correction_equals_forward_on_new_image():
     assert _rel(xc, xr) < 3e-2
 
 
-@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_pp"])
+@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split"])
 def test_attention_gqa_causal_paged(impl):
     """Kernel-level: grouped-query causal attention over a paged pool, packed query subset."""
     from appcorr_b200.ops import kernels as K

@@ -50,7 +50,7 @@ def test_windowed_tower_approx_and_full_correction():
     assert _rel(got, ref) < 3e-2
 
 
-@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split", "tcgen05_pp"])
+@pytest.mark.parametrize("impl", ["tcgen05", "tcgen05_split"])
 def test_attention_per_query_key_ranges(impl):
     from appcorr_b200.ops import kernels as K
 
