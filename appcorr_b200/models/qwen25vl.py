@@ -164,13 +164,40 @@ class VisionBlock(nn.Module):
         self.proj = nn.Linear(cfg.vis_heads * cfg.vis_head_dim, d)
         self.mlp = SwiGLU(d, cfg.vis_ffn, bias=True)
 
+    def _qkv(self, x, sin, cos):
+        c = self.cfg
+        n = x.shape[0]
+        q, k, v = self.qkv(self.norm1(x)).view(n, 3, c.vis_heads, c.vis_head_dim).unbind(1)
+        return q * cos[:, None] + rotate_half(q) * sin[:, None], k * cos[:, None] + rotate_half(k) * sin[:, None], v
+
+    def approx(self, x, sin, cos, windows: int, cache: Dict, tag: str):
+        """forward(), keeping this block's (rotated) keys and values for later corrections."""
+        _, k, v = self._qkv(x, sin, cos)
+        cache[f"{tag}_k"], cache[f"{tag}_v"] = k, v
+        return self.forward(x, sin, cos, windows)
+
+    def correct(self, xs, rows: torch.Tensor, sin, cos, windows: int, cache: Dict, tag: str):
+        """Corrected tokens only: xs [n, d] are the rows `rows` (tower order) on their new
+        trajectory; their keys / values replace the cached ones, the other tokens' stay as cached,
+        and each corrected token attends within its window (or to every token when windows == 1)."""
+        c = self.cfg
+        T = cache[f"{tag}_k"].shape[0]
+        q, k, v = self._qkv(xs, sin[rows], cos[rows])
+        cache[f"{tag}_k"] = cache[f"{tag}_k"].index_copy(0, rows, k)
+        cache[f"{tag}_v"] = cache[f"{tag}_v"].index_copy(0, rows, v)
+        kk, vv = cache[f"{tag}_k"].transpose(0, 1), cache[f"{tag}_v"].transpose(0, 1)  # [heads, T, dh]
+        w = T // windows
+        keys = torch.arange(T, device=xs.device)
+        mask = (keys[None] // w) == (rows[:, None] // w)                   # [n, T]
+        o = F.scaled_dot_product_attention(q.transpose(0, 1), kk, vv, attn_mask=mask[None])
+        xs = xs + self.proj(o.transpose(0, 1).reshape(xs.shape[0], -1))
+        return xs + self.mlp(self.norm2(xs))
+
     def forward(self, x, sin, cos, windows: int):
         """x: [T, d] in window-major order; windows: number of equal attention windows (1 = full)."""
         c = self.cfg
         T = x.shape[0]
-        q, k, v = self.qkv(self.norm1(x)).view(T, 3, c.vis_heads, c.vis_head_dim).unbind(1)
-        q = q * cos[:, None] + rotate_half(q) * sin[:, None]
-        k = k * cos[:, None] + rotate_half(k) * sin[:, None]
+        q, k, v = self._qkv(x, sin, cos)
         w = T // windows
         q, k, v = (t.view(windows, w, c.vis_heads, c.vis_head_dim).transpose(1, 2) for t in (q, k, v))
         o = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(T, -1)
@@ -198,9 +225,8 @@ class VisionTower(nn.Module):
         self.blocks = nn.ModuleList([VisionBlock(cfg) for _ in range(cfg.vis_depth)])
         self.merger = Merger(cfg)
 
-    def forward(self, img_u8: torch.Tensor) -> torch.Tensor:
-        """uint8 [H, W, 3] -> merged image embeddings [(H/28)*(W/28), hidden] in raster order of
-        merge units (window-major inside the tower, restored to raster order on output)."""
+    def _tokens(self, img_u8: torch.Tensor):
+        """-> patch rows in tower order, rotary tables, window count."""
         c = self.cfg
         H, W = img_u8.shape[:2]
         gh, gw = H // c.patch, W // c.patch
@@ -208,12 +234,33 @@ class VisionTower(nn.Module):
         cols = x.view(gh, c.patch, gw, c.patch, 3).permute(0, 2, 4, 1, 3).reshape(gh * gw, -1)
         order = window_order(gh, gw, c.window, c.merge).to(img_u8.device)
         sin, cos = (t.to(img_u8.device) for t in vision_rope(c, gh, gw, order.cpu()))
-        h = self.patch_embed(cols[order])
-        nwin = (gh // c.window) * (gw // c.window)
+        return cols[order], sin, cos, (gh // c.window) * (gw // c.window), (gh, gw)
+
+    def forward(self, img_u8: torch.Tensor, cache: Optional[Dict] = None) -> torch.Tensor:
+        """uint8 [H, W, 3] -> merged image embeddings [(H/28)*(W/28), hidden] in raster order of
+        merge units (window-major inside the tower, restored to raster order on output). With a
+        `cache`, every block keeps its keys / values for `correct`."""
+        c = self.cfg
+        cols, sin, cos, nwin, (gh, gw) = self._tokens(img_u8)
+        h = self.patch_embed(cols)
         for i, blk in enumerate(self.blocks):
-            h = blk(h, sin, cos, 1 if i in c.full_attn_layers else nwin)
+            win = 1 if i in c.full_attn_layers else nwin
+            h = blk(h, sin, cos, win) if cache is None else blk.approx(h, sin, cos, win, cache, f"v{i}")
         emb = self.merger(h)
         return emb[merge_raster_index(c, gh, gw).to(emb.device)]
+
+    def correct(self, img_u8: torch.Tensor, units: torch.Tensor, cache: Dict) -> torch.Tensor:
+        """Partial tower correction: only the merge units `units` (tower order) are recomputed
+        from the new image, through every block, against the cached keys / values of the other
+        tokens; -> their merged embeddings [len(units), hidden] (in the order of `units`)."""
+        c = self.cfg
+        g = c.merge ** 2
+        cols, sin, cos, nwin, _ = self._tokens(img_u8)
+        rows = (units[:, None] * g + torch.arange(g, device=units.device)[None]).reshape(-1)
+        h = self.patch_embed(cols[rows])
+        for i, blk in enumerate(self.blocks):
+            h = blk.correct(h, rows, sin, cos, 1 if i in c.full_attn_layers else nwin, cache, f"v{i}")
+        return self.merger(h)
 
 
 def merge_unit_raster(cfg: Qwen25VLConfig, gh: int, gw: int) -> torch.Tensor:

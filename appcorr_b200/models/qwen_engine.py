@@ -13,8 +13,14 @@ Kernel path (no PyTorch compute op on the per-layer path):
              [K/V rewritten in place in the cache] -> attention of the packed queries with each
              query's own causal frontier -> o GEMM [x_act + attn] -> RMSNorm -> SwiGLU -> down GEMM
              [scattered into x]
-The vision tower is recomputed in full on the current canvas each round; the LLM corrects the
-prompt text plus the image tokens whose embeddings moved most (top-k of ||e_new - e_old||^2).
+    vision correct  (after an approximate tower pass that kept every block's K / V)
+             patch drift ||cols_new - cols_old||^2 per patch -> summed per 2x2 merge unit -> top-k
+             units -> their 4 patches only: patch GEMM -> per block RMSNorm -> qkv GEMM [K / V of
+             the corrected tokens rewritten in the block's cache] -> attention of the packed
+             corrected queries over the cache, each within its own window (per-query key ranges)
+             or over all tokens -> proj / SwiGLU / down GEMMs -> merger on the corrected units,
+             scattered into their LLM input rows
+The LLM then corrects the prompt text plus exactly the image rows of the corrected units.
 
 Head dims that are not 64 / 128 (the tower's 80) run zero-padded to the next supported size:
 rotate-half pairs (d, d + Dh/2) are kept by placing the two halves at [0, Dh/2) and
@@ -185,7 +191,12 @@ class QwenVLEngine:
         dv = c.vis_hidden
         hp = c.vis_heads * self.vdp
         t["vx"], t["vxn"] = e(T, dv), e(T, dv)
-        t["vq"], t["vk"], t["vv"], t["vo"] = e(T, hp), e(T, hp), e(T, hp), e(T, hp)
+        t["vq"], t["vo"] = e(T, hp), e(T, hp)
+        # every block's keys / values of the approximate pass (the corrected tokens overwrite theirs)
+        t["vkc"], t["vvc"] = e(c.vis_depth, T, hp), e(c.vis_depth, T, hp)
+        t["cols_new"] = torch.zeros(T, self.kpatch, device=dev, dtype=BF16)
+        t["vdrift"] = torch.zeros(T, device=dev, dtype=torch.float32)
+        t["vrows"] = torch.zeros(T, device=dev, dtype=torch.int32)
         t["vh"] = e(T, self.vffn)
         t["m1"] = e(n_img, dv * c.merge ** 2)
         # merged unit u (tower order) -> its LLM input row
@@ -257,11 +268,11 @@ class QwenVLEngine:
         eps = 1e-6
         for i, w in enumerate(self.vis):
             K.rmsnorm(x, w.norm1, eps, xn)
-            K.qkv_gemm(xn, w.qkv_w, w.qkv_b, t["vq"], t["vk"], t["vv"], head_dim=dp, seq_len=T,
+            K.qkv_gemm(xn, w.qkv_w, w.qkv_b, t["vq"], t["vkc"][i], t["vvc"][i], head_dim=dp, seq_len=T,
                        rope=(t["vsin"], t["vcos"]), n_prefix=0)
             B = 1 if i in c.full_attn_layers else nwin
-            K.attention(t["vq"], t["vk"], t["vv"], t["vo"], B=B, Tq=T // B, Tk=T // B, H=c.vis_heads, Dh=dp,
-                        scale=c.vis_head_dim ** -0.5)
+            K.attention(t["vq"], t["vkc"][i], t["vvc"][i], t["vo"], B=B, Tq=T // B, Tk=T // B, H=c.vis_heads,
+                        Dh=dp, scale=c.vis_head_dim ** -0.5)
             K.gemm(t["vo"], w.proj_w, x, epi=K.EPI_RESID, bias=w.proj_b, gamma=self.vis_ones, resid=x)
             K.rmsnorm(x, w.norm2, eps, xn)
             K.gemm(xn, w.w12, t["vh"], epi=K.EPI_SWIGLU, bias=w.b12)
@@ -269,6 +280,53 @@ class QwenVLEngine:
         K.rmsnorm(x, self.merge_norm, eps, xn)
         K.gemm(xn.view(sess.n_img, -1), self.merge_w1, t["m1"], epi=K.EPI_GELU, bias=self.merge_b1)
         K.gemm(t["m1"], self.merge_w2, t["x_in"], bias=self.merge_b2, out_rows=t["img_rows"])
+
+    def vision_correct(self, sess: QwenSession, img: torch.Tensor, keep_ratio: float) -> torch.Tensor:
+        """Partial tower correction on the new canvas (after `vision` ran on the approximate one):
+        the keep_ratio share of merge units whose pixels moved most is recomputed through every
+        block against the cached keys / values of the rest; their merged embeddings replace
+        their LLM input rows. -> the corrected units (int32, tower order, ascending)."""
+        c, t = self.cfg, sess.tensors
+        T, dp, g = sess.T, self.vdp, c.merge ** 2
+        K.patch_im2col(img, c.patch, t["cols_new"], mean=CLIP_MEAN, std=CLIP_STD, perm=t["order"])
+        K.row_sqdist(t["cols_new"], t["cols"], t["vdrift"])
+        k = min(max(int(sess.n_img * keep_ratio), 1), sess.n_img)
+        units = torch.topk(t["vdrift"].view(sess.n_img, g).sum(1), k, sorted=False).indices.sort().values
+        units = units.to(torch.int32)
+        n = k * g
+        rows = t["vrows"][:n]
+        torch.add(units[:, None] * g, torch.arange(g, device=self.device, dtype=torch.int32)[None],
+                  out=rows.view(k, g))
+        cols = torch.empty(n, self.kpatch, device=self.device, dtype=BF16)
+        K.gather_rows(t["cols_new"], rows, cols)
+        K.scatter_rows(cols, rows, t["cols"])        # these patches are now current in the tower
+        x, xn = t["vx"][:n], t["vxn"][:n]
+        q, o, h = t["vq"][:n], t["vo"][:n], t["vh"][:n]
+        K.gemm(cols, self.patch_w, x)
+        w_tok = c.window ** 2                         # tokens per attention window (tower order)
+        lo_w = (rows // w_tok) * w_tok
+        hi_w = lo_w + (w_tok - 1)
+        lo_f = torch.zeros_like(rows)
+        hi_f = torch.full_like(rows, T - 1)
+        eps = 1e-6
+        for i, w in enumerate(self.vis):
+            K.rmsnorm(x, w.norm1, eps, xn)
+            K.qkv_gemm(xn, w.qkv_w, w.qkv_b, q, t["vkc"][i], t["vvc"][i], head_dim=dp, tok_idx=rows,
+                       kv_rows=rows, rope=(t["vsin"], t["vcos"]), n_prefix=0)
+            full = i in c.full_attn_layers
+            K.attention(q, t["vkc"][i], t["vvc"][i], o, B=1, Tq=n, Tk=T, H=c.vis_heads, Dh=dp,
+                        scale=c.vis_head_dim ** -0.5, causal=True, q_pos=hi_f if full else hi_w,
+                        q_lo=lo_f if full else lo_w)
+            K.gemm(o, w.proj_w, x, epi=K.EPI_RESID, bias=w.proj_b, gamma=self.vis_ones, resid=x)
+            K.rmsnorm(x, w.norm2, eps, xn)
+            K.gemm(xn, w.w12, h, epi=K.EPI_SWIGLU, bias=w.b12)
+            K.gemm(h, w.w3, x, epi=K.EPI_RESID, bias=w.b3, gamma=self.vis_ones, resid=x)
+        K.rmsnorm(x, self.merge_norm, eps, xn)
+        m1 = t["m1"][:k]
+        K.gemm(xn.view(k, -1), self.merge_w1, m1, epi=K.EPI_GELU, bias=self.merge_b1)
+        out_rows = t["img_rows"].index_select(0, units)
+        K.gemm(m1, self.merge_w2, t["x_in"], bias=self.merge_b2, out_rows=out_rows)
+        return units
 
     def embed_text(self, sess: QwenSession, ids: torch.Tensor) -> None:
         """int32 token ids of the text rows ([n_before + n_after], prompt order) -> x_in rows."""
@@ -307,12 +365,20 @@ class QwenVLEngine:
         sess.approx_done = True
         return x
 
-    def plan(self, sess: QwenSession, keep_ratio: float) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Text rows plus the top-k image rows by embedding change (ascending positions)."""
+    def plan(self, sess: QwenSession, keep_ratio: float,
+             units: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Text rows plus image rows (ascending positions): the rows of the corrected merge units
+        `units` (tower order) when given, else the top-k image rows by embedding change."""
         t = sess.tensors
         img = slice(sess.n_before, sess.n_before + sess.n_img)
-        K.row_sqdist(t["x_in"][img], t["emb_prev"], t["score"].view(-1)[img])
-        k = min(max(int(sess.n_img * keep_ratio), 0), sess.n_img)
+        if units is not None:
+            sc = t["score"].view(-1)
+            sc.zero_()
+            sc.index_fill_(0, t["img_rows"].index_select(0, units).long(), 1.0)
+            k = units.numel()
+        else:
+            K.row_sqdist(t["x_in"][img], t["emb_prev"], t["score"].view(-1)[img])
+            k = min(max(int(sess.n_img * keep_ratio), 0), sess.n_img)
         npre = t["pre"].shape[1]
         T = npre + k
         upd = t["upd"].view(-1)[:T].view(1, T)
@@ -320,10 +386,10 @@ class QwenVLEngine:
         K.correction_plan(t["score"], t["pre"], t["cand"], k, upd, rows, stats=t["plan_stats"])
         return upd, rows
 
-    def correct(self, sess: QwenSession, keep_ratio: float) -> torch.Tensor:
+    def correct(self, sess: QwenSession, keep_ratio: float, units: Optional[torch.Tensor] = None) -> torch.Tensor:
         c, t = self.cfg, sess.tensors
         N = sess.N
-        upd, rows = self.plan(sess, keep_ratio)
+        upd, rows = self.plan(sess, keep_ratio, units)
         T = upd.shape[1]
         kv_sel = t["phys"].index_select(0, rows)
         x = t["x"]

@@ -124,10 +124,10 @@ class QwenVLEngineTP(QwenVLEngine):
         sess.approx_done = True
         return x
 
-    def correct(self, sess: QwenSession, keep_ratio: float) -> torch.Tensor:
+    def correct(self, sess: QwenSession, keep_ratio: float, units=None) -> torch.Tensor:
         c, t, comm = self.cfg, sess.tensors, self.comm
         N, D, R = sess.N, c.hidden, t["R"]
-        upd, rows = self.plan(sess, keep_ratio)
+        upd, rows = self.plan(sess, keep_ratio, units)
         T = upd.shape[1]
         kv_sel = t["phys"].index_select(0, rows)
         x = t["x"]

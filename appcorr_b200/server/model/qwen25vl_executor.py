@@ -5,9 +5,15 @@ Reference: offload/server/model/qwen25vl_executor.py:33-339 (preprocess :63-93, 
 :128-138, approx_forward :148-172, correct_forward :174-250, head_inference :252-286). Differences
 by design: the model is random-init with the configured shape (no checkpoints offline), the
 prompt is `n_text` synthetic token ids around the image, the canvas is centre-cropped to a
-multiple of 112 px (the reference processor resizes), the vision tower is recomputed in full
-each round, and only the first token is produced (the reference falls back to HF generate for
-the rest).
+multiple of 112 px (the reference processor resizes), and only the first token is produced (the
+reference falls back to HF generate for the rest).
+
+Rounds: the approximate round runs the whole vision tower on the approximate canvas (keeping
+every block's K / V) and the LLM prefill. A correction round recomputes only the merge units
+whose pixels changed most (token_keep_ratio of them, ranked by patch drift) through the tower
+against the cached K / V of the others, then corrects the prompt text plus exactly those units'
+image rows in the LLM (the reference corrects the merge units of the transmission group that
+arrived, :174-250).
 """
 from __future__ import annotations
 
@@ -81,18 +87,21 @@ class Qwen25VLExecutor(ModelExecutor):
             sess = self.engine.new_session(H, W, self.n_before, self.n_after)
             self._sessions = {key: sess}
             self.engine.embed_text(sess, self.text_ids)
-        self.engine.vision(sess, img)
         context["session"] = sess
         return {}
 
     def approx_forward(self, params, context, config):
-        self.engine.approx(context["session"])
+        sess = context["session"]
+        self.engine.vision(sess, context["image"])
+        self.engine.approx(sess)
         return {"precision": "fp8" if self.engine.fp8 else "bf16"}
 
     def correct_forward(self, params, context, config):
         opts = normalize_appcorr_kwargs(config.appcorr_kwargs, config.transmission_kwargs)
         keep = float(opts.get("token_keep_ratio", 0.25))
-        self.engine.correct(context["session"], keep)
+        sess = context["session"]
+        units = self.engine.vision_correct(sess, context["image"], keep)
+        self.engine.correct(sess, keep, units=units)
         return {}
 
     def head_inference(self, task, context, config) -> Dict[str, Any]:
@@ -101,6 +110,7 @@ class Qwen25VLExecutor(ModelExecutor):
 
     def full_inference(self, task, context, config):
         sess = context["session"]
+        self.engine.vision(sess, context["image"])
         self.engine.approx(sess)
         self.head_inference(task, context, config)
 

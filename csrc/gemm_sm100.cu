@@ -392,7 +392,8 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* sfull = tempty + 2;  // F4: scales of stage s are in TMEM (4 scale warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sfull + (F4 ? STAGES : 0));
+  uint64_t* sf_full = sfull + (F4 ? STAGES : 0);  // F4: scale bytes of stage s landed in shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_full + (F4 ? STAGES : 0));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -401,7 +402,10 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_addr(&full[s]), 1);
       mbar_init(smem_addr(&empty[s]), 1);
-      if constexpr (F4) mbar_init(smem_addr(&sfull[s]), 4);
+      if constexpr (F4) {
+        mbar_init(smem_addr(&sfull[s]), 4);
+        mbar_init(smem_addr(&sf_full[s]), 1);
+      }
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_addr(&tfull[a]), 1);
@@ -435,18 +439,21 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) goto producer_done;
           const uint32_t fb = smem_addr(&full[s]);
-          mbar_arrive_expect_tx(fb, STAGE_BYTES);
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
-          tma_load_2d(sa, &tmA, fb, kb * BKX, mb * kBM);
-          tma_load_2d(sa + A_BYTES, &tmB, fb, kb * BKX, nb * BN);
-          if constexpr (F4) {
+          if constexpr (F4) {  // scales first, on their own barrier: the scale warps move them to
+                               // TMEM while A / B are still in flight
+            const uint32_t sfb = smem_addr(&sf_full[s]);
+            mbar_arrive_expect_tx(sfb, SFA_BYTES + SFB_BYTES);
             const uint32_t sf = sa + A_BYTES + B_BYTES;
-            bulk_g2s(sf, ep.sfa + ((long)mb * ep.sf_kt + kb * 4) * 512, SFA_BYTES, fb);
+            bulk_g2s(sf, ep.sfa + ((long)mb * ep.sf_kt + kb * 4) * 512, SFA_BYTES, sfb);
 #pragma unroll
             for (int j = 0; j < BN / 128; ++j)
               bulk_g2s(sf + SFA_BYTES + j * 2048, ep.sfb + ((long)(nb * (BN / 128) + j) * ep.sf_kt + kb * 4) * 512,
-                       2048, fb);
+                       2048, sfb);
           }
+          mbar_arrive_expect_tx(fb, A_BYTES + B_BYTES);
+          tma_load_2d(sa, &tmA, fb, kb * BKX, mb * kBM);
+          tma_load_2d(sa + A_BYTES, &tmB, fb, kb * BKX, nb * BN);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
       }
@@ -514,7 +521,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutEpilogue)) { ok = false; break; }
+          if (!mbar_wait(smem_addr(&sf_full[s]), ph, shp.err, kErrTimeoutEpilogue)) { ok = false; break; }
           const uint8_t* sfs = smem + s * STAGE_BYTES + A_BYTES + B_BYTES;
           uint32_t r[32], r2[16];
 #pragma unroll

@@ -99,3 +99,44 @@ def test_lowres_sr_engine_upscales_to_target():
     assert sr.upscale(base).shape == (2, 64, 96, 3)
     out = sr.upscale(base, (32, 48))
     assert out.shape == (2, 32, 48, 3) and out.dtype == torch.uint8
+
+
+def test_depther_eval_grid_and_flip_tta():
+    """NYU profile: images go onto the fixed eval grid, mirrored sources are flipped back and
+    averaged (so the result is mirror-symmetric for a mirror-symmetric input), and the depth map
+    comes back at the image's own size."""
+    from appcorr_b200.common.protocol import ExperimentConfig, Task
+    from appcorr_b200.server.model import PyramidBatch, get_model_executor
+
+    cfg = ExperimentConfig(exp_id="t", model_name="dinov3_depther", batch_size=2, image_shape=(96, 160, 3),
+                           input_profile_name="dinov3_nyu_synthmix_dpt",
+                           input_profile_kwargs={"backbone_arch": "vits16", "depther_eval_size": 128,
+                                                 "dpt_features": 64},
+                           transmission_kwargs={"pyramid_levels": [1, 0], "num_groups": 1},
+                           appcorr_kwargs={"token_keep_ratio": 1.0})
+    ex = get_model_executor(cfg.model_name, DEV)
+    ex.load_model(cfg.model_name, cfg)
+    import numpy as np
+
+    from appcorr_b200.policies.transmission.pyramid import pyr_up
+
+    base = torch.randint(0, 256, (2, 48, 80, 3), dtype=torch.uint8)
+    half = torch.randint(0, 256, (2, 96, 80, 3), dtype=torch.int16)
+    target = torch.cat([half, torch.flip(half, dims=[2])], 2)             # mirror-symmetric 96 x 160
+    up = torch.from_numpy(np.stack([pyr_up(b) for b in base.numpy()]).astype(np.int16))
+    res = target - up                                                      # full canvas = target
+    task = Task(task_id=0, request_id=0, payload=[], instructions=[])
+    ctx = {}
+    L = ex.cfg.depth
+    ex.preprocess(PyramidBatch(base, None), task, ctx, cfg)
+    assert ctx["canvas"].shape == (4, 128, 128, 3)  # 2 images + 2 mirrors on the 128 grid
+    ex.prepare_tokens(task, ctx, cfg)
+    ex.approx_forward({"layers": (0, L)}, ctx, cfg)
+    ex.preprocess(PyramidBatch(base, res), task, ctx, cfg)
+    ex.prepare_tokens(task, ctx, cfg)
+    ex.correct_forward({"layers": (0, L), "group_id": 1}, ctx, cfg)
+    ex.head_inference(task, ctx, cfg)
+    out = ex.get_final_results(task, ctx, cfg)
+    d = torch.from_numpy(out[0]["depth"])
+    assert d.shape == (96, 160) and bool(torch.isfinite(d).all())
+    assert torch.allclose(d, torch.flip(d, dims=[1]), rtol=1e-4, atol=1e-4)

@@ -168,3 +168,52 @@ def test_llm_fp8_tracks_fp32():
     assert _rel(x, xr) < 8e-2
     xc = eng.correct(sess, 1.0)
     assert _rel(xc, xr) < 8e-2
+
+
+def test_partial_vision_correction_matches_oracle():
+    """Only the merge units whose pixels moved most are recomputed through the tower (against the
+    approximate pass's cached K / V); their LLM input rows change, the others do not; the LLM
+    correction then covers the text plus exactly those rows. Both against the fp32 model."""
+    from appcorr_b200.models.qwen25vl import merge_unit_raster, mrope_positions, mrope_tables
+
+    cfg, m, eng, ids, nb, na = _setup(4)
+    img0 = torch.randint(0, 256, (1, 224, 224, 3), dtype=torch.uint8, device=DEV)
+    img1 = img0.clone()
+    img1[:, 56:112, 112:224] = torch.randint(0, 256, (1, 56, 112, 3), dtype=torch.uint8, device=DEV)
+    sess = eng.new_session(224, 224, nb, na)
+    t = sess.tensors
+    eng.vision(sess, img0)
+    eng.embed_text(sess, ids)
+    eng.approx(sess)
+    x_in0 = t["x_in"].clone()
+    units = eng.vision_correct(sess, img1, 0.125)                      # 8 of 64 units
+    raster = merge_unit_raster(cfg, 16, 16).to(DEV)
+    changed = set((nb + raster[units.long()]).tolist())
+    # the changed pixels cover raster units rows 2..3 x cols 4..7 = 8 units: exactly those are picked
+    expect = {nb + r * 8 + c for r in (2, 3) for c in range(4, 8)}
+    assert changed == expect
+    cache = {}
+    with torch.no_grad():
+        m.visual(img0[0], cache)
+        emb = m.visual.correct(img1[0], units.long(), cache)
+    got = t["x_in"][(nb + raster[units.long()]).long()]
+    assert _rel(got, emb) < 2e-2
+    keep_rows = [i for i in range(sess.N) if i not in changed]
+    assert torch.equal(t["x_in"][keep_rows], x_in0[keep_rows])
+    xc = eng.correct(sess, 0.125, units=units).clone()
+    rows = t["rows"][: nb + na + units.numel()].long()
+    assert set(rows.tolist()) == set(range(nb)) | set(range(nb + 64, nb + 64 + na)) | changed
+    pos = mrope_positions(nb, 8, 8, na)
+    sin, cos = (v.to(DEV) for v in mrope_tables(cfg, pos))
+    lcache = {}
+    with torch.no_grad():
+        xr = _oracle_x_in(m, img0, ids, nb)
+        for i, ly in enumerate(m.layers):
+            xr = ly.approx(xr, sin, cos, lcache, f"l{i}")
+        x_in1 = _oracle_x_in(m, img0, ids, nb)
+        x_in1[(nb + raster[units.long()]).long()] = emb
+        xr2 = x_in1
+        for i, ly in enumerate(m.layers):
+            xr2 = ly.correct(xr2, rows, sin, cos, lcache, f"l{i}")
+    torch.cuda.synchronize()
+    assert _rel(xc, xr2) < 3e-2
