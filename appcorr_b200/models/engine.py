@@ -245,16 +245,18 @@ def quantize_layer_e4m3(lw: LayerW) -> None:
 
 
 def quantize_layer_nvfp4(lw: LayerW, swiglu: bool) -> None:
-    """Attach NVFP4 copies of qkv / fc1 / fc2. A packed SwiGLU fc1 is re-packed in 64-row blocks:
-    the NVFP4 SwiGLU GEMM runs 128-wide tiles (two accumulators, so its epilogue overlaps the next
-    tile; measured 20.4 ms per ViT-7B step against 24.0 ms for 256-wide tiles with one)."""
+    """Attach NVFP4 copies of qkv / fc1 / fc2. A packed SwiGLU fc1 keeps blocks of half the NVFP4
+    tile width of fc1 (ops.kernels.fp4_tile): 128 rows for the default 256-wide tiles, whose
+    accumulator the early-release epilogue frees before its stores (ViT-7B step 87.1 ms against
+    87.9 ms with 128-wide tiles); fc2 keeps 128-wide tiles (its residual epilogue measured slower
+    at 256)."""
     q4: Dict[str, object] = {"fc1_b": lw.fc1_b}
     for n in _Q4_NAMES:
         w = getattr(lw, n + "_w")
         if w.shape[1] % 256:
             raise ValueError(f"nvfp4 precision needs GEMM K % 256 == 0 ({n}: K = {w.shape[1]})")
-        if n == "fc1" and swiglu:
-            w, q4["fc1_b"] = repack_swiglu(w, lw.fc1_b, SWIGLU_BLOCK, 64)
+        if n == "fc1" and swiglu and K.fp4_tile("fc1") != 2 * SWIGLU_BLOCK:
+            w, q4["fc1_b"] = repack_swiglu(w, lw.fc1_b, SWIGLU_BLOCK, K.fp4_tile("fc1") // 2)
         q4[n] = K.quantize_weight_nvfp4(w)
     lw.q4 = q4
 
@@ -456,7 +458,8 @@ class ViTEngine:
     def _mlp(self, lw: LayerW, xin: torch.Tensor, hbuf: torch.Tensor, a_scale=None) -> torch.Tensor:
         w, ws = self._w(lw, "fc1")
         epi = K.EPI_SWIGLU if self.cfg.is_swiglu else K.EPI_GELU
-        K.gemm(xin, w, hbuf, epi=epi, bias=self._fc1_bias(lw), a_scale=a_scale, b_scale=ws)
+        K.gemm(xin, w, hbuf, epi=epi, bias=self._fc1_bias(lw), a_scale=a_scale, b_scale=ws,
+               bn=K.fp4_tile("fc1") if self._fp4 else None)
         return hbuf
 
     def approx_layer(self, sess: Session, l: int, x: torch.Tensor, x_out: torch.Tensor, server_pscore: str) -> None:
@@ -483,7 +486,7 @@ class ViTEngine:
         a, sa = self._act(sess, sess.h)
         w, ws = self._w(lw, "fc2")
         K.gemm(a, w, x_out, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_out,
-               aux=sess.bos[l], aux_mode=K.AUX_ADD, a_scale=sa, b_scale=ws)
+               aux=sess.bos[l], aux_mode=K.AUX_ADD, a_scale=sa, b_scale=ws, bn=K.fp4_tile("fc2") if self._fp4 else None)
 
     def _attention_with_score(self, sess: Session, l: int, H: int, kind: str, score_out: torch.Tensor) -> None:
         """Full attention of layer l over H (local) heads, plus the server patch score `kind`
@@ -630,7 +633,8 @@ class ViTEngine:
         a, sa = self._act(sess, h)
         w, ws = self._w(lw, "fc2")
         K.gemm(a, w, x, epi=K.EPI_RESID, bias=lw.fc2_b, gamma=lw.ls2, resid=x_att, out_rows=rows,
-               aux=sess.bos[l], aux_mode=K.AUX_OUT_MINUS, resid2=x_act, a_scale=sa, b_scale=ws)
+               aux=sess.bos[l], aux_mode=K.AUX_OUT_MINUS, resid2=x_act, a_scale=sa, b_scale=ws,
+               bn=K.fp4_tile("fc2") if self._fp4 else None)
 
     def correct(self, sess: Session, start: int, end: int, pre: torch.Tensor, cand: torch.Tensor, opts: Dict,
                 mobile: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None,

@@ -55,6 +55,9 @@ def main(argv=None) -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--once", action="store_true")
     ap.add_argument("--ref", action="store_true")
+    ap.add_argument("--prof", action="store_true",
+                    help="gemm: one extra launch with the kernel's wait-cycle counters on; prints each wait "
+                         "as a share of the MMA warp's loop time")
     a = ap.parse_args(argv)
     torch.manual_seed(0)
     dev = "cuda"
@@ -162,6 +165,27 @@ def main(argv=None) -> None:
         check_errors(torch.device(dev))
         print(json.dumps({**res, "launched": 1}))
         return
+    if a.prof and a.op == "gemm":
+        from .native import lib
+
+        fn()
+        cnt = torch.zeros(16, dtype=torch.int64, device=dev)
+        lib().gemm_set_profile(cnt)
+        fn()
+        torch.cuda.synchronize()
+        lib().gemm_set_profile(None)
+        c = cnt.tolist()
+        loop = max(c[4], 1)
+        res["prof"] = {"ctas": c[7], "mma_loop_cycles_per_cta": c[4] // max(c[7], 1),
+                       "share_of_mma_loop": {"mma_wait_acc_free": round(c[1] / loop, 3),
+                                             "mma_wait_stage_full": round(c[2] / loop, 3),
+                                             "mma_wait_scales": round(c[3] / loop, 3),
+                                             "producer_wait_stage_free": round(c[0] / loop, 3),
+                                             "epilogue_wait_acc_full": round(c[5] / loop, 3),
+                                             "epilogue_body": round(c[6] / loop, 3),
+                                             "epilogue_release": round(c[10] / loop, 3),
+                                             "scale_warp_wait_bytes": round(c[8] / loop, 3),
+                                             "scale_warp_store": round(c[9] / loop, 3)}}
     ms = _time(fn, a.iters)
     res["ms"] = round(ms, 4)
     if flops:

@@ -21,6 +21,14 @@ LAUNCHES = [0]
 # 18.7 ms per ViT-7B step against 20.2 ms at 128), 128 = always 128 (two accumulators). The other
 # NVFP4 GEMMs run 128-wide tiles (SwiGLU 20.4 vs 24.0 ms, residual fc2 12.6 vs 13.3 ms).
 FP4_BN = [int(os.environ.get("APPCORR_FP4_BN", "0"))]
+# NVFP4 GEMMs that run 128 x 256 tiles (one accumulator, early-release epilogue); the others run
+# 128 x 128 tiles with two accumulators. A SwiGLU weight is packed in BN / 2-row blocks to match.
+FP4_WIDE = set(filter(None, os.environ.get("APPCORR_FP4_WIDE", "qkv,fc1").split(",")))
+
+
+def fp4_tile(name: str) -> int:
+    """Tile width of the NVFP4 GEMM `name` ("qkv", "fc1", "fc2")."""
+    return 256 if name in FP4_WIDE and FP4_BN[0] != 128 else 128
 
 
 def _count(n: int = 1) -> None:
@@ -93,7 +101,7 @@ def qkv_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], q_o
         a_scale, a_sf = a_scale
         b_scale, b_sf = b_scale
         if bn is None:
-            bn = 256 if dim % 256 == 0 and (kv_dim or dim) % 256 == 0 and FP4_BN[0] != 128 else 128
+            bn = 256 if dim % 256 == 0 and (kv_dim or dim) % 256 == 0 and fp4_tile("qkv") == 256 else 128
     if bn is None:  # widest tile that divides the q and the k / v widths (tiles never straddle)
         bn = next((t for t in (256, 128, 64) if dim % t == 0 and (kv_dim or dim) % t == 0), 128)
     sin, cos = rope if rope is not None else (None, None)

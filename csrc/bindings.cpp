@@ -32,6 +32,19 @@ static void check_rows_i32(const optional<Tensor>& t, const char* name) {
   }
 }
 
+// Wait-cycle counters of the persistent GEMM (clock64 sums over CTAs; see gemm_sm100.cu
+// GemmProf): a CUDA uint64 tensor of at least 8 entries, or None to switch them off.
+static unsigned long long* g_gemm_prof = nullptr;
+void gemm_set_profile(optional<Tensor> counters) {
+  if (!counters.has_value()) {
+    g_gemm_prof = nullptr;
+    return;
+  }
+  TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == at::kLong && counters->numel() >= 8 &&
+                  counters->is_contiguous(), "gemm profile counters: contiguous CUDA int64 [>= 8]");
+  g_gemm_prof = reinterpret_cast<unsigned long long*>(counters->data_ptr());
+}
+
 void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Tensor& err,
              optional<Tensor> out, optional<Tensor> out_rows, optional<Tensor> bias, optional<Tensor> gamma,
              optional<Tensor> resid, optional<Tensor> resid_rows, optional<Tensor> aux,
@@ -114,6 +127,7 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
   ep.sfa = sfa;
   ep.sfb = sfb;
   ep.sf_kt = K / 64;
+  ep.prof = g_gemm_prof;
   if (!rs_out.empty()) {
     TORCH_CHECK(epi == EPI_BF16 && rs_out.size() <= 8 && rs_rows_per_rank > 0 && rs_ld % 8 == 0,
                 "gemm: the reduce-scatter epilogue is EPI_BF16 with 1..8 slot buffers");
@@ -163,6 +177,7 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using namespace appcorr;
   m.doc() = "appcorr_b200 native sm_100a kernels";
+  m.def("gemm_set_profile", &gemm_set_profile, py::arg("counters") = py::none());
   m.def("gemm", &gemm_op, py::arg("A"), py::arg("B"), py::arg("epi"), py::arg("bn"), py::arg("err"),
         py::arg("out") = py::none(), py::arg("out_rows") = py::none(), py::arg("bias") = py::none(),
         py::arg("gamma") = py::none(), py::arg("resid") = py::none(), py::arg("resid_rows") = py::none(),

@@ -304,6 +304,273 @@ __device__ __forceinline__ void run_epilogue(uint32_t taddr, int m, int n0, cons
   }
 }
 
+// ------------------------------------------------------------ early-release epilogue
+// With one accumulator (NVFP4, 128 x 256 tiles: the scale slots leave no room for a second) the
+// MMA warp idles while the epilogue runs, and an NVFP4 tile's main loop (16 stages at K = 4096)
+// is only a few microseconds long. So every thread first drains its BN / 64 chunks of 32
+// columns into registers -- scaled, biased and rounded to bf16, which every bf16 epilogue does
+// first anyway -- and releases the accumulator; the stores and the fused elementwise work then
+// overlap the next tile's main loop. Each warp of a lane-quarter pair takes every other chunk
+// (SwiGLU: matching w1 / w2 chunks; QKV: matching rotate-half chunks of a head).
+__device__ __forceinline__ uint4 ldg_u4(const __nv_bfloat16* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ uint4 ld_u4(const __nv_bfloat16* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ void st_u4(__nv_bfloat16* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
+__device__ __forceinline__ void unpack8(uint4 u, float (&f)[8]) {
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ bool early_epilogue_ok(const GemmEpilogue& ep) {
+  if constexpr (EPI == EPI_F32) return false;
+  if constexpr (EPI == EPI_QKV) return ep.head_dim % 64 == 0 && ep.head_dim <= BN;
+  return true;
+}
+
+// Columns of the tile this thread drains, per epilogue (see run_epilogue_early).
+template <int BN, int EPI>
+struct EarlyCols {
+  static constexpr int NCH = BN / 64;  // 32-column chunks per thread (two warps per lane quarter)
+  int col[NCH];
+  int which = 0, half = 0, c0 = 0;
+  __device__ __forceinline__ EarlyCols(const GemmEpilogue& ep, int n0, int part) {
+    if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll
+      for (int j = 0; j < NCH / 2; ++j) {
+        col[2 * j] = (part + 2 * j) * 32;
+        col[2 * j + 1] = BN / 2 + (part + 2 * j) * 32;
+      }
+    } else if constexpr (EPI == EPI_QKV) {
+      const int kvd = ep.kv_dim > 0 ? ep.kv_dim : ep.dim;
+      which = n0 < ep.dim ? 0 : (n0 < ep.dim + kvd ? 1 : 2);
+      c0 = which == 0 ? n0 : (which == 1 ? n0 - ep.dim : n0 - ep.dim - kvd);
+      half = ep.head_dim >> 1;
+      const int per = half / 32;
+#pragma unroll
+      for (int j = 0; j < NCH / 2; ++j) {
+        if (which == 2) {
+          col[2 * j] = (part + 4 * j) * 32;
+          col[2 * j + 1] = (part + 4 * j + 2) * 32;
+        } else {
+          const int i = part + 2 * j;
+          col[2 * j] = (i / per) * ep.head_dim + (i % per) * 32;
+          col[2 * j + 1] = col[2 * j] + half;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) col[j] = (part + 2 * j) * 32;
+    }
+  }
+};
+
+// Before the accumulator is ready: the warp copies the column scales and the bias of its
+// chunks into its own shared-memory slice cs ([NCH * 32] scales, then [NCH * 32] biases), so
+// draining the accumulator waits on no global load.
+template <int BN, int EPI>
+__device__ __forceinline__ void early_stage_columns(float* cs, const EarlyCols<BN, EPI>& cc, int n0,
+                                                   const GemmShape& shp, const GemmEpilogue& ep, int lane) {
+  constexpr int NCH = EarlyCols<BN, EPI>::NCH;
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) {
+    const int n = n0 + cc.col[j] + lane;
+    const bool ok = n < shp.N;
+    cs[j * 32 + lane] = (ep.a_scale != nullptr && ok) ? __ldg(ep.b_scale + n) : 1.f;
+    cs[(NCH + j) * 32 + lane] = (ep.bias != nullptr && ok) ? __bfloat162float(ep.bias[n]) : 0.f;
+  }
+  __syncwarp();
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void run_epilogue_early(uint32_t taddr, int m, int n0, const GemmShape& shp,
+                                                   const GemmEpilogue& ep, const EarlyCols<BN, EPI>& cc,
+                                                   const float* cs, float rs, uint32_t tempty_bar,
+                                                   long long* phase1_cycles = nullptr) {
+  const long long tp_ = phase1_cycles ? clock64() : 0;
+  constexpr int NCH = EarlyCols<BN, EPI>::NCH;
+  const bool row_ok = m < shp.M;
+  const int* col = cc.col;
+  const int which = cc.which, half = cc.half, c0 = cc.c0;
+  (void)which; (void)half; (void)c0;
+  // phase 1: accumulator -> registers (bf16 pairs), then release it
+  uint32_t pk[NCH][16];
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) {
+    uint32_t r[32];
+    tmem_ld32(taddr + col[j], r);
+    tmem_wait_ld();
+    // the same arithmetic as scale_acc + add_bias: acc * (row scale * column scale) + bias
+    const float4* sc4 = reinterpret_cast<const float4*>(cs + j * 32);
+    const float4* bi4 = reinterpret_cast<const float4*>(cs + (NCH + j) * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 w = sc4[i], bb = bi4[i];
+      float v0 = __uint_as_float(r[4 * i]), v1 = __uint_as_float(r[4 * i + 1]);
+      float v2 = __uint_as_float(r[4 * i + 2]), v3 = __uint_as_float(r[4 * i + 3]);
+      if (ep.a_scale != nullptr) {
+        v0 *= rs * w.x;
+        v1 *= rs * w.y;
+        v2 *= rs * w.z;
+        v3 *= rs * w.w;
+      }
+      if (ep.bias != nullptr) {
+        v0 += bb.x;
+        v1 += bb.y;
+        v2 += bb.z;
+        v3 += bb.w;
+      }
+      pk[j][2 * i] = pack_bf16x2(v0, v1);
+      pk[j][2 * i + 1] = pack_bf16x2(v2, v3);
+    }
+  }
+  tc_fence_before();
+  mbar_arrive(tempty_bar);
+  if (phase1_cycles) *phase1_cycles += clock64() - tp_;
+  if (!row_ok) return;
+  // phase 2: fused elementwise work and stores, 8 columns (16 bytes) at a time
+  if constexpr (EPI == EPI_SWIGLU) {
+    const int orow = ep.out_rows ? ep.out_rows[m] : m;
+    if (orow < 0) return;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + n0 / 2;
+#pragma unroll
+    for (int j = 0; j < NCH / 2; ++j) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float a[8], b[8];
+        unpack8(make_uint4(pk[2 * j][4 * g], pk[2 * j][4 * g + 1], pk[2 * j][4 * g + 2], pk[2 * j][4 * g + 3]), a);
+        unpack8(make_uint4(pk[2 * j + 1][4 * g], pk[2 * j + 1][4 * g + 1], pk[2 * j + 1][4 * g + 2],
+                           pk[2 * j + 1][4 * g + 3]), b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[e] = bf16_round(silu(a[e])) * b[e];
+        st_u4(dst + col[2 * j] + 8 * g, pack8(a));
+      }
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    const int tok = ep.tok_idx ? ep.tok_idx[m] : (m % ep.seq_len);
+    const int kvrow = ep.kv_rows ? ep.kv_rows[m] : m;
+    const long ldkv = ep.ld_kv > 0 ? ep.ld_kv : ep.ld_qkv;
+    __nv_bfloat16* dst;
+    if (which == 0) dst = ep.q_out + (long)m * ep.ld_qkv;
+    else if (kvrow < 0) return;
+    else dst = (which == 1 ? ep.k_out : ep.v_out) + (long)kvrow * ldkv;
+    dst += c0;
+    const bool rope = which != 2 && ep.rope_sin != nullptr && tok >= ep.n_prefix;
+    const int rrow = tok - ep.n_prefix;
+#pragma unroll
+    for (int j = 0; j < NCH / 2; ++j) {
+      const int cl = col[2 * j];
+      const int ch = col[2 * j + 1];
+      const int cin = cl % ep.head_dim;  // offset inside the first half of the head
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 ul = make_uint4(pk[2 * j][4 * g], pk[2 * j][4 * g + 1], pk[2 * j][4 * g + 2], pk[2 * j][4 * g + 3]);
+        uint4 uh = make_uint4(pk[2 * j + 1][4 * g], pk[2 * j + 1][4 * g + 1], pk[2 * j + 1][4 * g + 2],
+                              pk[2 * j + 1][4 * g + 3]);
+        if (rope) {
+          // DINOv3 RoPE tables repeat their first half, so the pair (d, d + half) shares one angle
+          const float4* sn = reinterpret_cast<const float4*>(ep.rope_sin + (long)rrow * ep.head_dim + cin + 8 * g);
+          const float4* cs = reinterpret_cast<const float4*>(ep.rope_cos + (long)rrow * ep.head_dim + cin + 8 * g);
+          const float4 s0 = __ldg(sn), s1 = __ldg(sn + 1), k0 = __ldg(cs), k1 = __ldg(cs + 1);
+          const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          const float cv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+          float lo[8], hi[8];
+          unpack8(ul, lo);
+          unpack8(uh, hi);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float xl = lo[e], xh = hi[e];
+            lo[e] = xl * cv[e] - xh * sv[e];
+            hi[e] = xh * cv[e] + xl * sv[e];
+          }
+          ul = pack8(lo);
+          uh = pack8(hi);
+        }
+        st_u4(dst + cl + 8 * g, ul);
+        st_u4(dst + ch + 8 * g, uh);
+      }
+    }
+  } else {
+    const int orow = ep.out_rows ? ep.out_rows[m] : m;
+    if (orow < 0) return;
+    int rrow = -1, arow = -1;
+    if constexpr (EPI == EPI_RESID) {
+      rrow = ep.resid_rows ? ep.resid_rows[m] : m;
+      arow = ep.aux_rows ? ep.aux_rows[m] : orow;
+    }
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      const int n = n0 + col[j];
+      if (n >= shp.N) continue;
+      __nv_bfloat16* dst;
+      if constexpr (EPI == EPI_BF16) {
+        if (ep.rs_out[0] != nullptr) {
+          const int owner = orow / ep.rs_rows_per_rank;
+          dst = ep.rs_out[owner] + ((long)ep.rs_rank * ep.rs_slot_rows + m) * ep.ldo + n;
+        } else {
+          dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + n;
+        }
+      } else {
+        dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long)orow * ep.ldo + n;
+      }
+      uint4 gmv[4], rsv[4], axv[4];  // RESID: every load of the chunk before its stores
+      if constexpr (EPI == EPI_RESID) {
+        __nv_bfloat16* ap = ep.aux + (long)arow * ep.ldaux + n;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          gmv[g] = ldg_u4(ep.gamma + n + 8 * g);
+          rsv[g] = ld_u4(ep.resid + (long)rrow * ep.ldr + n + 8 * g);
+          if (ep.aux_mode == AUX_ADD && arow >= 0) axv[g] = ld_u4(ap + 8 * g);
+          else if (ep.aux_mode == AUX_OUT_MINUS && arow >= 0) axv[g] = ld_u4(ep.resid2 + (long)m * ep.ldr2 + n + 8 * g);
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 u = make_uint4(pk[j][4 * g], pk[j][4 * g + 1], pk[j][4 * g + 2], pk[j][4 * g + 3]);
+        if constexpr (EPI == EPI_GELU) {
+          float f[8];
+          unpack8(u, f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = gelu_erf(f[e]);
+          u = pack8(f);
+        } else if constexpr (EPI == EPI_RESID) {
+          float v[8], gm[8], rv[8], d[8];
+          unpack8(u, v);
+          unpack8(gmv[g], gm);
+          unpack8(rsv[g], rv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            d[e] = bf16_round(v[e] * gm[e]);
+            v[e] = rv[e] + d[e];
+          }
+          if (ep.aux_mode != AUX_NONE && arow >= 0) {
+            __nv_bfloat16* ap = ep.aux + (long)arow * ep.ldaux + n + 8 * g;
+            float a[8];
+            if (ep.aux_mode == AUX_SET) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) a[e] = d[e];
+            } else if (ep.aux_mode == AUX_ADD) {
+              unpack8(axv[g], a);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) a[e] += d[e];
+            } else {
+              float r2[8];
+              unpack8(axv[g], r2);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) a[e] = bf16_round(rv[e] - r2[e]) + d[e];
+            }
+            st_u4(ap, pack8(a));
+          }
+          u = pack8(v);
+        }
+        st_u4(dst + 8 * g, u);
+      }
+    }
+  }
+}
+
 // KIND 0: bf16 x bf16 (kind::f16, 64-element K blocks); KIND 1: e4m3 x e4m3 (kind::f8f6f4,
 // 128-element K blocks). Both stage 128-byte rows, so the shared-memory layout is identical.
 __device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -358,6 +625,13 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 // Eight epilogue warps (2..9): two per TMEM lane quarter, each draining half of the columns, so a
 // heavy epilogue (residual + increment, SwiGLU, RoPE) stays shorter than the next tile's main loop.
 constexpr int kEpiWarps = 8;
+constexpr uint32_t kBarRegion = 256;     // mbarriers + TMEM slot after the stage ring
+constexpr int kEarlyColFloats = 256;     // early-release epilogue: per-warp column scales + biases
+// shared memory beyond the stage ring: alignment slack, barrier region, early-epilogue slices
+template <int BN, int KIND>
+constexpr size_t gemm_smem_extra() {
+  return 1024 + kBarRegion + ((KIND == 2 && BN == 256) ? kEpiWarps * kEarlyColFloats * 4 : 0);
+}
 template <int KIND>
 constexpr int gemm_threads() { return 64 + kEpiWarps * 32 + (KIND == 2 ? 128 : 0); }
 
@@ -397,6 +671,16 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // GemmProf counters (ep.prof): clock64 spent in each wait, summed over CTAs
+  long long pw0 = 0, pw1 = 0, pw2 = 0, pw3 = 0;
+  const bool prof = ep.prof != nullptr;
+#define GEMM_TIMED(acc_, expr_)                      \
+  ([&]() {                                            \
+    const long long t0_ = prof ? clock64() : 0;       \
+    const bool r_ = (expr_);                          \
+    if (prof) acc_ += clock64() - t0_;                \
+    return r_;                                        \
+  }())
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -437,7 +721,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) goto producer_done;
+          if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer))) goto producer_done;
           const uint32_t fb = smem_addr(&full[s]);
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
           if constexpr (F4) {  // scales first, on their own barrier: the scale warps move them to
@@ -470,17 +754,18 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
       uint32_t ph = 0;
       int t_local = 0;
       bool issued = false;
+      const long long tstart = prof ? clock64() : 0;
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++t_local) {
         const int acc = NACC == 2 ? (t_local & 1) : 0;
         const uint32_t acc_ph = NACC == 2 ? ((t_local >> 1) & 1) : (t_local & 1);
-        if (!mbar_wait(smem_addr(&tempty[acc]), acc_ph ^ 1, shp.err, kErrTimeoutMma)) break;
+        if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&tempty[acc]), acc_ph ^ 1, shp.err, kErrTimeoutMma))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
+          if (!GEMM_TIMED(pw1, mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma))) { ok = false; break; }
           if constexpr (F4)
-            if (!mbar_wait(smem_addr(&sfull[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
+            if (!GEMM_TIMED(pw2, mbar_wait(smem_addr(&sfull[s]), ph, shp.err, kErrTimeoutMma))) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
@@ -505,6 +790,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
         umma_commit(smem_addr(&tfull[acc]));
       }
       (void)issued;
+      if (prof) pw3 = clock64() - tstart;
     }
   } else if (F4 && warp >= 2 + kEpiWarps) {
     // scale warps: lane a of quarter q writes, for every 64-element step k, the words of rows
@@ -521,7 +807,8 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(smem_addr(&sf_full[s]), ph, shp.err, kErrTimeoutEpilogue)) { ok = false; break; }
+          if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&sf_full[s]), ph, shp.err, kErrTimeoutEpilogue))) { ok = false; break; }
+          const long long ts_ = prof ? clock64() : 0;
           const uint8_t* sfs = smem + s * STAGE_BYTES + A_BYTES + B_BYTES;
           uint32_t r[32], r2[16];
 #pragma unroll
@@ -542,6 +829,7 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_addr(&sfull[s]));
+          if (prof) pw1 += clock64() - ts_;
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -557,13 +845,50 @@ __global__ void __launch_bounds__(gemm_threads<KIND>(), 1)
       const int acc = NACC == 2 ? (t_local & 1) : 0;
       const uint32_t acc_ph = NACC == 2 ? ((t_local >> 1) & 1) : (t_local & 1);
       // All lanes wait (tcgen05.ld below is warp-collective).
-      if (!mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue)) break;
-      tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      run_epilogue<BN, EPI>(taddr, mb * kBM + row_in_tile, nb * BN, shp, ep, (warp - 2) / 4, kEpiWarps / 4);
-      tc_fence_before();
-      mbar_arrive(smem_addr(&tempty[acc]));
+      bool early = false;
+      if constexpr (NACC == 1) {
+        static_assert(kEpiWarps == 8 && BN == 256, "early-release epilogue: two warps per lane quarter");
+        early = early_epilogue_ok<BN, EPI>(ep);
+        if (early) {
+          const int m = mb * kBM + row_in_tile;
+          const EarlyCols<BN, EPI> cc(ep, nb * BN, (warp - 2) / 4);
+          float* cs = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + kBarRegion) + (warp - 2) * kEarlyColFloats;
+          early_stage_columns<BN, EPI>(cs, cc, nb * BN, shp, ep, lane);
+          const float rs = (ep.a_scale != nullptr && m < shp.M) ? ep.a_scale[m] : 1.f;
+          if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue))) break;
+          tc_fence_after();
+          GEMM_TIMED(pw1, (run_epilogue_early<BN, EPI>(taddr, m, nb * BN, shp, ep, cc, cs, rs, smem_addr(&tempty[acc]), prof ? &pw2 : nullptr), true));
+        }
+      }
+      if (!early) {
+        if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue))) break;
+        tc_fence_after();
+        GEMM_TIMED(pw1, (run_epilogue<BN, EPI>(taddr, mb * kBM + row_in_tile, nb * BN, shp, ep, (warp - 2) / 4, kEpiWarps / 4), true));
+        tc_fence_before();
+        mbar_arrive(smem_addr(&tempty[acc]));
+      }
     }
+  }
+#undef GEMM_TIMED
+  if (prof && lane == 0) {  // 0 producer empty; 1-3 MMA tempty / full / sfull; 4 MMA loop; 5-6 epilogue tfull / body
+    if (warp == 0) atomicAdd(ep.prof + 0, (unsigned long long)pw0);
+    if (warp == 1) {
+      atomicAdd(ep.prof + 1, (unsigned long long)pw0);
+      atomicAdd(ep.prof + 2, (unsigned long long)pw1);
+      atomicAdd(ep.prof + 3, (unsigned long long)pw2);
+      atomicAdd(ep.prof + 4, (unsigned long long)pw3);
+    }
+    if (warp == 2) {
+      atomicAdd(ep.prof + 5, (unsigned long long)pw0);
+      atomicAdd(ep.prof + 6, (unsigned long long)pw1);
+    }
+    if (threadIdx.x == 0) atomicAdd(ep.prof + 7, 1ull);
+    if (F4 && warp == 2 + kEpiWarps) {  // 8-9 scale warp: bytes wait / TMEM store + wait
+      atomicAdd(ep.prof + 8, (unsigned long long)pw0);
+      atomicAdd(ep.prof + 9, (unsigned long long)pw1);
+    }
+    if (warp == 2) atomicAdd(ep.prof + 10, (unsigned long long)pw2);  // 10 epilogue phase 1
   }
   tc_fence_before();
   __syncthreads();
@@ -781,6 +1106,15 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
+  long long pw0 = 0, pw1 = 0, pw2 = 0, pw3 = 0;
+  const bool prof = ep.prof != nullptr;
+#define GEMM_TIMED(acc_, expr_)                      \
+  ([&]() {                                            \
+    const long long t0_ = prof ? clock64() : 0;       \
+    const bool r_ = (expr_);                          \
+    if (prof) acc_ += clock64() - t0_;                \
+    return r_;                                        \
+  }())
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -821,7 +1155,7 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer)) goto producer_done;
+          if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&empty[s]), ph ^ 1, shp.err, kErrTimeoutProducer))) goto producer_done;
           const uint32_t fb = mapa_shared(smem_addr(&full[s]), 0);
           if (leader) mbar_arrive_expect_tx_cluster(fb, 2 * (A_BYTES + B_BYTES));
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
@@ -849,16 +1183,17 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
       int s = 0;
       uint32_t ph = 0;
       int t_local = 0;
+      const long long tstart = prof ? clock64() : 0;
       for (int tile = cluster_id; tile < total; tile += num_clusters, ++t_local) {
         const int acc = NACC == 2 ? (t_local & 1) : 0;
         const uint32_t acc_ph = NACC == 2 ? ((t_local >> 1) & 1) : (t_local & 1);
-        if (!mbar_wait(smem_addr(&tempty[acc]), acc_ph ^ 1, shp.err, kErrTimeoutMma)) break;
+        if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&tempty[acc]), acc_ph ^ 1, shp.err, kErrTimeoutMma))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
-          if (!mbar_wait(smem_addr(&sfull[s]), ph, shp.err, kErrTimeoutMma)) { ok = false; break; }
+          if (!GEMM_TIMED(pw1, mbar_wait(smem_addr(&full[s]), ph, shp.err, kErrTimeoutMma))) { ok = false; break; }
+          if (!GEMM_TIMED(pw2, mbar_wait(smem_addr(&sfull[s]), ph, shp.err, kErrTimeoutMma))) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
@@ -873,6 +1208,7 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
         if (!ok) break;
         umma_commit_pair_mask(smem_addr(&tfull[acc]), 0x3);
       }
+      if (prof) pw3 = clock64() - tstart;
     }
   } else if (warp >= 2 + kEpiWarps) {
     // scale warps: stage s's A scales (4 groups of 4 columns) and B scales (SFB_COLS columns)
@@ -884,7 +1220,8 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
     for (int tile = cluster_id; tile < total; tile += num_clusters) {
       bool ok = true;
       for (int kb = 0; kb < KB; ++kb) {
-        if (!mbar_wait(smem_addr(&sf_full[s]), ph, shp.err, kErrTimeoutEpilogue)) { ok = false; break; }
+        if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&sf_full[s]), ph, shp.err, kErrTimeoutEpilogue))) { ok = false; break; }
+        const long long ts_ = prof ? clock64() : 0;
         const uint8_t* sfs = smem + s * STAGE_BYTES + A_BYTES + B_BYTES;
         uint32_t r[32], r2[16];
 #pragma unroll
@@ -905,6 +1242,7 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster_relaxed(sfull_leader + s * 8);
+        if (prof) pw1 += clock64() - ts_;
         if (++s == STAGES) { s = 0; ph ^= 1; }
       }
       if (!ok) break;
@@ -919,14 +1257,33 @@ __global__ void __launch_bounds__(gemm_threads<2>(), 1)
       tile_coords(tile, num_m, num_n, mb, nb);
       const int acc = NACC == 2 ? (t_local & 1) : 0;
       const uint32_t acc_ph = NACC == 2 ? ((t_local >> 1) & 1) : (t_local & 1);
-      if (!mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue)) break;
+      if (!GEMM_TIMED(pw0, mbar_wait(smem_addr(&tfull[acc]), acc_ph, shp.err, kErrTimeoutEpilogue))) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      run_epilogue<BN, EPI>(taddr, mb * 2 * kBM + rank * kBM + row_in_tile, nb * BN, shp, ep, (warp - 2) / 4,
-                            kEpiWarps / 4);
+      GEMM_TIMED(pw1, (run_epilogue<BN, EPI>(taddr, mb * 2 * kBM + rank * kBM + row_in_tile, nb * BN, shp, ep,
+                                             (warp - 2) / 4, kEpiWarps / 4), true));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster_relaxed(tempty_leader + acc * 8);
+    }
+  }
+#undef GEMM_TIMED
+  if (prof && lane == 0 && leader) {  // the leader CTA's warps, same slots as the one-CTA kernel
+    if (warp == 0) atomicAdd(ep.prof + 0, (unsigned long long)pw0);
+    if (warp == 1) {
+      atomicAdd(ep.prof + 1, (unsigned long long)pw0);
+      atomicAdd(ep.prof + 2, (unsigned long long)pw1);
+      atomicAdd(ep.prof + 3, (unsigned long long)pw2);
+      atomicAdd(ep.prof + 4, (unsigned long long)pw3);
+    }
+    if (warp == 2) {
+      atomicAdd(ep.prof + 5, (unsigned long long)pw0);
+      atomicAdd(ep.prof + 6, (unsigned long long)pw1);
+    }
+    if (warp == 0) atomicAdd(ep.prof + 7, 1ull);
+    if (warp == 2 + kEpiWarps) {
+      atomicAdd(ep.prof + 8, (unsigned long long)pw0);
+      atomicAdd(ep.prof + 9, (unsigned long long)pw1);
     }
   }
   tc_fence_before();
@@ -1003,7 +1360,8 @@ template <int BN, int STAGES, int EPI, int KIND = 0>
 void launch_gemm(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const GemmEpilogue& ep,
                  int* err, int max_ctas, cudaStream_t stream) {
   constexpr uint32_t STAGE_BYTES = (kBM + BN) * kBK * 2 + (KIND == 2 ? (kBM + BN) * 16 : 0);
-  constexpr size_t SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  constexpr size_t SMEM = STAGES * STAGE_BYTES + gemm_smem_extra<BN, KIND>();
+  static_assert(SMEM <= 232448, "shared memory per CTA");
   auto kern = gemm_bf16_tn_kernel<BN, STAGES, EPI, KIND>;
   static bool configured = false;
   if (!configured) {

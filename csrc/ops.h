@@ -54,6 +54,8 @@ struct GemmEpilogue {
   const uint8_t* sfa;
   const uint8_t* sfb;
   int sf_kt;
+  // optional wait-cycle counters (gemm_set_profile); nullptr: off
+  unsigned long long* prof;
 };
 
 struct GemmShape {

@@ -194,3 +194,86 @@ def test_engine_nvfp4_tracks_oracle():
     xc = eng.correct(sess, 0, len(m.blocks), pre, cand, {"token_keep_ratio": 1.0})
     torch.cuda.synchronize()
     assert _rel(xc.view(B, -1, m.embed_dim), xr) < 0.15
+
+
+@pytest.mark.parametrize("M", [1029, 77])
+def test_gemm_nvfp4_wide_tiles_match_narrow(M):
+    """128 x 256 tiles (one accumulator, released to the MMA warp before the epilogue's stores and
+    fused work) give the same bytes as 128 x 128 tiles (two accumulators, classic epilogue) for
+    every bf16 epilogue: plain + row map, GELU, SwiGLU, residual with each increment mode, and
+    qkv with RoPE, a k/v row scatter and dropped rows. Both accumulate each output in the same
+    K order, so the results are identical."""
+    K = _k()
+    from appcorr_b200.models.weights import pack_swiglu
+
+    torch.manual_seed(11)
+    D, N = 512, 768
+    a4, a_sf, a_s = _quant(_rand(M, D))
+    A = (a_s, a_sf)
+
+    def both(fn):
+        outs = []
+        for bn in (128, 256):
+            outs.append(fn(bn))
+        torch.cuda.synchronize()
+        for x, y in zip(*outs):
+            assert torch.equal(x, y), f"max diff {(x.float() - y.float()).abs().max().item()}"
+
+    w4, (ws, wsf) = K.quantize_weight_nvfp4(_rand(N, D, scale=D ** -0.5))
+    W = (ws, wsf)
+    bias = _rand(N, scale=0.1)
+    perm = torch.randperm(M, device=DEV).to(torch.int32)
+    perm[::7] = -1  # dropped rows
+
+    def plain(bn, epi):
+        out = torch.full((M, N), 7.0, device=DEV, dtype=torch.bfloat16)
+        K.gemm(a4, w4, out, epi=epi, bias=bias, out_rows=perm, a_scale=A, b_scale=W, bn=bn)
+        return [out]
+
+    both(lambda bn: plain(bn, K.EPI_BF16))
+    both(lambda bn: plain(bn, K.EPI_GELU))
+
+    Hd = 512
+    w1, w2 = _rand(Hd, D, scale=D ** -0.5), _rand(Hd, D, scale=D ** -0.5)
+    b1, b2 = _rand(Hd, scale=0.1), _rand(Hd, scale=0.1)
+
+    def swiglu(bn):
+        wp, bp = pack_swiglu(w1, w2, b1, b2, bn // 2)
+        wq, (s, sf) = K.quantize_weight_nvfp4(wp)
+        h = torch.empty(M, Hd, device=DEV, dtype=torch.bfloat16)
+        K.gemm(a4, wq, h, epi=K.EPI_SWIGLU, bias=bp, a_scale=A, b_scale=(s, sf), bn=bn)
+        return [h]
+
+    both(swiglu)
+
+    gamma, resid, resid2 = _rand(N, scale=0.5), _rand(M, N), _rand(M, N)
+    rows = torch.randperm(M, device=DEV).to(torch.int32)
+    aux0 = _rand(M, N)
+    for mode in (K.AUX_SET, K.AUX_ADD, K.AUX_OUT_MINUS):
+        def resid_fn(bn, mode=mode):
+            out = resid.clone()
+            aux = aux0.clone()
+            K.gemm(a4, w4, out, epi=K.EPI_RESID, bias=bias, gamma=gamma, resid=resid, out_rows=rows, aux=aux,
+                   aux_mode=mode, resid2=resid2 if mode == K.AUX_OUT_MINUS else None, a_scale=A, b_scale=W, bn=bn)
+            return [out, aux]
+
+        both(resid_fn)
+
+    Dh, H, npre = 128, 2, 5
+    wq4, (wqs, wqsf) = K.quantize_weight_nvfp4(_rand(3 * H * Dh, D, scale=D ** -0.5))
+    bq = _rand(3 * H * Dh, scale=0.1)
+    sin = torch.randn(M, Dh // 2, device=DEV).repeat(1, 2).contiguous()
+    cos = torch.randn(M, Dh // 2, device=DEV).repeat(1, 2).contiguous()
+    tok = torch.randint(0, M, (M,), device=DEV, dtype=torch.int32)
+    kvr = torch.randperm(M, device=DEV).to(torch.int32)
+    kvr[::5] = -1
+
+    def qkv(bn):
+        q = torch.zeros(M, H * Dh, device=DEV, dtype=torch.bfloat16)
+        k = torch.zeros_like(q)
+        v = torch.zeros_like(q)
+        K.qkv_gemm(a4, wq4, bq, q, k, v, head_dim=Dh, tok_idx=tok, kv_rows=kvr, rope=(sin, cos), n_prefix=npre,
+                   a_scale=A, b_scale=(wqs, wqsf), bn=bn)
+        return [q, k, v]
+
+    both(qkv)
