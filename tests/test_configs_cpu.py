@@ -76,3 +76,37 @@ def test_sweep_runs_two_points_on_cpu(tmp_path):
     assert rc == 0 and len(rows) == 2, rows
     assert {r["appcorr_kwargs.token_keep_ratio"] for r in rows} == {"0.25", "0.5"}
     assert all(float(r["latency_p50_ms"]) > 0 for r in rows)
+
+
+# The reference's own experiment corpus (offload/config/**.json of the installed reference under
+# baseline/_ref, when it is installed): every file must parse through this build's
+# ExperimentConfig unchanged and resolve to registered policies, executors and input profiles.
+REF_CONFIGS = sorted(glob.glob(os.path.join(ROOT, "baseline", "_ref", "offload", "config", "**", "*.json"),
+                            recursive=True))
+
+
+@pytest.mark.skipif(not REF_CONFIGS, reason="reference not installed (bash baseline/install_reference.sh)")
+@pytest.mark.parametrize("path", REF_CONFIGS or ["none"],
+                         ids=[os.path.relpath(p, os.path.join(ROOT, "baseline", "_ref", "offload", "config"))
+                              for p in REF_CONFIGS] or ["none"])
+def test_reference_config_loads(path):
+    import itertools
+
+    import torch
+
+    from appcorr_b200.common.protocol import ExperimentConfig, Patch, normalize_appcorr_kwargs
+    from appcorr_b200.policies import SCHEDULER_REGISTRY, TRANSMISSION_REGISTRY, get_scheduler
+    from appcorr_b200.server import model as models
+
+    cfg = ExperimentConfig(**json.load(open(path)))
+    assert cfg.scheduler_policy_name in SCHEDULER_REGISTRY
+    assert cfg.transmission_policy_name in TRANSMISSION_REGISTRY
+    cfg.get_input_profile_config()
+    normalize_appcorr_kwargs(cfg.appcorr_kwargs, cfg.transmission_kwargs)
+    assert models.get_model_executor(cfg.model_name, torch.device("cpu")) is not None
+    sched = get_scheduler(cfg.scheduler_policy_name, cfg)
+    n = cfg.batch_size
+    buf = [Patch(image_idx=i, spatial_idx=0, data=b"", res_level=1, group_id=0, batch_group_total=n,
+                 num_correction_groups=1) for i in range(n)]
+    task = sched.decide(buf, cfg, itertools.count())
+    assert task is not None and task.instructions
