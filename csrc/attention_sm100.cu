@@ -402,8 +402,11 @@ __device__ __forceinline__ void umma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a
 // scheduler to hide the ex2 / tcgen05.ld latencies. Warps whose 32 rows lie past Tq and
 // column halves that lie wholly past the last key skip their exponentials.
 constexpr int kFaSThreads = 320;
+constexpr int kFaPoly8Default = 0;
 
-template <int DH>
+// POLY8: of every 8 consecutive probabilities a thread computes, the first POLY8 use exp2_poly
+// (FMA pipe) and the rest ex2.approx (MUFU), so both pipes share the softmax's exponentials.
+template <int DH, int POLY8 = 0>
 __global__ void __launch_bounds__(kFaSThreads, 1)
     fa_fwd_split_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, FaParams p) {
@@ -662,8 +665,9 @@ __global__ void __launch_bounds__(kFaSThreads, 1)
         float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          const float e0 = ex2_approx(fmaf(sv[2 * t], sl2, -moff));
-          const float e1 = ex2_approx(fmaf(sv[2 * t + 1], sl2, -moff));
+          const float x0 = fmaf(sv[2 * t], sl2, -moff), x1 = fmaf(sv[2 * t + 1], sl2, -moff);
+          const float e0 = ((2 * t) & 7) < POLY8 ? exp2_poly(x0) : ex2_approx(x0);
+          const float e1 = ((2 * t + 1) & 7) < POLY8 ? exp2_poly(x1) : ex2_approx(x1);
           ls8[(2 * t) & 7] += e0;
           ls8[(2 * t + 1) & 7] += e1;
           pk[t] = pack_bf16x2(e0, e1);
@@ -1064,8 +1068,20 @@ void attention_sm100_op(const at::Tensor& q, const at::Tensor& k, const at::Tens
     dim3 grid((Tq + kFaBM - 1) / kFaBM, H, B);
     const int smem = static_cast<int>(Dh / 64) * 16384 * 7 + 1024 + 256;  // Q + 3 K/V stages
     if (Dh == 128) {
-      FA_CHECK_ATTR(cudaFuncSetAttribute(fa_fwd_split_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      fa_fwd_split_kernel<128><<<grid, kFaSThreads, smem, st>>>(tq, tk, tv, p);
+      // share of exponentials on the FMA pipe (APPCORR_ATTN_POLY8: 0..4 of every 8)
+      static const int poly8 = [] {
+        const char* e = std::getenv("APPCORR_ATTN_POLY8");
+        return e ? std::atoi(e) : kFaPoly8Default;
+      }();
+      auto launch = [&](auto kern) {
+        FA_CHECK_ATTR(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        kern<<<grid, kFaSThreads, smem, st>>>(tq, tk, tv, p);
+      };
+      if (poly8 == 1) launch(fa_fwd_split_kernel<128, 1>);
+      else if (poly8 == 2) launch(fa_fwd_split_kernel<128, 2>);
+      else if (poly8 == 3) launch(fa_fwd_split_kernel<128, 3>);
+      else if (poly8 == 4) launch(fa_fwd_split_kernel<128, 4>);
+      else launch(fa_fwd_split_kernel<128, 0>);
     } else {
       FA_CHECK_ATTR(cudaFuncSetAttribute(fa_fwd_split_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       fa_fwd_split_kernel<64><<<grid, kFaSThreads, smem, st>>>(tq, tk, tv, p);

@@ -1199,7 +1199,25 @@ void head_mean_op(const at::Tensor& probs, int64_t B, int64_t H, int64_t N, at::
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// The FMA-pipe exp2 of the attention softmax, exposed for its accuracy test.
+__global__ void exp2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, long n) {
+  const long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x;
+  if (i < n) y[i] = exp2_poly(x[i]);
+}
+
+void exp2_poly_op(const at::Tensor& x, at::Tensor& y) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous() && y.sizes() == x.sizes() &&
+                  y.scalar_type() == at::kFloat && y.is_contiguous(), "exp2_poly: contiguous fp32 x, y");
+  c10::cuda::CUDAGuard g(x.device());
+  const long n = x.numel();
+  if (n == 0) return;
+  exp2_poly_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      x.data_ptr<float>(), y.data_ptr<float>(), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void register_elementwise_ops(pybind11::module_& m) {
+  m.def("exp2_poly", &exp2_poly_op);
   m.def("head_mean", &head_mean_op);
   namespace py = pybind11;
   m.def("layernorm", &layernorm_op, py::arg("x"), py::arg("rows"), py::arg("w"), py::arg("b"), py::arg("eps"),

@@ -112,6 +112,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// ---------------------------------------------------------------- exp2 on the FMA pipe
+// 2^x for x <= 0 without the special-function unit, so a softmax can split its exponentials
+// between the MUFU and FMA pipes. Method: Cody-Waite style range reduction x = j + f with
+// j = rint(x) (the 1.5 * 2^23 shifter puts j in the low mantissa bits), f in [-0.5, 0.5];
+// 2^f by a degree-3 polynomial in Horner form whose coefficients are a relative-error minimax
+// fit computed for this file (iteratively reweighted least squares on 4000 Chebyshev nodes,
+// max relative error 7.5e-5 in fp32); 2^j is added to the exponent field. x is clamped to
+// -125 so that the exponent field stays normal; the result there (about 2e-38) is below every
+// bf16 probability that matters.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;  // 1.5 * 2^23: rint(x) in the low bits
+  const float j = t - 12582912.f;
+  const float f = x - j;
+  float p = fmaf(0.0551716648f, f, 0.2426111251f);
+  p = fmaf(p, f, 0.6932609677f);
+  p = fmaf(p, f, 0.9999280572f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -345,3 +345,22 @@ def test_attention_fused_cls_score(impl):
     ref = torch.empty(B, N, device=DEV)
     K_.cls_attn_pscore(q, k, B=B, N=N, H=H, Dh=Dh, scratch=torch.empty(B, H, N, device=DEV), out=ref)
     _close(fused, ref, rtol=1e-3, atol=1e-5)
+
+
+def test_exp2_poly_error_bound():
+    """The FMA-pipe exp2 that the attention softmax uses for part of its probabilities stays within
+    its fitted relative-error bound (7.5e-5, plus fp32 rounding) of exp2 on the softmax's input
+    range x <= 0, and gives tiny non-negative values (no sign or exponent wrap) far below it."""
+    from appcorr_b200.ops.native import lib
+
+    x = torch.cat([torch.linspace(-124.0, 0.0, 1 << 20, device=DEV),
+                   -torch.rand(1 << 16, device=DEV) * 8, torch.tensor([0.0, -0.5, -1e-7], device=DEV)])
+    y = torch.empty_like(x)
+    lib().exp2_poly(x, y)
+    ref = torch.exp2(x.double())
+    rel = ((y.double() - ref).abs() / ref).max().item()
+    assert rel < 8e-5, rel
+    far = torch.tensor([-125.0, -200.0, -1e30, -3.0e38], device=DEV)
+    yf = torch.empty_like(far)
+    lib().exp2_poly(far, yf)
+    assert bool((yf >= 0).all()) and bool((yf < 1e-37).all()), yf.tolist()
