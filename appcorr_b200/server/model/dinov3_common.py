@@ -190,7 +190,8 @@ class DINOv3BackboneMixin:
         start, end = params.get("layers", (0, self.cfg.depth))
         opts = normalize_appcorr_kwargs(config.appcorr_kwargs, config.transmission_kwargs)
         if self.engine is not None:
-            self.engine.approx(context["session"], start, end, opts["server_pscore"])
+            sess, kind = context["session"], opts["server_pscore"]
+            self.engine.run_graphed(sess, ("approx", start, end, kind), lambda: self.engine.approx(sess, start, end, kind))
         else:
             x = context["x_in"].clone() if start == 0 or "x" not in context else context["x"]
             with torch.no_grad():
@@ -239,7 +240,16 @@ class DINOv3BackboneMixin:
             mobile = None
             if hint is not None and opts["mobile_pscore_weight"] != 0.0:
                 mobile = hint.to(self.device, torch.float32).gather(1, (cand - self.cfg.n_prefix).long()).contiguous()
-            self.engine.correct(sess, start, end, pre, cand, opts, mobile=mobile)
+            # replayed as one CUDA graph when every input is static: no per-request mobile score,
+            # no random score, no threshold without a cap (that plan needs a host read)
+            static = (mobile is None and opts.get("server_pscore") != "random" and
+                      not (opts.get("token_keep_thres") is not None and not opts.get("token_keep_cap")))
+            if static:
+                key = ("correct", start, end, pre.data_ptr(), cand.data_ptr(), tuple(pre.shape), tuple(cand.shape),
+                       repr(sorted(opts.items())))
+                self.engine.run_graphed(sess, key, lambda: self.engine.correct(sess, start, end, pre, cand, opts))
+            else:
+                self.engine.correct(sess, start, end, pre, cand, opts, mobile=mobile)
         else:
             x = context["x_in"].clone() if start == 0 or "x" not in context else context["x"]
             B = x.shape[0]

@@ -177,3 +177,43 @@ def test_engine_fp8_tracks_oracle(name, over):
     xc = eng.correct(sess, 0, len(m.blocks), pre, cand, {"token_keep_ratio": 1.0})
     torch.cuda.synchronize()
     assert _rel(xc.view(B, -1, m.embed_dim), xr) < 6e-2
+
+
+@pytest.mark.parametrize("precision,kind", [("bf16", "cls_attn_prob_layermean"), ("nvfp4", "patch_attn_prob")])
+def test_engine_graph_replay_matches_eager(precision, kind):
+    """Passes run through ViTEngine.run_graphed (eager, then captured, then replayed) give the same
+    bytes as eager passes over a sequence of requests with new images each time, including the
+    Python-side state the replay re-applies (the layer-mean score entry that the approximate pass
+    drops and the correction pass rebuilds)."""
+    from appcorr_b200.models.engine import ViTEngine
+
+    m = _model("vit7b16", depth=3, embed_dim=512, num_heads=4)
+    B, H, W = 2, 64, 64
+    npre = m.cfg.n_prefix
+    opts = {"token_keep_ratio": 0.4, "server_pscore": kind}
+    outs = {}
+    for graphs in (True, False):
+        eng = ViTEngine.from_module(m, DEV, precision=precision)
+        eng.graphs_enabled = graphs
+        sess = eng.new_session(B, H, W)
+        pre = torch.arange(npre, dtype=torch.int32, device=DEV).repeat(B, 1).contiguous()
+        cand = torch.arange(npre, sess.N, dtype=torch.int32, device=DEV).repeat(B, 1).contiguous()
+        g = torch.Generator(device=DEV).manual_seed(0)
+        res = []
+        for _ in range(4):
+            img0 = torch.randint(0, 256, (B, H, W, 3), dtype=torch.uint8, device=DEV, generator=g)
+            img1 = torch.randint(0, 256, (B, H, W, 3), dtype=torch.uint8, device=DEV, generator=g)
+            eng.prepare_tokens(sess, img0)
+            x = eng.run_graphed(sess, ("approx", 0, 3, kind), lambda: eng.approx(sess, 0, 3, kind))
+            res.append(x.clone())
+            eng.prepare_tokens(sess, img1)
+            xc = eng.run_graphed(sess, ("correct", 0, 3), lambda: eng.correct(sess, 0, 3, pre, cand, opts))
+            res.append(xc.clone())
+            res.append(eng.patch_features(sess).clone())
+            res.append(sess.upd.clone())
+        torch.cuda.synchronize()
+        outs[graphs] = res
+        if graphs:
+            assert len(sess._graphs) == 2 and all(isinstance(v, tuple) for v in sess._graphs.values())
+    for a, b in zip(outs[True], outs[False]):
+        assert torch.equal(a, b)
