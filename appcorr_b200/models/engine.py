@@ -458,15 +458,23 @@ class ViTEngine:
             return fn()
         cache = sess.__dict__.setdefault("_graphs", {})
         ent = cache.get(key)
-        if ent is None:
-            cache[key] = "warm"
+        if ent is None or ent == "eager":
+            if ent is None:
+                cache[key] = "warm"
             return fn()
         if ent == "warm":
             snap = self._py_state(sess)
             n0 = K.LAUNCHES[0]
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                out = fn()
+            try:
+                with torch.cuda.graph(g):
+                    out = fn()
+            except RuntimeError:  # something in fn cannot be captured: this key stays eager
+                cache[key] = "eager"
+                K.LAUNCHES[0] = n0
+                self._py_apply(([(o, a, e, [k for k in o.extra if k not in e]) for o, a, e in snap[0]], snap[1]))
+                torch.cuda.synchronize()
+                return fn()
             delta = self._py_delta(snap), K.LAUNCHES[0] - n0
             cache[key] = (g, out, delta)
             g.replay()
