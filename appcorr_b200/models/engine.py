@@ -467,7 +467,9 @@ class ViTEngine:
             n0 = K.LAUNCHES[0]
             g = torch.cuda.CUDAGraph()
             try:
-                with torch.cuda.graph(g):
+                # thread-local: the server's decoder and reaper threads keep using the GPU
+                # (their own streams, host reads) while the launcher thread captures
+                with torch.cuda.graph(g, capture_error_mode="thread_local"):
                     out = fn()
             except RuntimeError:  # something in fn cannot be captured: this key stays eager
                 cache[key] = "eager"
