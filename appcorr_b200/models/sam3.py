@@ -129,3 +129,75 @@ def sam3_engine_weights(model: SAM3Tower, device):
                          periods=model.rope.periods.detach().to(device=device, dtype=torch.float32),
                          layers=layers, norm_w=bf(model.norm.weight), norm_b=bf(model.norm.bias),
                          pos_embed=bf(model.pos_embed))
+
+
+# ----------------------------------------------------------------------------- stock SAM 3 head
+# Downstream of the tower the reference runs the stock `transformers` Sam3Model untouched, fed
+# with the tower's features through `vision_embeds` (offload/server/model/sam3_executor.py:140-160):
+# FPN neck, CLIP text encoder, geometry (box prompt) encoder, DETR encoder / decoder, mask decoder
+# and scoring. The same is done here; only the stock model's own ViT backbone is dropped, since the
+# features come from this build's tower. Random init (no checkpoints offline).
+CLIP_BOS, CLIP_EOS = 49406, 49407
+
+
+def stock_head_config(c: ViTConfig):
+    """Sam3Config whose vision backbone geometry matches tower config `c`. Towers of the
+    facebook/sam3 width (1024) take the stock defaults of every downstream part; narrower test
+    towers get a proportionally small detector."""
+    from transformers.models.sam3 import configuration_sam3 as hf
+
+    g = c.img_size // c.patch_size
+    back = dict(hidden_size=c.embed_dim, num_attention_heads=c.num_heads, image_size=c.img_size,
+                patch_size=c.patch_size, window_size=c.window_size, global_attn_indexes=list(c.global_layers),
+                num_hidden_layers=c.depth)
+    if c.embed_dim >= 1024:
+        return hf.Sam3Config(vision_config=dict(backbone_config=back))
+    small = dict(hidden_size=64, num_attention_heads=2, intermediate_size=128)
+    return hf.Sam3Config(
+        vision_config=dict(backbone_config=back, fpn_hidden_size=64, backbone_feature_sizes=[[4 * g, 4 * g],
+                                                                                            [2 * g, 2 * g], [g, g]]),
+        text_config=dict(hidden_size=64, intermediate_size=128, num_hidden_layers=1, num_attention_heads=2,
+                         projection_dim=64),
+        geometry_encoder_config=dict(num_layers=1, **small),
+        detr_encoder_config=dict(num_layers=1, **small),
+        detr_decoder_config=dict(num_layers=1, num_queries=20, **small),
+        mask_decoder_config=dict(hidden_size=64, num_attention_heads=2))
+
+
+def build_stock_head(c: ViTConfig, seed: int = 0, device=None, dtype=torch.float32):
+    """The stock Sam3Model for tower config `c`, without its own vision backbone (nn.Identity)."""
+    from transformers.models.sam3.modeling_sam3 import Sam3Model
+
+    torch.manual_seed(seed)
+    m = Sam3Model(stock_head_config(c)).eval()
+    m.vision_encoder.backbone = nn.Identity()
+    return m.to(device=device, dtype=dtype)
+
+
+def stock_head_forward(model, feat: torch.Tensor, boxes: Optional[torch.Tensor] = None,
+                       input_ids: Optional[torch.Tensor] = None):
+    """Tower features in raster order [B, gh, gw, D] -> the stock detector's outputs
+    (pred_masks, pred_boxes, pred_logits, ...). boxes: [B, n, 4] normalised (cx, cy, w, h) box
+    prompts (default: one whole-image box per image); input_ids: the text prompt (default: the
+    empty CLIP prompt, BOS + EOS)."""
+    from transformers.models.sam3.modeling_sam3 import Sam3VisionEncoderOutput
+
+    B = feat.shape[0]
+    dtype = next(model.parameters()).dtype
+    x = feat.to(dtype).permute(0, 3, 1, 2).contiguous()
+    fpn, pos = model.vision_encoder.neck(x)
+    if boxes is None:
+        boxes = torch.tensor([0.5, 0.5, 1.0, 1.0], device=feat.device).repeat(B, 1, 1)
+    if input_ids is None:
+        input_ids = torch.tensor([[CLIP_BOS, CLIP_EOS]], device=feat.device).repeat(B, 1)
+    with torch.no_grad():
+        return model(vision_embeds=Sam3VisionEncoderOutput(fpn_hidden_states=fpn, fpn_position_encoding=pos),
+                     input_ids=input_ids, input_boxes=boxes.to(dtype))
+
+
+def raster_features(tokens: torch.Tensor, c: ViTConfig, gh: int, gw: int) -> torch.Tensor:
+    """Window-major tower tokens [B, N, D] -> raster feature map [B, gh, gw, D]."""
+    order = window_order(gh, gw, c.window_size, 1).to(tokens.device)
+    out = torch.empty_like(tokens)
+    out[:, order] = tokens
+    return out.view(tokens.shape[0], gh, gw, -1)

@@ -4,9 +4,12 @@ Reference: offload/server/model/sam3_executor.py:41-190 (approx / correct on the
 stock model downstream). The tower is models/sam3.py (random init of the facebook/sam3 vision
 geometry; no checkpoints offline). Token selection for the correction pass ranks tokens by how far
 their input embedding moved between the approximate and the current canvas (the tower has no class
-token for an attention score). Downstream of the tower this executor returns the tower features
-(window order restored to raster) and a linear per-patch segmentation (BatchNorm-folded 1x1 head
-with fused upsample + argmax); the reference's stock SAM 3 detector is not part of this build.
+token for an attention score). Downstream of the tower, input profile key `sam3_head` selects:
+"stock" -- as in the reference, the stock `transformers` Sam3Model (FPN neck, text and box-prompt
+encoders, DETR encoder / decoder, mask decoder) fed with the tower features through
+`vision_embeds`, prompted by the request's `input_boxes` (default one whole-image box) and text ids
+(default the empty prompt); or "linear" (default) -- a linear per-patch segmentation
+(BatchNorm-folded 1x1 head with fused upsample + argmax) on the raster-ordered tower features.
 """
 from __future__ import annotations
 
@@ -18,7 +21,7 @@ import torch
 from ...common.protocol import normalize_appcorr_kwargs
 from ...models.engine import ViTEngine
 from ...models.heads import LinearSegHead, SegHeadGPU
-from ...models.sam3 import SAM3_PRESETS, SAM3Tower, sam3_engine_weights
+from ...models.sam3 import SAM3_PRESETS, SAM3Tower, build_stock_head, sam3_engine_weights, stock_head_forward
 from ...ops import kernels as K
 from .base import ModelExecutor
 from .dinov3_common import DINOv3BackboneMixin
@@ -28,6 +31,7 @@ class Sam3Executor(ModelExecutor):
     def __init__(self, device):
         super().__init__(device)
         self.engine = None
+        self.stock = None
         self._sessions: Dict = {}
 
     def load_model(self, model_name: str, config: Any):
@@ -40,10 +44,14 @@ class Sam3Executor(ModelExecutor):
         self.engine = ViTEngine(sam3_engine_weights(tower, self.device), self.device,
                                 DINOv3BackboneMixin.engine_precision(config))
         del tower
+        self.head_kind = str(profile.get("sam3_head", "linear"))
+        if self.head_kind not in ("linear", "stock"):
+            raise ValueError(f"sam3_head must be 'linear' or 'stock', got {self.head_kind!r}")
         head = LinearSegHead(self.cfg.embed_dim, int(profile.get("num_classes", 150)))
         head.random_init(seed)
         self.head_gpu = SegHeadGPU(head, self.device)
         self.num_classes = head.num_classes
+        self.stock = build_stock_head(self.cfg, seed, self.device, torch.bfloat16) if self.head_kind == "stock" else None
         self.model = self.engine
 
     def preprocess(self, batch_data, task, context, config):
@@ -108,6 +116,11 @@ class Sam3Executor(ModelExecutor):
         B, H, W, _ = canvas.shape
         feat = self.features(context)
         context["vision_embeds"] = feat.view(B, sess.grid_hw[0], sess.grid_hw[1], -1)
+        if self.stock is not None:
+            out = stock_head_forward(self.stock, context["vision_embeds"], context.get("input_boxes"),
+                                     context.get("input_ids"))
+            context["output"] = out
+            return {"num_masks": int(out.pred_masks.shape[1])}
         context["labels"] = self.head_gpu.labels(feat, B, sess.grid_hw[0], sess.grid_hw[1], H, W)
         return {}
 
@@ -116,6 +129,9 @@ class Sam3Executor(ModelExecutor):
         self.head_inference(task, context, config)
 
     def get_final_results(self, task, context, config) -> Dict[int, Any]:
+        out = context.get("output") if self.stock is not None else None
+        if out is not None:  # per image: the best-scoring query's mask, box and score
+            return stock_results(out)
         labels = context.get("labels")
         if labels is None:
             return {}
@@ -129,3 +145,16 @@ class Sam3Executor(ModelExecutor):
         kv = (sess.kc.numel() + sess.vc.numel()) * 2
         inc = sess.bos.numel() * 2
         return {"total": kv + inc, "breakdown": {"kv": kv, "blocks_out_sum": inc}}
+
+
+def stock_results(out) -> Dict[int, Any]:
+    """Per image of a stock Sam3Model output: the highest-scoring query's binary mask (logit > 0,
+    at the mask decoder's resolution), its normalised (cx, cy, w, h) box and its sigmoid score."""
+    best = out.pred_logits.float().argmax(1)
+    res = {}
+    for i in range(best.shape[0]):
+        q = int(best[i])
+        res[i] = {"mask": np.ascontiguousarray((out.pred_masks[i, q] > 0).cpu().numpy().astype(np.uint8)),
+                  "box": out.pred_boxes[i, q].float().cpu().tolist(),
+                  "score": float(out.pred_logits[i, q].float().sigmoid())}
+    return res
