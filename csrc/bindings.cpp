@@ -32,17 +32,23 @@ static void check_rows_i32(const optional<Tensor>& t, const char* name) {
   }
 }
 
-// Wait-cycle counters of the persistent GEMM (clock64 sums over CTAs; see gemm_sm100.cu
-// GemmProf): a CUDA uint64 tensor of at least 8 entries, or None to switch them off.
+// Wait-cycle counters of the persistent GEMM (clock64 sums over CTAs: 0 producer waits for free
+// stages; 1-3 MMA waits for a free accumulator / a landed stage / the scales; 4 MMA loop; 5-6
+// epilogue waits / body; 7 CTAs; 8-9 scale warps waiting for bytes / storing; 10 epilogue release):
+// a CUDA int64 tensor of at least 16 entries, or None to switch them off.
+// The counters live on one device; GEMMs launched on any other device run without them.
 static unsigned long long* g_gemm_prof = nullptr;
+static int g_gemm_prof_device = -1;
 void gemm_set_profile(optional<Tensor> counters) {
   if (!counters.has_value()) {
     g_gemm_prof = nullptr;
+    g_gemm_prof_device = -1;
     return;
   }
-  TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == at::kLong && counters->numel() >= 8 &&
-                  counters->is_contiguous(), "gemm profile counters: contiguous CUDA int64 [>= 8]");
+  TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == at::kLong && counters->numel() >= 16 &&
+                  counters->is_contiguous(), "gemm profile counters: contiguous CUDA int64 [>= 16]");
   g_gemm_prof = reinterpret_cast<unsigned long long*>(counters->data_ptr());
+  g_gemm_prof_device = counters->device().index();
 }
 
 void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Tensor& err,
@@ -127,7 +133,7 @@ void gemm_op(const Tensor& A, const Tensor& B, int64_t epi, int64_t bn, const Te
   ep.sfa = sfa;
   ep.sfb = sfb;
   ep.sf_kt = K / 64;
-  ep.prof = g_gemm_prof;
+  ep.prof = A.device().index() == g_gemm_prof_device ? g_gemm_prof : nullptr;
   if (!rs_out.empty()) {
     TORCH_CHECK(epi == EPI_BF16 && rs_out.size() <= 8 && rs_rows_per_rank > 0 && rs_ld % 8 == 0,
                 "gemm: the reduce-scatter epilogue is EPI_BF16 with 1..8 slot buffers");
