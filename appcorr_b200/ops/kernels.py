@@ -324,7 +324,28 @@ def gather_rows(src: torch.Tensor, rows: torch.Tensor, out: torch.Tensor) -> tor
     return out
 
 
+# APPCORR_DEBUG_CHECKS=1: host-side index checks after the kernels that assume them (each one
+# synchronises with the device; skipped while a CUDA graph is being captured)
+DEBUG_CHECKS = os.environ.get("APPCORR_DEBUG_CHECKS", "0") == "1"
+
+
+def check_unique_rows(rows: torch.Tensor, what: str) -> None:
+    """Raise if the non-negative entries of `rows` repeat: a scatter to repeated destination rows
+    races (which writer wins is undefined)."""
+    r = rows.reshape(-1)
+    r = r[r >= 0]
+    n_unique = torch.unique(r).numel()
+    if n_unique != r.numel():
+        raise RuntimeError(f"{what}: {r.numel() - n_unique} repeated destination rows")
+
+
+def _debug_checks_on() -> bool:
+    return DEBUG_CHECKS and not torch.cuda.is_current_stream_capturing()
+
+
 def scatter_rows(src: torch.Tensor, rows: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
+    if _debug_checks_on():
+        check_unique_rows(rows, "scatter_rows")
     _count()
     lib().scatter_rows(src, rows, dst)
     return dst
@@ -394,6 +415,8 @@ def correction_plan(server: torch.Tensor, pre: torch.Tensor, cand: torch.Tensor,
     _count()
     lib().correction_plan(server, pre, cand, mobile, float(ws), float(wm), FUSION.get(fusion, 0), valid, int(k),
                           upd, rows, stats, None if thres is None else float(thres), counts)
+    if thres is None and valid is None and _debug_checks_on():  # top-k rows feed row scatters
+        check_unique_rows(rows, "correction_plan")
 
 
 def token_prune(x: torch.Tensor, x_ref: torch.Tensor, N: int, dindice: torch.Tensor, npre: int, threshold: float,

@@ -85,6 +85,11 @@ class WorkerModule(multiprocessing.Process):
         finally:
             if self.device.type == "cuda":
                 torch.cuda.synchronize(self.device)
+                # ends a `nsys profile --capture-range=cudaProfilerApi` capture at worker exit
+                try:
+                    torch.cuda.profiler.stop()
+                except RuntimeError:
+                    pass
             for t in threads:
                 t.join(timeout=5)
 

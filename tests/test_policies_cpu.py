@@ -328,3 +328,16 @@ def test_nyu_policies_decode_on_fixed_model_grid():
     assert len(group) == 2 and group[0].target_shape == (128, 192)
     out = pol.decode(group, cfg)
     assert out.shape == (2, 64, 96, 3)
+
+
+def test_check_unique_rows():
+    """The debug index check (APPCORR_DEBUG_CHECKS=1) accepts distinct rows, ignores dropped (-1)
+    rows and names the op when destination rows repeat."""
+    import pytest
+    import torch
+
+    from appcorr_b200.ops.kernels import check_unique_rows
+
+    check_unique_rows(torch.tensor([3, 1, -1, -1, 7], dtype=torch.int32), "x")
+    with pytest.raises(RuntimeError, match="scatter_rows: 1 repeated"):
+        check_unique_rows(torch.tensor([[3, 1], [3, 8]], dtype=torch.int32), "scatter_rows")
