@@ -180,3 +180,40 @@ def test_realesrgan_key_conversion_loads_strictly():
             k = f"body.{parts[1]}.rdb{int(parts[3]) + 1}.conv{int(parts[5]) + 1}.{parts[6]}"
         ref[k] = v
     net.load_state_dict(convert_realesrgan_state({"params_ema": ref}), strict=True)
+
+
+def test_graph_replay_state_delta():
+    """The Python-side effects that ViTEngine.run_graphed records around a captured pass (session
+    attributes, `extra` entries set, replaced or removed, also on micro-batch sub-sessions, and the
+    engine's precision flags) are re-applied exactly on replay."""
+    import types
+
+    import torch
+
+    from appcorr_b200.models.engine import ViTEngine
+
+    eng = types.SimpleNamespace(_GRAPH_ENGINE_ATTRS=ViTEngine._GRAPH_ENGINE_ATTRS, _fp4=False, _fp8=False)
+    sub = types.SimpleNamespace(approx_done=0, extra={"k": 1})
+    sess = types.SimpleNamespace(approx_done=0, extra={"layermean": torch.zeros(1), "plan_id": 3, "subs": [sub]})
+    snap = ViTEngine._py_state(eng, sess)
+    # the "captured" call
+    new_t = torch.ones(2)
+    sess.approx_done = 40
+    sess.extra.pop("layermean")
+    sess.extra["plan_id"] = 4
+    sess.extra["tap3"] = new_t
+    sub.approx_done = 40
+    sub.extra["k"] = 2
+    eng._fp4, eng._fp8 = True, True
+    delta = ViTEngine._py_delta(eng, snap)
+    # a later request: state as before the call, then the replay re-applies the recorded effects
+    sess.approx_done = 0
+    sess.extra["layermean"] = torch.zeros(1)
+    sess.extra["plan_id"] = 9
+    del sess.extra["tap3"]
+    sub.approx_done, sub.extra["k"] = 0, 1
+    eng._fp4 = eng._fp8 = False
+    ViTEngine._py_apply(eng, delta)
+    assert sess.approx_done == 40 and sub.approx_done == 40 and sub.extra["k"] == 2
+    assert "layermean" not in sess.extra and sess.extra["plan_id"] == 4 and sess.extra["tap3"] is new_t
+    assert eng._fp4 and eng._fp8
